@@ -1,0 +1,151 @@
+/*
+ * dory_decode.h — C ABI of the B200 (sm_100a) gated decode-attention + KV-append path.
+ *
+ * One entry point replaces the three Triton launches of the reference's
+ * DecodeAttention (kernels/dory_decode_attention.py):
+ *
+ *   _decode_attention_kernel  (dory_decode_attention.py:47-161)   split-KV flash decoding,
+ *                                                                  q/k normalisation, K/V append
+ *   _write_new_kv_kernel      (dory_decode_attention.py:164-186)  shared-cache pre-write
+ *   _combine_gate_kernel      (dory_decode_attention.py:189-222)  LSE merge, gate, nibble-major store
+ *
+ * as launched by DecodeAttention._launch (dory_decode_attention.py:307-331) for __call__
+ * (:248-256), from_raw (:258-268) and multi_from_raw (:270-305).  Everything is enqueued
+ * on the caller's stream with no host synchronisation, no allocation and no host read of
+ * device data, so a call can be captured in a CUDA graph.
+ *
+ * All pointers are device pointers.  Strides and offsets are in ELEMENTS of the pointed-to
+ * type, as in the reference (torch strides, int64 cache/table offsets).  No function
+ * throws; every function returns a DoryStatus, and dory_decode_last_error() gives a
+ * human-readable reason for the last non-OK status on the calling thread.
+ */
+#ifndef DORY_DECODE_H_
+#define DORY_DECODE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DORY_DECODE_ABI_VERSION 1
+
+/* Status codes returned by every entry point. */
+typedef enum DoryStatus {
+  DORY_OK = 0,
+  DORY_ERR_INVALID_ARGUMENT = 1, /* shapes / counts the reference rejects with ValueError */
+  DORY_ERR_UNSUPPORTED = 2,      /* a valid configuration this build has no kernel for  */
+  DORY_ERR_ALIGNMENT = 3,        /* pointers / strides not 16-byte aligned               */
+  DORY_ERR_CUDA = 4              /* a CUDA runtime call failed                           */
+} DoryStatus;
+
+/* Element type of the per-dimension query scale `sqk` (the checkpoint's dtype). */
+typedef enum DoryDType { DORY_DTYPE_F32 = 0, DORY_DTYPE_BF16 = 1, DORY_DTYPE_F16 = 2 } DoryDType;
+
+/* Call kinds (bit flags of DoryDecodeParams.flags). */
+enum {
+  /* q holds FP32 rotated, unnormalised q heads then k heads, v holds FP32 v, and the
+   * kernel normalises q and k and appends k/v (reference RAW_QKV, from_raw). */
+  DORY_FLAG_RAW_QKV = 1u,
+  /* num_tokens query tokens, each with its own seq_len, cache_offsets[t] and
+   * block_table_offsets[t]; the slot comes from the token's block table at
+   * seq_len - 1 (reference MULTI_TOKEN, multi_from_raw). */
+  DORY_FLAG_MULTI_TOKEN = 2u,
+  /* Tokens of one call share one cache and read each other's new entries
+   * (reference shared_cache=True: write-all-first semantics). */
+  DORY_FLAG_SHARED_CACHE = 4u
+};
+
+/* Device error bits, accumulated in the scratch header and read back with
+ * dory_decode_fetch_errors(). The kernel skips the offending access instead of faulting. */
+enum {
+  DORY_DEVERR_BLOCK_OOB = 1u,     /* a block-table entry outside [0, num_cache_blocks)   */
+  DORY_DEVERR_SLOT_OOB = 2u,      /* an append slot outside the cache                     */
+  DORY_DEVERR_OFFSET_ALIGN = 4u,  /* a cache offset not a multiple of 8 elements          */
+  DORY_DEVERR_WAIT_TIMEOUT = 8u   /* a pipeline wait gave up after its iteration limit    */
+};
+
+/*
+ * Parameters of one decode-attention call.  Shapes use NH = num_heads, NKV = num_kv_heads,
+ * HD = head_dim, Q = NH * HD, T = num_tokens.
+ */
+typedef struct DoryDecodeParams {
+  /* RAW_QKV: FP32 [T, (NH + NKV) * HD] (q heads, then k heads, RoPE applied).
+   * otherwise: BF16 [T, NH * HD], already normalised and scaled by (sqk * sqk_factor)^2. */
+  const void* q;
+  const float* v;                 /* RAW_QKV: FP32 [T, NKV * HD]                          */
+  const void* sqk;                /* RAW_QKV: [NH * HD] of sqk_dtype                        */
+  const int64_t* slot_mapping;    /* RAW_QKV single-token: int64 [1]; < 0 = padding, no write */
+  void* key_cache;                /* BF16 view [num_cache_blocks, block_size, NKV, HD]      */
+  void* value_cache;              /* same strides as key_cache, unit last stride            */
+  const int32_t* block_table;     /* int32; the sequence's row (single) or the table base   */
+  const int64_t* block_table_offsets; /* MULTI_TOKEN: int64 [T] element offsets, else NULL */
+  const int64_t* cache_offsets;   /* MULTI_TOKEN: int64 [T] element offsets, else NULL      */
+  const int32_t* seq_lens;        /* int32 [T]: tokens including this one (0 = padding)     */
+  const float* gate;              /* FP32 [T, Q], post-sigmoid output gate                  */
+  float* out_nibble_major;        /* FP32 [T, 8, Q / 8]: out[t][e % 8][e / 8] = gated attn[e] */
+  void* scratch;                  /* dory_decode_scratch_bytes() bytes, zeroed once by
+                                   * dory_decode_scratch_init(); partials, merge counters and
+                                   * the device error word live here                         */
+  int64_t scratch_bytes;
+  int64_t stride_block;           /* key_cache.stride(0) */
+  int64_t stride_offset;          /* key_cache.stride(1) */
+  int64_t stride_head;            /* key_cache.stride(2) */
+  int64_t num_cache_blocks;       /* key_cache.shape[0]; > 0 enables block / slot bounds checks */
+  float softmax_scale;
+  float sqk_factor;
+  float eps;
+  int32_t num_tokens;             /* T (1 for the single-token calls)                        */
+  int32_t num_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;               /* 64, 128 or 256                                         */
+  int32_t block_size;             /* key_cache.shape[1]; a multiple of 16                   */
+  int32_t window;                 /* 0: full attention; > 0: keys [seq_len - window, seq_len) */
+  int32_t splits;                 /* split-KV partitions per (token, KV head)               */
+  int32_t blocks_per_tile;        /* split granularity in cache blocks (reference knob)      */
+  int32_t min_blocks_per_split;   /* lower bound on cache blocks per active split (>= 1)     */
+  int32_t max_tokens;             /* scratch capacity in tokens                             */
+  int32_t sqk_dtype;              /* DoryDType                                               */
+  uint32_t flags;                 /* DORY_FLAG_*                                             */
+} DoryDecodeParams;
+
+/* ABI version of the loaded library (DORY_DECODE_ABI_VERSION). */
+int32_t dory_decode_abi_version(void);
+
+/* sizeof(DoryDecodeParams) as compiled into the library, so a foreign-function binding
+ * (ctypes, cgo, JNI) can check its own struct layout before the first call. */
+int64_t dory_decode_params_bytes(void);
+
+/* Bytes of scratch one DecodeAttention instance needs (partials, counters, error word).
+ * Mirrors the buffers DecodeAttention.__init__ allocates (dory_decode_attention.py:242-246). */
+int64_t dory_decode_scratch_bytes(int32_t max_tokens, int32_t splits, int32_t num_heads,
+                                  int32_t num_kv_heads, int32_t head_dim);
+
+/* Zeroes the scratch (merge counters and error word) on `stream` (a cudaStream_t). */
+int32_t dory_decode_scratch_init(void* scratch, int64_t scratch_bytes, void* stream);
+
+/*
+ * Gated decode attention with optional q/k normalisation and K/V append, on `stream`.
+ * Single token (flags without MULTI_TOKEN): DecodeAttention.__call__ / from_raw
+ *   (dory_decode_attention.py:248-268).
+ * MULTI_TOKEN (| SHARED_CACHE): DecodeAttention.multi_from_raw
+ *   (dory_decode_attention.py:270-305), including the shared-cache write-all-first order
+ *   of _write_new_kv_kernel (:164-186), done inside the same kernel.
+ * Host-side argument errors return DORY_ERR_INVALID_ARGUMENT with the reference's
+ * ValueError conditions (:235-236, :291-293, :310-311).
+ */
+int32_t dory_decode_attention(const DoryDecodeParams* params, void* stream);
+
+/* Copies the device error word (DORY_DEVERR_* bits) to *flags_out, synchronising `stream`;
+ * clears it when `clear` is non-zero.  The only entry point that waits on the device. */
+int32_t dory_decode_fetch_errors(void* scratch, uint32_t* flags_out, int32_t clear, void* stream);
+
+/* Reason for the last non-OK status returned on this thread ("" if none). */
+const char* dory_decode_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DORY_DECODE_H_ */

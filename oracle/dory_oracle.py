@@ -1,0 +1,266 @@
+"""CPU oracle of the decode-attention + KV-append path — TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline / reference legs may
+import this module, and only as the checker or the timed CPU baseline.  The product path
+(dory-vllm-experiments_b200/) never calls it: it has no CPU fallback.
+
+It restates, in PyTorch eager (FP32 on CPU) and NumPy, the semantics of the reference
+chrisbennight/dory-vllm-experiments:
+
+* justnorm / normalize_rows: x * rsqrt(sum(x^2) + eps), eps = 1e-6 inside the root
+  (vllm-patched/vllm/model_executor/models/dory.py:43-47, kernels/dory_common.py:20,
+  kernels/bench_decode_attention.py:100-101);
+* the raw-mode q, k, v of the attention kernel (kernels/dory_decode_attention.py:110-114,
+  :96): q = bf16((sqk * sqk_factor)^2 * norm(q)), k = bf16(norm(k)), v = bf16(v), and the
+  query scaling q = bf16(float(q) * softmax_scale) (:123);
+* the attended range [max(seq_len - window, 0), seq_len) or [0, seq_len) (:28-44, :131-133);
+* softmax attention through the paged block table (kernels/bench_decode_attention.py:58-68,
+  `reference_attention`), GQA by repeat_interleave;
+* padding: seq_len 0 gives a zero output (:218-219), slot < 0 writes nothing (:118);
+* gate product and the nibble-major store out[e % 8][e / 8] (:220-222,
+  kernels/w4a16_gemv.py:91-93);
+* multi-token calls (:270-305): token t uses cache_offsets[t] and block_table_offsets[t];
+  shared_cache=True caches every token's k/v before any attention (:294-301), which the
+  reference's own test checks against single-token calls in position order
+  (kernels/bench_multi_token.py:160-197).
+
+Normalisation arithmetic (bit-exact cache contract).  Sum x^2 is accumulated in FP64 and
+rounded once to FP32, eps is added in FP32, and the inverse square root is the correctly
+rounded FP32 value; the product x * r and the bf16 rounding are FP32 round-to-nearest-even.
+This removes the dependence of the FP32 sum on reduction order, which differs between
+PyTorch's CPU builds (AVX2 vs AVX-512) and GPU kernels; the CUDA kernel computes exactly
+these quantities, so appended cache rows compare bit for bit.  Against PyTorch's own FP32
+`normalize_rows` the result agrees to the bit on the large majority of rows and within one
+bf16 ulp elsewhere (tests/test_oracle.py measures both).
+
+Parity is pinned by tests/golden/*.npz, produced by tests/golden/make_golden.py from the
+reference's own eager functions (`reference_attention`, `normalize_rows`, `to_nibble_major`).
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import torch
+
+EPS = 1e-6
+
+
+# ---------------------------------------------------------------------------------------
+# normalisation (dory.py:43-47; dory_decode_attention.py:110-114)
+# ---------------------------------------------------------------------------------------
+
+def inv_norm(x: np.ndarray, eps: float = EPS) -> np.ndarray:
+    """Canonical FP32 1/sqrt(sum(x^2) + eps) over the last axis of an FP32 array."""
+    x = np.asarray(x, dtype=np.float32)
+    s32 = np.sum(x.astype(np.float64) ** 2, axis=-1).astype(np.float32)
+    t = (s32 + np.float32(eps)).astype(np.float32)
+    return (1.0 / np.sqrt(t.astype(np.float64))).astype(np.float32)
+
+
+def normalize(x: np.ndarray, eps: float = EPS) -> np.ndarray:
+    """FP32 x * inv_norm(x) (the product rounded once to FP32)."""
+    x = np.asarray(x, dtype=np.float32)
+    return (x * inv_norm(x, eps)[..., None]).astype(np.float32)
+
+
+def bf16(x) -> torch.Tensor:
+    """Round-to-nearest-even FP32 -> bfloat16 (torch's conversion)."""
+    return torch.as_tensor(np.asarray(x, dtype=np.float32)).to(torch.bfloat16)
+
+
+def raw_qkv(qk: torch.Tensor, v: torch.Tensor, sqk: torch.Tensor, sqk_factor: float,
+            eps: float, num_heads: int, num_kv_heads: int, head_dim: int):
+    """(q bf16 [NH, HD] before the softmax scale, k bf16 [NKV, HD], v bf16 [NKV, HD]) of one
+    token, as the raw-mode kernel computes them (dory_decode_attention.py:93-96,110-114)."""
+    NH, NKV, HD = num_heads, num_kv_heads, head_dim
+    x = qk.detach().float().cpu().numpy().reshape(NH + NKV, HD)
+    s = (sqk.detach().float().cpu().numpy().reshape(NH, HD).astype(np.float32)
+         * np.float32(sqk_factor)).astype(np.float32)
+    qn = normalize(x[:NH], eps)
+    q = bf16((s * s).astype(np.float32) * qn)
+    k = bf16(normalize(x[NH:], eps))
+    vb = v.detach().float().cpu().reshape(NKV, HD).to(torch.bfloat16)
+    return q, k, vb
+
+
+def scaled_query(q_bf16: torch.Tensor, softmax_scale: float) -> torch.Tensor:
+    """The kernel's second rounding, q = bf16(float(q) * softmax_scale) (:123)."""
+    return (q_bf16.float() * np.float32(softmax_scale)).to(torch.bfloat16)
+
+
+# ---------------------------------------------------------------------------------------
+# paged attention (bench_decode_attention.py:58-68; dory_decode_attention.py:28-44,130-161)
+# ---------------------------------------------------------------------------------------
+
+def attended(seq_len: int, window: int) -> tuple[int, int]:
+    first = max(seq_len - window, 0) if window > 0 else 0
+    return first, seq_len
+
+
+def gather(cache: torch.Tensor, table: torch.Tensor, positions: torch.Tensor,
+           block_size: int) -> torch.Tensor:
+    """cache [blocks, B, NKV, HD] rows for logical positions -> FP32 [len, NKV, HD]."""
+    blocks = table[positions // block_size].long()
+    return cache[blocks, positions % block_size].float()
+
+
+def attention(q: torch.Tensor, key: torch.Tensor, value: torch.Tensor,
+              table: torch.Tensor, seq_len: int, window: int, num_heads: int,
+              block_size: int, softmax_scale: float, second_rounding: bool = True
+              ) -> torch.Tensor:
+    """FP32 softmax attention of one token from its bf16 query [NH, HD].
+
+    second_rounding=True follows the attention kernel (q = bf16(float(q) * scale) before the
+    dot products, dory_decode_attention.py:123); False follows the reference's FP32 test
+    oracle `reference_attention` (bench_decode_attention.py:58-68), which scales the FP32
+    scores instead.  Returns FP32 [NH * HD]; zero for seq_len 0 (:218-219)."""
+    first, last = attended(seq_len, window)
+    HD = key.shape[-1]
+    if last <= first:
+        return torch.zeros(num_heads * HD)
+    positions = torch.arange(first, last)
+    keys = gather(key, table, positions, block_size)
+    values = gather(value, table, positions, block_size)
+    group = num_heads // keys.shape[1]
+    keys = keys.repeat_interleave(group, dim=1)
+    values = values.repeat_interleave(group, dim=1)
+    q = q.reshape(num_heads, -1).cpu()
+    if second_rounding:
+        scores = torch.einsum("hd,thd->ht", scaled_query(q, softmax_scale).float(), keys)
+    else:
+        scores = torch.einsum("hd,thd->ht", q.float(), keys) * softmax_scale
+    return torch.einsum("ht,thd->hd", scores.softmax(dim=-1), values).reshape(-1)
+
+
+def nibble_major(x: torch.Tensor) -> torch.Tensor:
+    """FP32 [Q] -> [8, Q/8] with element [j, w] = x[8w + j] (w4a16_gemv.py:91-93)."""
+    return x.float().reshape(-1, 8).t().contiguous()
+
+
+# ---------------------------------------------------------------------------------------
+# the three entry points (dory_decode_attention.py:248-305); caches are modified in place
+# ---------------------------------------------------------------------------------------
+
+def _write(key, value, slot: int, block_size: int, k_new, v_new):
+    key[slot // block_size, slot % block_size] = k_new
+    value[slot // block_size, slot % block_size] = v_new
+
+
+def call(q: torch.Tensor, key, value, block_table, seq_len: int, window: int,
+         softmax_scale: float, gate: torch.Tensor, num_heads: int,
+         second_rounding: bool = True) -> torch.Tensor:
+    """DecodeAttention.__call__: q bf16 [NH*HD] already normalised; returns [8, Q/8]."""
+    B = key.shape[1]
+    out = attention(q, key, value, block_table, seq_len, window, num_heads, B, softmax_scale,
+                    second_rounding)
+    return nibble_major(out * gate.float().cpu())
+
+
+def from_raw(qk, v, sqk, sqk_factor, eps, slot: int, key, value, block_table, seq_len: int,
+             window: int, softmax_scale: float, gate, num_heads: int, num_kv_heads: int,
+             second_rounding: bool = True) -> torch.Tensor:
+    """DecodeAttention.from_raw on CPU tensors: appends at `slot` (if >= 0 and the token is
+    not padding) and returns the gated output [8, Q/8].  The attention sees the new k/v at
+    position seq_len - 1 (the reference substitutes them from registers, :141-145)."""
+    HD = key.shape[-1]
+    B = key.shape[1]
+    q, k_new, v_new = raw_qkv(qk, v, sqk, sqk_factor, eps, num_heads, num_kv_heads, HD)
+    if seq_len > 0:
+        pos = seq_len - 1
+        phys = int(block_table[pos // B])
+        saved_k = key[phys, pos % B].clone()
+        saved_v = value[phys, pos % B].clone()
+        key[phys, pos % B], value[phys, pos % B] = k_new, v_new
+        out = attention(q, key, value, block_table, seq_len, window, num_heads, B,
+                        softmax_scale, second_rounding)
+        key[phys, pos % B], value[phys, pos % B] = saved_k, saved_v
+        if slot >= 0:
+            _write(key, value, slot, B, k_new, v_new)
+    else:
+        out = torch.zeros(num_heads * HD)
+    return nibble_major(out * gate.float().cpu())
+
+
+def multi_from_raw(qk, v, sqk, sqk_factor, eps, cache_offsets, key_flat, value_flat,
+                   cache_shape, cache_strides, block_tables_flat, block_table_offsets,
+                   seq_lens, window: int, softmax_scale: float, gate, num_heads: int,
+                   num_kv_heads: int, shared_cache: bool = False,
+                   second_rounding: bool = True) -> torch.Tensor:
+    """DecodeAttention.multi_from_raw on CPU.  key_flat / value_flat are the flat storage
+    the caches live in; token t's cache view is as_strided(cache_shape, cache_strides,
+    offset = cache_offsets[t]), its table block_tables_flat[block_table_offsets[t]:].
+    Returns the gated outputs [T, 8, Q/8]."""
+    T = qk.shape[0]
+    HD = cache_shape[-1]
+    B = cache_shape[1]
+    views = []
+    news = []
+    for t in range(T):
+        off = int(cache_offsets[t])
+        kv = key_flat.as_strided(cache_shape, cache_strides, off)
+        vv = value_flat.as_strided(cache_shape, cache_strides, off)
+        table = block_tables_flat[int(block_table_offsets[t]):]
+        views.append((kv, vv, table))
+        news.append(raw_qkv(qk[t], v[t], sqk, sqk_factor, eps, num_heads, num_kv_heads, HD))
+    outs = []
+    if shared_cache:
+        # write-all-first (dory_decode_attention.py:294-301), in token order
+        for t in range(T):
+            n = int(seq_lens[t])
+            if n > 0:
+                kv, vv, table = views[t]
+                pos = n - 1
+                slot = int(table[pos // B]) * B + pos % B
+                _write(kv, vv, slot, B, news[t][1], news[t][2])
+        for t in range(T):
+            kv, vv, table = views[t]
+            out = attention(news[t][0], kv, vv, table, int(seq_lens[t]), window, num_heads,
+                            B, softmax_scale, second_rounding)
+            outs.append(nibble_major(out * gate[t].float().cpu()))
+    else:
+        for t in range(T):
+            kv, vv, table = views[t]
+            n = int(seq_lens[t])
+            if n > 0:
+                pos = n - 1
+                slot = int(table[pos // B]) * B + pos % B
+                saved_k, saved_v = kv[slot // B, slot % B].clone(), vv[slot // B, slot % B].clone()
+                _write(kv, vv, slot, B, news[t][1], news[t][2])
+                out = attention(news[t][0], kv, vv, table, n, window, num_heads, B,
+                                softmax_scale, second_rounding)
+                kv[slot // B, slot % B], vv[slot // B, slot % B] = saved_k, saved_v
+            else:
+                out = torch.zeros(num_heads * HD)
+            outs.append(nibble_major(out * gate[t].float().cpu()))
+        for t in range(T):  # the appends land after every token has attended
+            kv, vv, table = views[t]
+            n = int(seq_lens[t])
+            if n > 0:
+                pos = n - 1
+                slot = int(table[pos // B]) * B + pos % B
+                _write(kv, vv, slot, B, news[t][1], news[t][2])
+    return torch.stack(outs)
+
+
+def split_layout(seq_len: int, window: int, block_size: int, splits: int,
+                 blocks_per_tile: int) -> tuple[int, int, int, int, int]:
+    """The reference's _split_layout (dory_decode_attention.py:28-44): (seq_len, first,
+    first_block, tiles, tiles_per_split)."""
+    first = max(seq_len - window, 0) if window > 0 else 0
+    first_block = first // block_size
+    num_blocks = -(-seq_len // block_size) - first_block
+    tiles = -(-num_blocks // blocks_per_tile)
+    return seq_len, first, first_block, tiles, max(-(-tiles // splits), 1)
+
+
+def relative_error(x: torch.Tensor, reference: torch.Tensor) -> float:
+    """Relative L2 error (kernels/bench_mlp.py:120-121)."""
+    x, reference = x.float().flatten(), reference.float().flatten()
+    denom = reference.norm().item()
+    return (x - reference).norm().item() / (denom if denom > 0 else 1.0)
+
+
+def softmax_scale(head_dim: int) -> float:
+    return 1.0 / math.sqrt(head_dim)

@@ -1,0 +1,54 @@
+"""Golden-case specifications shared by make_golden.py (which evaluates them with the
+reference's own eager functions) and the tests (which rebuild the same seeded inputs)."""
+
+from __future__ import annotations
+
+import hashlib
+
+import numpy as np
+import torch
+
+import workloads as W
+
+# Sequence lengths around block and window boundaries (the reference's edge-case list,
+# EXPERIMENTS.md:325-327 — 0, 1, 15-17, 1023-1025, 1040, 3000 — with seq_len = context + 1).
+EDGE_SEQ_LENS = (1, 15, 16, 17, 1023, 1024, 1025, 1040, 3000)
+
+
+def specs() -> dict:
+    """name -> zero-argument builder of a workloads.Case."""
+    out = {
+        # configuration 1: 32q/8kv x 128, block 16, 640 cached tokens, 64-block pool, seed 0
+        "config1": lambda: W.single(seed=0, context=640, pool_blocks=64),
+        "single_window": lambda: W.single(seed=10, context=1500, pool_blocks=100, window=1024),
+        # the real model's attention shape: 16q/4kv x 256, sliding window 1024
+        "dory_shape": lambda: W.single(seed=11, context=1100, pool_blocks=80, window=1024,
+                                       num_heads=16, num_kv_heads=4, head_dim=256),
+        "gqa8": lambda: W.single(seed=12, context=777, pool_blocks=60, num_heads=32,
+                                 num_kv_heads=4, head_dim=128),
+        # shared-KV wavefront (configuration 2 shape, short prompt for CPU speed)
+        "wavefront": lambda: W.wavefront(seed=1, prompt=700, generated=37, tokens=4),
+        "wavefront_window": lambda: W.wavefront(seed=13, prompt=1010, generated=5, tokens=4,
+                                                window=1024),
+        "wavefront_t2": lambda: W.wavefront(seed=14, prompt=333, generated=0, tokens=2),
+        # batched independent sequences (configuration 3 shape, few sequences)
+        "batched": lambda: W.batched(seed=2, lens=[128, 1152, 15, 640, 16, 300]),
+    }
+    for i, n in enumerate(EDGE_SEQ_LENS):
+        for window in (0, 1024):
+            out[f"edge_{n}_w{window}"] = (
+                lambda n=n, window=window, i=i: W.single(
+                    seed=100 + i, context=n - 1, pool_blocks=200, window=window, num_heads=8,
+                    num_kv_heads=2, head_dim=64))
+    return out
+
+
+def digest(case: W.Case) -> str:
+    """SHA-256 over every input tensor of a case (checks that regeneration matches)."""
+    h = hashlib.sha256()
+    for t in (case.qk, case.v, case.gate, case.sqk.float(), case.key, case.value, case.tables):
+        h.update(np.ascontiguousarray(t.float().numpy() if t.dtype != torch.int32
+                                      else t.numpy()).tobytes())
+    h.update(np.asarray(case.seq_lens, dtype=np.int64).tobytes())
+    h.update(np.asarray(case.table_rows, dtype=np.int64).tobytes())
+    return h.hexdigest()

@@ -1,0 +1,295 @@
+"""Parity of the sm_100a kernel (through DecodeAttention and the C ABI) with the reference.
+
+* Outputs against the golden vectors from the reference's own eager code, within the
+  BASELINE bar (2e-2 abs / 1e-2 rel) and a relative-L2 bound.
+* The whole cache pool after the call, bit for bit: only the appended slots change and they
+  hold the oracle's rows (the reference's appended rows agree with those to the bit on
+  all but ~1e-5 of elements, within one bf16 ulp there).
+* Every cache layout the drop-in must read; split counts, tiles, windows, edge lengths,
+  padding tokens, per-loop offsets, shared-cache wavefronts, batched sequences, the non-raw
+  __call__, CUDA-graph replay, error words.
+"""
+
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+import dory_oracle as O
+import specs
+import workloads as W
+from dory_decode_attention import EPS, DecodeAttention
+from gpu_helpers import assert_close, expected_raw, oracle_out, oracle_rows, run
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+CASES = specs.specs()
+SINGLE = sorted(n for n in CASES if n not in ("wavefront", "wavefront_window", "wavefront_t2",
+                                               "batched"))
+MULTI = ["wavefront", "wavefront_window", "wavefront_t2", "batched"]
+
+
+def golden(name):
+    g = np.load(GOLDEN / f"{name}.npz")
+    return torch.from_numpy(g["out"]), g
+
+
+def check_cache(case, layout, d, before):
+    exp = expected_raw(case, layout, before, oracle_rows(case))
+    got = d["raw"].cpu()
+    assert torch.equal(got.view(torch.int16), exp.view(torch.int16)), \
+        f"{int((got.view(torch.int16) != exp.view(torch.int16)).sum())} cache elements differ"
+
+
+@pytest.mark.parametrize("layout", W.LAYOUTS)
+@pytest.mark.parametrize("name", SINGLE)
+def test_single_token_golden(name, layout):
+    case = CASES[name]()
+    out, d, before = run(case, layout)
+    ref, _ = golden(name)
+    assert_close(out, ref)
+    check_cache(case, layout, d, before)
+
+
+@pytest.mark.parametrize("layout", W.LAYOUTS)
+@pytest.mark.parametrize("name", MULTI)
+def test_multi_token_golden(name, layout):
+    case = CASES[name]()
+    out, d, before = run(case, layout)
+    ref, _ = golden(name)
+    assert_close(out, ref)
+    check_cache(case, layout, d, before)
+
+
+@pytest.mark.parametrize("splits,bpt,min_bps", [(1, 1, 1), (3, 1, 1), (32, 2, 1), (64, 1, 1),
+                                                (7, 1, 4), (32, 1, 8), (148, 1, 1)])
+@pytest.mark.parametrize("name", ["config1", "single_window", "wavefront", "batched"])
+def test_split_layouts(name, splits, bpt, min_bps):
+    case = CASES[name]()
+    out, d, before = run(case, "triton", splits=splits, blocks_per_tile=bpt,
+                         min_blocks_per_split=min_bps)
+    ref, _ = golden(name)
+    assert_close(out, ref)
+    check_cache(case, "triton", d, before)
+
+
+def test_single_token_via_multi_entry_is_identical():
+    """multi_from_raw with one token equals from_raw bit for bit (the reference records the
+    same property, multi-token attention bit-identical to single calls)."""
+    case = CASES["config1"]()
+    a, _, _ = run(case, "triton", single_entry=True)
+    b, _, _ = run(case, "triton", single_entry=False)
+    assert torch.equal(a, b)
+
+
+def test_repeat_is_deterministic():
+    case = CASES["single_window"]()
+    a, _, _ = run(case, "triton")
+    b, _, _ = run(case, "triton")
+    assert torch.equal(a, b)
+
+
+def test_non_raw_call_matches_golden():
+    """__call__ (q already normalised and scaled, its k/v already cached) on the cache the
+    raw call left behind gives the golden output."""
+    name = "config1"
+    case = CASES[name]()
+    out, d, _ = run(case, "triton")
+    _, g = golden(name)
+    q = torch.from_numpy(g["q_bf16"][0]).view(torch.bfloat16).cuda().reshape(-1)
+    attn = DecodeAttention(32, 8, 128, torch.device("cuda"))
+    out2 = torch.full_like(d["out"][0], float("nan"))
+    attn(q, d["key"], d["value"], d["tables"][0], d["seq_lens"][0:1], case.window, case.scale,
+         d["gate"][0], out2)
+    torch.cuda.synchronize()
+    assert_close(out2.cpu(), golden(name)[0][0])
+
+
+def test_padding_slot_negative_writes_nothing():
+    case = CASES["config1"]()
+    d = W.to_device(case, "triton", "cuda")
+    before = d["raw"].clone()
+    attn = DecodeAttention(32, 8, 128, torch.device("cuda"))
+    slot = torch.tensor([-1], dtype=torch.int64, device="cuda")
+    attn.from_raw(d["qk"][0], d["v"][0], d["sqk"], case.sqk_factor, EPS, slot, d["key"],
+                  d["value"], d["tables"][0], d["seq_lens"][0:1], 0, case.scale, d["gate"][0],
+                  d["out"][0])
+    torch.cuda.synchronize()
+    attn.check_errors()
+    assert torch.equal(d["raw"], before)
+    # the attention itself still sees the new token (reference substitutes it from registers)
+    assert_close(d["out"][0].cpu(), golden("config1")[0][0])
+
+
+def test_padding_seq_len_zero():
+    case = W.batched(seed=7, lens=[200, 50, 700], num_heads=32, num_kv_heads=8)
+    case.seq_lens[1] = 0  # a padding request inside the batch
+    out, d, before = run(case, "triton")
+    ref = oracle_out(case)
+    assert torch.count_nonzero(out[1]) == 0
+    assert_close(out, ref)
+    check_cache(case, "triton", d, before)
+    # padding in single-token mode: zero output, no write
+    one = CASES["config1"]()
+    one.seq_lens[0] = 0
+    out, d, before = run(one, "triton")
+    assert torch.count_nonzero(out) == 0
+    assert torch.equal(d["raw"].cpu(), before.cpu())
+
+
+def test_per_loop_cache_offsets():
+    """Tokens at different loop depths, each with its own cache (element offsets into one
+    allocation, as dory_wavefront.py:137-151,194-195) and its own shuffled block table."""
+    T, P = 4, 40
+    cases = [W.single(seed=200 + t, context=500 - 3 * t, pool_blocks=P) for t in range(T)]
+    raws, keys, values = [], [], []
+    raw = torch.empty(T, P, 8, 16, 256, dtype=torch.bfloat16, device="cuda")
+    for t, c in enumerate(cases):
+        k, v = raw[t].transpose(1, 2).split(128, dim=-1)
+        k.copy_(c.key.to(torch.bfloat16))
+        v.copy_(c.value.to(torch.bfloat16))
+    key, value = raw[0].transpose(1, 2).split(128, dim=-1)
+    cache_offsets = torch.arange(T, dtype=torch.int64, device="cuda") * raw[0].numel()
+    tables = torch.stack([c.tables[0] for c in cases]).cuda()
+    table_offsets = torch.arange(T, dtype=torch.int64, device="cuda") * P
+    qk = torch.stack([c.qk[0] for c in cases]).cuda()
+    v_in = torch.stack([c.v[0] for c in cases]).cuda()
+    gate = torch.stack([c.gate[0] for c in cases]).cuda()
+    seq_lens = torch.tensor([c.seq_lens[0] for c in cases], dtype=torch.int32, device="cuda")
+    sqk = cases[0].sqk.cuda()
+    out = torch.full((T, 8, 512), float("nan"), device="cuda")
+    before = raw.clone().cpu()
+    attn = DecodeAttention(32, 8, 128, torch.device("cuda"), max_tokens=T)
+    attn.multi_from_raw(qk, v_in, sqk, 0.7, EPS, cache_offsets, key, value, tables,
+                        table_offsets, seq_lens, 0, 128 ** -0.5, gate, out)
+    torch.cuda.synchronize()
+    attn.check_errors()
+    for t, c in enumerate(cases):
+        c.sqk = cases[0].sqk
+        ref = oracle_out(c)
+        assert_close(out[t].cpu(), ref[0])
+        exp = expected_raw(c, "triton", before[t], oracle_rows(c))
+        assert torch.equal(raw[t].cpu().view(torch.int16), exp.view(torch.int16))
+
+
+@pytest.mark.parametrize("block_size", [32, 64])
+def test_larger_block_sizes(block_size):
+    for case in (W.single(seed=31, context=900, pool_blocks=40, block_size=block_size,
+                          window=512),
+                 W.wavefront(seed=32, prompt=600, tokens=4, pool_blocks=30,
+                             block_size=block_size),
+                 W.batched(seed=33, lens=[100, 1000, 31, 32, 33], block_size=block_size)):
+        out, d, before = run(case, "unbind")
+        assert_close(out, oracle_out(case))
+        check_cache(case, "unbind", d, before)
+
+
+@pytest.mark.parametrize("tokens", [3, 8, 16])
+def test_shared_wavefront_token_counts(tokens):
+    case = W.wavefront(seed=40 + tokens, prompt=450, generated=3, tokens=tokens)
+    out, d, before = run(case, "triton")
+    assert_close(out, oracle_out(case))
+    check_cache(case, "triton", d, before)
+
+
+def test_shared_with_distinct_tables_falls_back_per_token():
+    """shared_cache with tokens reading through different table rows of one pool: the
+    kernel cannot group them, processes them per token and still substitutes every
+    token's new entry where it aliases (write-all-first semantics)."""
+    case = W.wavefront(seed=50, prompt=300, tokens=4)
+    width = case.tables.shape[1]
+    # two identical copies of the table: tokens 0,1 use row 0, tokens 2,3 use row 1
+    case.tables = torch.cat([case.tables, case.tables])
+    case.table_rows = [0, 0, 1, 1]
+    out, d, before = run(case, "triton")
+    assert_close(out, oracle_out(case))
+    check_cache(case, "triton", d, before)
+    assert case.tables.shape[1] == width
+
+
+def test_gqa_groups_and_head_dims():
+    for nh, nkv, hd in ((8, 8, 128), (16, 2, 64), (32, 2, 128), (16, 4, 256), (8, 1, 256)):
+        case = W.single(seed=60 + nh + hd, context=333, pool_blocks=30, num_heads=nh,
+                        num_kv_heads=nkv, head_dim=hd, window=200)
+        out, d, before = run(case, "bench")
+        assert_close(out, oracle_out(case))
+        check_cache(case, "bench", d, before)
+
+
+def test_cuda_graph_replay_matches_eager():
+    case = CASES["single_window"]()
+    d = W.to_device(case, "triton", "cuda")
+    attn = DecodeAttention(32, 8, 128, torch.device("cuda"))
+
+    def step():
+        attn.from_raw(d["qk"][0], d["v"][0], d["sqk"], case.sqk_factor, EPS, d["slots"][0:1],
+                      d["key"], d["value"], d["tables"][0], d["seq_lens"][0:1], case.window,
+                      case.scale, d["gate"][0], d["out"][0])
+
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    eager = d["out"].clone()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step()
+    for _ in range(3):
+        d["out"].fill_(float("nan"))
+        graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(d["out"], eager)
+    attn.check_errors()
+
+
+def test_out_of_range_block_is_reported_not_dereferenced():
+    case = W.single(seed=70, context=300, pool_blocks=30)
+    d = W.to_device(case, "triton", "cuda")
+    bad = d["tables"].clone()
+    bad[0, 3] = 10_000_000  # far outside the 30-block pool
+    attn = DecodeAttention(32, 8, 128, torch.device("cuda"))
+    attn.from_raw(d["qk"][0], d["v"][0], d["sqk"], case.sqk_factor, EPS, d["slots"][0:1],
+                  d["key"], d["value"], bad[0], d["seq_lens"][0:1], 0, case.scale,
+                  d["gate"][0], d["out"][0])
+    torch.cuda.synchronize()
+    assert attn.fetch_errors() & 1  # DORY_DEVERR_BLOCK_OOB
+    assert attn.fetch_errors() == 0  # cleared
+
+
+def test_out_of_range_slot_is_reported_not_written():
+    case = W.single(seed=71, context=300, pool_blocks=30)
+    d = W.to_device(case, "triton", "cuda")
+    before = d["raw"].clone()
+    attn = DecodeAttention(32, 8, 128, torch.device("cuda"))
+    slot = torch.tensor([30 * 16 + 5], dtype=torch.int64, device="cuda")  # block 30 of 30
+    attn.from_raw(d["qk"][0], d["v"][0], d["sqk"], case.sqk_factor, EPS, slot, d["key"],
+                  d["value"], d["tables"][0], d["seq_lens"][0:1], 0, case.scale, d["gate"][0],
+                  d["out"][0])
+    torch.cuda.synchronize()
+    assert attn.fetch_errors() & 2  # DORY_DEVERR_SLOT_OOB
+    assert torch.equal(d["raw"], before)
+
+
+def test_argument_errors_raise_like_reference():
+    case = CASES["wavefront"]()
+    d = W.to_device(case, "triton", "cuda")
+    attn = DecodeAttention(32, 8, 128, torch.device("cuda"), max_tokens=2)
+    with pytest.raises(ValueError, match="too many tokens"):
+        attn.multi_from_raw(d["qk"], d["v"], d["sqk"], 0.7, EPS, d["cache_offsets"], d["key"],
+                            d["value"], d["tables"], d["table_offsets"], d["seq_lens"], 0,
+                            case.scale, d["gate"], d["out"], shared_cache=True)
+    attn = DecodeAttention(32, 8, 128, torch.device("cuda"), max_tokens=4)
+    with pytest.raises(ValueError, match="int64"):
+        attn.multi_from_raw(d["qk"], d["v"], d["sqk"], 0.7, EPS, d["cache_offsets"].int(),
+                            d["key"], d["value"], d["tables"], d["table_offsets"],
+                            d["seq_lens"], 0, case.scale, d["gate"], d["out"])
+    with pytest.raises(ValueError, match="equal strides"):
+        attn.from_raw(d["qk"][0], d["v"][0], d["sqk"], 0.7, EPS, d["slots"][0:1], d["key"],
+                      d["value"].contiguous(), d["tables"][0], d["seq_lens"][0:1], 0,
+                      case.scale, d["gate"][0], d["out"][0])

@@ -1,0 +1,103 @@
+"""The C-ABI library: builds for sm_100a, loads without a GPU, exports every symbol the
+header declares, and rejects bad arguments on the host before any CUDA call."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+import _native
+import build_native
+
+ROOT = Path(__file__).resolve().parent.parent
+HEADER = ROOT / "include" / "dory_decode.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    build_native.build()
+    return _native.load()
+
+
+def declared_functions() -> list[str]:
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"^\s*[A-Za-z_][\w\s\*]*?\b(dory_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_binding_exports():
+    assert declared_functions() == sorted(_native.EXPORTS)
+
+
+def test_every_declared_symbol_is_exported(lib):
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+
+
+def test_abi_version_and_struct_layout(lib):
+    assert lib.dory_decode_abi_version() == _native.ABI_VERSION
+    assert lib.dory_decode_params_bytes() == ctypes.sizeof(_native.DoryDecodeParams)
+
+
+def test_library_is_sm100a_only():
+    # The build targets exactly compute_100a / sm_100a (no PTX for other arches).
+    flags = " ".join(build_native.NVCC_FLAGS)
+    assert "arch=compute_100a,code=sm_100a" in flags
+    assert "sm_90" not in flags and "sm_89" not in flags
+
+
+def test_scratch_bytes(lib):
+    n = lib.dory_decode_scratch_bytes(4, 32, 32, 8, 128)
+    # partial outputs alone: 4 tokens x 32 splits x 32 heads x 128 dims x 4 B
+    assert n >= 4 * 32 * 32 * 128 * 4
+    assert n % 256 == 0
+    assert lib.dory_decode_scratch_bytes(0, 32, 32, 8, 128) == 0
+
+
+def _params(**kw):
+    p = _native.DoryDecodeParams()
+    dummy = 0x1000  # never dereferenced: validation fails before any CUDA call
+    for f in ("q", "v", "sqk", "slot_mapping", "key_cache", "value_cache", "block_table",
+              "seq_lens", "gate", "out_nibble_major", "scratch"):
+        setattr(p, f, dummy)
+    p.scratch_bytes = 1 << 30
+    p.stride_block, p.stride_offset, p.stride_head = 16 * 8 * 256, 256, 16 * 256
+    p.num_tokens, p.num_heads, p.num_kv_heads, p.head_dim = 1, 32, 8, 128
+    p.block_size, p.splits, p.blocks_per_tile, p.min_blocks_per_split = 16, 32, 1, 1
+    p.max_tokens, p.flags = 1, _native.FLAG_RAW_QKV
+    p.softmax_scale, p.eps, p.sqk_factor = 128 ** -0.5, 1e-6, 0.7
+    for k, val in kw.items():
+        setattr(p, k, val)
+    return p
+
+
+@pytest.mark.parametrize("kw,status,message", [
+    (dict(num_heads=30, num_kv_heads=8), _native.ERR_INVALID_ARGUMENT, "multiple of KV heads"),
+    (dict(num_tokens=2, max_tokens=1, flags=_native.FLAG_RAW_QKV | _native.FLAG_MULTI_TOKEN,
+          cache_offsets=0x1000, block_table_offsets=0x1000),
+     _native.ERR_INVALID_ARGUMENT, "too many tokens"),
+    (dict(head_dim=96), _native.ERR_UNSUPPORTED, "head_dim"),
+    (dict(block_size=8), _native.ERR_UNSUPPORTED, "block_size"),
+    (dict(stride_offset=100), _native.ERR_ALIGNMENT, "16-byte"),
+    (dict(key_cache=0x1004), _native.ERR_ALIGNMENT, "16-byte"),
+    (dict(scratch_bytes=64), _native.ERR_INVALID_ARGUMENT, "scratch too small"),
+    (dict(flags=_native.FLAG_MULTI_TOKEN | _native.FLAG_RAW_QKV), _native.ERR_INVALID_ARGUMENT,
+     "offsets"),
+    (dict(flags=_native.FLAG_SHARED_CACHE), _native.ERR_INVALID_ARGUMENT, "shared_cache"),
+    (dict(window=-1), _native.ERR_INVALID_ARGUMENT, "window"),
+])
+def test_host_validation(lib, kw, status, message):
+    p = _params(**kw)
+    assert lib.dory_decode_attention(ctypes.byref(p), None) == status
+    assert message in lib.dory_decode_last_error().decode()
+
+
+def test_status_maps_to_reference_exceptions(lib):
+    p = _params(num_heads=30)
+    with pytest.raises(ValueError, match="multiple of KV heads"):
+        _native.check(lib.dory_decode_attention(ctypes.byref(p), None))
+    p = _params(head_dim=96)
+    with pytest.raises(NotImplementedError):
+        _native.check(lib.dory_decode_attention(ctypes.byref(p), None))
