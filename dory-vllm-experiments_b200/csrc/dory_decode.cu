@@ -46,7 +46,7 @@ constexpr int kConsumerWarps = 4;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;  // + one producer warp
 constexpr int kChunk = 16;                           // cache rows per pipeline stage (MMA M)
 constexpr int kMaxSub = 16;                          // new tokens a CTA can substitute
-constexpr long long kWaitLimitCycles = 4000000000LL; // ~2 s at 1.9 GHz, then give up
+constexpr long long kWaitLimitCycles = 500000000LL;  // ~0.25 s at 1.9 GHz, then give up
 constexpr float kLog2e = 1.4426950408889634f;
 
 // ------------------------------------------------------------------------------------
