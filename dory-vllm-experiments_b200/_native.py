@@ -30,7 +30,10 @@ DEVERR_NAMES = {DEVERR_BLOCK_OOB: "block id out of range", DEVERR_SLOT_OOB: "slo
 # Every symbol include/dory_decode.h declares (checked by the CPU test suite).
 EXPORTS = ("dory_decode_abi_version", "dory_decode_params_bytes", "dory_decode_scratch_bytes",
            "dory_decode_scratch_init", "dory_decode_attention", "dory_decode_fetch_errors",
-           "dory_decode_last_error")
+           "dory_decode_last_error", "dory_decode_attention_static_scratch")
+
+# Size of the library's static scratch array (DORY_DECODE_STATIC_SCRATCH_BYTES).
+STATIC_SCRATCH_BYTES = 4 << 20
 
 _vp, _i32, _i64, _f32, _u32 = ctypes.c_void_p, ctypes.c_int32, ctypes.c_int64, ctypes.c_float, ctypes.c_uint32
 
@@ -80,6 +83,8 @@ def load(path: os.PathLike | None = None) -> ctypes.CDLL:
     lib.dory_decode_fetch_errors.argtypes = [_vp, ctypes.POINTER(_u32), _i32, _vp]
     lib.dory_decode_last_error.restype = ctypes.c_char_p
     lib.dory_decode_last_error.argtypes = []
+    lib.dory_decode_attention_static_scratch.restype = _i32
+    lib.dory_decode_attention_static_scratch.argtypes = [ctypes.POINTER(DoryDecodeParams), _vp]
     if lib.dory_decode_abi_version() != ABI_VERSION:
         raise RuntimeError(f"{path}: ABI version {lib.dory_decode_abi_version()} != {ABI_VERSION}")
     if lib.dory_decode_params_bytes() != ctypes.sizeof(DoryDecodeParams):

@@ -38,6 +38,8 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <mutex>
+
 #include "../../include/dory_decode.h"
 
 namespace {
@@ -968,3 +970,63 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------
+// Allocation-free entry point: the scratch is a file-scope device array of this library.
+// ------------------------------------------------------------------------------------
+namespace {
+
+// Split partials, merge counters and error word for callers that cannot allocate device
+// memory.  Device code could name it directly; host code only through the address
+// cudaGetSymbolAddress returns (the host-side symbol is a stand-in, not a device pointer).
+__device__ __align__(256) uint8_t g_static_scratch[DORY_DECODE_STATIC_SCRATCH_BYTES];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_static_mutex;
+void* g_static_ptr[kMaxDevices] = {nullptr};
+
+// Device address of g_static_scratch on the current device, looked up once per device.
+int32_t static_scratch_address(void** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(DORY_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+  if (dev < 0 || dev >= kMaxDevices)
+    return fail(DORY_ERR_UNSUPPORTED, "device ordinal %d beyond %d", dev, kMaxDevices);
+  std::lock_guard<std::mutex> lock(g_static_mutex);
+  if (!g_static_ptr[dev]) {
+    void* ptr = nullptr;
+    e = cudaGetSymbolAddress(&ptr, g_static_scratch);
+    if (e != cudaSuccess || ptr == nullptr)
+      return fail(DORY_ERR_CUDA, "cudaGetSymbolAddress(static scratch): %s",
+                  cudaGetErrorString(e));
+    g_static_ptr[dev] = ptr;
+  }
+  *out = g_static_ptr[dev];
+  return DORY_OK;
+}
+
+}  // namespace
+
+extern "C" int32_t dory_decode_attention_static_scratch(const DoryDecodeParams* P, void* stream) {
+  if (!P) return fail(DORY_ERR_INVALID_ARGUMENT, "null params");
+  if (P->max_tokens < 1 || P->splits < 1 || P->num_heads < 1 || P->num_kv_heads < 1 ||
+      P->head_dim < 1)
+    return fail(DORY_ERR_INVALID_ARGUMENT, "invalid scratch shape");
+  const ScratchLayout SL =
+      scratch_layout(P->max_tokens, P->splits, P->num_heads, P->num_kv_heads, P->head_dim);
+  if (SL.total > DORY_DECODE_STATIC_SCRATCH_BYTES)
+    return fail(DORY_ERR_INVALID_ARGUMENT,
+                "this call needs %lld bytes of scratch; the static scratch holds %lld "
+                "(use fewer splits or tokens, or dory_decode_attention with caller scratch)",
+                (long long)SL.total, (long long)DORY_DECODE_STATIC_SCRATCH_BYTES);
+  void* scratch = nullptr;
+  const int32_t st = static_scratch_address(&scratch);
+  if (st != DORY_OK) return st;
+  // The previous call's counters and error word must not leak into this one.
+  cudaError_t e = cudaMemsetAsync(scratch, 0, size_t(SL.pml), (cudaStream_t)stream);
+  if (e != cudaSuccess) return fail(DORY_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
+  DoryDecodeParams a = *P;
+  a.scratch = scratch;
+  a.scratch_bytes = DORY_DECODE_STATIC_SCRATCH_BYTES;
+  return dory_decode_attention(&a, stream);
+}

@@ -137,6 +137,30 @@ int32_t dory_decode_scratch_init(void* scratch, int64_t scratch_bytes, void* str
  */
 int32_t dory_decode_attention(const DoryDecodeParams* params, void* stream);
 
+/*
+ * dory_decode_attention without caller-owned scratch, for callers that cannot allocate
+ * device memory: code that enqueues work while a CUDA graph is being captured in the
+ * global capture mode (where cudaMalloc is an error), engines that have already reserved
+ * the whole device for their own KV-cache allocator, and foreign-function hosts with no
+ * device allocator of their own.  No counterpart in the reference (its DecodeAttention
+ * always allocates its scratch, dory_decode_attention.py:242-246).
+ *
+ * Takes the same parameters; `scratch` and `scratch_bytes` are ignored.  The split partials,
+ * merge counters and error word live instead in one statically sized device array inside
+ * this library (DORY_DECODE_STATIC_SCRATCH_BYTES = 4 MiB), which every GPU that loads the
+ * library holds until the process exits.  A call whose layout needs more scratch than that
+ * (max_tokens * splits * num_heads * head_dim * 4 bytes of partials, plus counters) fails
+ * with DORY_ERR_INVALID_ARGUMENT.  Allocates nothing: no cudaMalloc, no cudaFree.
+ *
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress,
+ * with that device current) and must therefore happen before any stream capture on that
+ * device.  Every call clears the merge counters and the error word on `stream` before its
+ * kernel.  All calls share the one array and it keeps the last call's contents, so calls
+ * that can overlap on the GPU (different streams, without ordering between them) race.
+ */
+#define DORY_DECODE_STATIC_SCRATCH_BYTES (4ll << 20)
+int32_t dory_decode_attention_static_scratch(const DoryDecodeParams* params, void* stream);
+
 /* Copies the device error word (DORY_DEVERR_* bits) to *flags_out, synchronising `stream`;
  * clears it when `clear` is non-zero.  The only entry point that waits on the device. */
 int32_t dory_decode_fetch_errors(void* scratch, uint32_t* flags_out, int32_t clear, void* stream);
