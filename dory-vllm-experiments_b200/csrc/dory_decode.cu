@@ -17,9 +17,12 @@
 //
 // B200 design:
 //   * K/V rows (head_dim * 2 bytes, contiguous for any of the three cache layouts) are
-//     staged into a multi-stage shared-memory ring by the TMA engine (cp.async.bulk, one
-//     row per lane of a producer warp, mbarrier complete_tx), rows padded by 16 bytes so
-//     ldmatrix reads are bank-conflict free.  Only rows inside the attended range are read.
+//     staged into a multi-stage shared-memory ring by a producer warp with 16-byte cp.async
+//     copies (two whole rows per warp instruction) that complete onto mbarriers; rows are
+//     padded by 16 bytes so ldmatrix reads are bank-conflict free.  Only rows inside the
+//     attended range are read; the others are zero-filled in flight.  (One cp.async.bulk
+//     per 256-byte row was measured first: the copy engine's per-request cost, ~1.3 us per
+//     16-row chunk, capped a CTA at a few GB/s.)
 //   * Four consumer warps each own a ring slot in turn and run the 16-token chunk through
 //     mma.sync m16n8k16 (bf16 in, fp32 accumulate) with tokens on M and the GQA group's query
 //     rows (plus the other tokens of a shared-cache group) on N: S^T = K Q^T, then
@@ -31,6 +34,8 @@
 //     drains its own copies before returning.  Out-of-range block ids / slots are recorded
 //     and skipped, never dereferenced.
 
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdarg.h>
@@ -55,6 +60,8 @@ constexpr float kLog2e = 1.4426950408889634f;
 // Kernel parameters (device-side copy of DoryDecodeParams plus derived values).
 // ------------------------------------------------------------------------------------
 struct KParams {
+  CUtensorMap tmk;  // K / V cache views as 4-D tensors (dims sorted by stride), 16x64 boxes,
+  CUtensorMap tmv;  // 128-byte swizzle; valid when tm_ok
   const void* q;
   const float* v;
   const void* sqk;
@@ -77,6 +84,9 @@ struct KParams {
   int raw, multi, shared;
   int q_stride;  // elements of q per token
   int nsub;      // new tokens whose k/v this call substitutes (shared: T, raw: 1, else 0)
+  int tm_ok;     // tensor maps usable
+  int tm_rowdim; // tensor dim (1 or 2) that indexes the row within a block (the other: head)
+  int64_t tm_blocks;  // extent of the block dimension of the tensor maps
 };
 
 // Scratch layout (bytes), shared by host and device.
@@ -94,17 +104,24 @@ __host__ __device__ inline ScratchLayout scratch_layout(int max_tokens, int S, i
   return L;
 }
 
-// Dynamic shared memory layout for one instantiation.
+// Dynamic shared memory layout for one instantiation.  Each ring stage holds the K tile
+// and then the V tile of one 16-row chunk, each as HD / 64 boxes of [16 rows][64 dims] bf16
+// in the 128-byte swizzle of the tensor copies: the 16-byte piece j of row r sits at
+// r * 128 + ((j ^ (r % 8)) * 16) within its box, so ldmatrix rows never share banks.
+constexpr int kBoxBytes = kChunk * 128;
+__host__ __device__ constexpr uint32_t tile_off(int r, int d) {  // d: a multiple of 8
+  return uint32_t((d >> 6) * kBoxBytes + r * 128 + ((((d >> 3) & 7) ^ (r & 7)) << 4));
+}
 template <int HD, int NS>
 struct Smem {
-  static constexpr int kRowBytes = HD * 2 + 16;               // padded row
-  static constexpr int kStageBytes = 2 * kChunk * kRowBytes;  // K rows then V rows
-  static constexpr int kStages = 0;
+  static constexpr int kTileBytes = (HD / 64) * kBoxBytes;    // one K (or V) tile
+  static constexpr int kStageBytes = 2 * kTileBytes;
+  static constexpr int kStages = 0;                           // 1024-byte aligned at run time
   static constexpr int kBars = kStages + NS * kStageBytes;    // full[NS], empty[NS]
-  static constexpr int kMeta = kBars + 2 * NS * 8;            // int4 {phys, mask, chunk, -}
+  static constexpr int kMeta = kBars + 2 * NS * 8;            // int4 {phys, -, chunk, -}
   static constexpr int kQ = kMeta + NS * 16;                  // bf16 [16][HD]
   static constexpr int kSub = kQ + 16 * HD * 2;               // bf16 [nsub][2][HD]
-  static int bytes(int nsub) { return kSub + (nsub > 0 ? nsub : 1) * 2 * HD * 2; }
+  static int bytes(int nsub) { return kSub + (nsub > 0 ? nsub : 1) * 2 * HD * 2 + 1024; }
 };
 
 // ------------------------------------------------------------------------------------
@@ -143,16 +160,48 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
   }
   return true;
 }
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes,
-                                         uint32_t bar) {
+// K/V rows are read once per launch: mark them first to leave L2 (evict_first), so the
+// small, re-read data (block tables, seq lens, q/k/v/gate rows, split partials) stays.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t policy;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  return policy;
+}// One box of a tensor map into shared memory, completing on `bar` (no multicast).
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                            int c2, int c3, uint32_t bar, uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
-          "r"(dst),
-      "l"(src), "r"(bytes), "r"(bar)
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar),
+      "l"(policy)
       : "memory");
 }
+__device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+// Orders this thread's generic-proxy shared-memory writes before later tensor copies.
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+// 16-byte global->shared copy; src_bytes 0 reads nothing and zero-fills the 16 bytes.
+__device__ __forceinline__ void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes,
+                                            uint64_t policy) {
+  asm volatile(
+      "cp.async.cg.shared.global.L2::cache_hint.L2::256B [%0], [%1], 16, %2, %3;" ::"r"(dst),
+      "l"(src), "r"(src_bytes), "l"(policy)
+      : "memory");
+}
+// The mbarrier receives one arrival when all of this thread's earlier cp.async copies landed.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+__device__ __forceinline__ void prefetch_l2(const void* ptr) {
+  asm volatile("prefetch.global.L2 [%0];" ::"l"(ptr));
+}
+// Issues L2 prefetches for `bytes` bytes at `ptr`, one 128-byte line per lane.
+__device__ __forceinline__ void prefetch_range(const void* ptr, int bytes, int lane) {
+  const char* c = static_cast<const char*>(ptr);
+  for (int off = lane * 128; off < bytes; off += 32 * 128) prefetch_l2(c + off);
 }
 __device__ __forceinline__ void named_barrier_consumers() {
   asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
@@ -248,14 +297,17 @@ __device__ __forceinline__ Split split_layout(int lo, int hi, int B, int S, int 
 // The kernel.  grid = (splits, NKV, T); block = 160 threads (4 consumer warps + producer).
 // ------------------------------------------------------------------------------------
 template <int HD, int NT, int NS>
-__global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant__ KParams p) {
+__global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
+    decode_kernel(const __grid_constant__ KParams p) {
   using L = Smem<HD, NS>;
   constexpr int KT = HD / 16;          // MMA k-steps over head_dim / m-tiles of O^T
   constexpr int ROWS = NT * 8;         // query rows per CTA
   constexpr int PER_LANE = HD / 32;    // elements per lane in row-wise prologue math
-  constexpr int ROWB = L::kRowBytes;
+  constexpr int TILE = L::kTileBytes;
 
-  extern __shared__ __align__(128) uint8_t smem[];
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  // Swizzled boxes need 1024-byte alignment; the allocation has the slack for it.
+  uint8_t* smem = smem_raw + ((1024 - (smem_u32(smem_raw) & 1023)) & 1023);
   // Per-token info, indexed by token for shared-cache calls and by 0 otherwise.
   __shared__ int s_len[kMaxSub], s_phys[kMaxSub];
   __shared__ long long s_coff[kMaxSub], s_toff[kMaxSub];
@@ -275,6 +327,28 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
   // ---- token info: the group's tokens and the tokens whose new k/v this CTA may have to
   //      substitute (shared-cache: every token of the call; otherwise this token alone).
   const int ninfo = p.shared ? p.T : 1;
+  if (warp == kConsumerWarps) {
+    // This token's per-head inputs are needed once the sequence length is known; start
+    // pulling them into L2 now, while that first load is in flight.
+    const int hq = kvh * G;
+    const int64_t qrow = int64_t(tok) * p.q_stride;
+    if (p.raw) {
+      const float* qf = static_cast<const float*>(p.q) + qrow;
+      prefetch_range(qf + hq * HD, G * HD * 4, lane);
+      prefetch_range(qf + (p.NH + kvh) * HD, HD * 4, lane);
+      prefetch_range(p.v + int64_t(tok) * p.NKV * HD + kvh * HD, HD * 4, lane);
+      prefetch_range(static_cast<const char*>(p.sqk) + (p.sqk_dtype == DORY_DTYPE_F32 ? 4 : 2) *
+                         int64_t(hq) * HD,
+                     G * HD * (p.sqk_dtype == DORY_DTYPE_F32 ? 4 : 2), lane);
+    } else {
+      prefetch_range(static_cast<const __nv_bfloat16*>(p.q) + qrow + hq * HD, G * HD * 2, lane);
+    }
+    prefetch_range(p.gate + int64_t(tok) * Q + hq * HD, G * HD * 4, lane);
+    if (p.tm_ok && lane == 0) {
+      prefetch_tensormap(&p.tmk);
+      prefetch_tensormap(&p.tmv);
+    }
+  }
   if (tid == 0) s_grouped = 1;
   if (tid < ninfo) {
     const int t = p.shared ? tid : tok;
@@ -349,37 +423,50 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
   __nv_bfloat16* q2 = reinterpret_cast<__nv_bfloat16*>(smem + L::kQ);
   __nv_bfloat16* subkv = reinterpret_cast<__nv_bfloat16*>(smem + L::kSub);
 
+  const bool offset_ok = (coff & 7) == 0;
+  // Tensor copies address the cache by block index, so an offset must be whole blocks.
+  const bool use_tma = p.tm_ok && offset_ok && coff % p.sb == 0 && coff >= 0 &&
+                       coff / p.sb + p.ncache_blocks <= p.tm_blocks;
+  const long long coff_blocks = use_tma ? coff / p.sb : 0;
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
-      mbar_init(full_bar(s), 1);
-      mbar_init(empty_bar(s), 1);
+      // tensor path: the producer's arrive.expect_tx; copy path: 32 lanes' completions + 1
+      mbar_init(full_bar(s), use_tma ? 1 : 33);
+      mbar_init(empty_bar(s), 1);  // the consumer warp that read the stage
     }
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    if ((coff & 7) != 0) record_error(p.err, DORY_DEVERR_OFFSET_ALIGN);
+    if (!offset_ok) record_error(p.err, DORY_DEVERR_OFFSET_ALIGN);
   }
   __syncthreads();
-  const bool offset_ok = (coff & 7) == 0;
 
   if (warp == kConsumerWarps) {
     // =============================== producer warp ===============================
+    // Tensor path (the usual one): lane 0 publishes the stage's block id, arms full[stage]
+    // with the stage's byte count and issues 2 * HD / 64 box copies (K, then V) through
+    // the tensor maps; 16-row boxes at (row 0 of the chunk, KV head, block).  Rows of the
+    // box outside the attended range are read too and zeroed by the consumer.
+    // Copy path (cache offsets that are not whole blocks): every lane copies 16-byte
+    // pieces with cp.async into the same swizzled layout, zero-filling rows outside
+    // [lo, hi); completion reaches full[stage] through one cp.async.mbarrier.arrive per
+    // lane, plus lane 0's arrive after publishing the block id.
     const __nv_bfloat16* kbase = p.kc + coff + int64_t(kvh) * p.sh;
     const __nv_bfloat16* vbase = p.vc + coff + int64_t(kvh) * p.sh;
     const int32_t* table = p.table + toff;
-    const int row = lane & 15;
-    const bool is_v = lane >= 16;
+    constexpr int VEC = HD / 8;                    // 16-byte pieces per row
+    constexpr int PER_LANE = 2 * kChunk * VEC / 32;
     // Block-table window of 32 entries, prefetched one window ahead.
     const int b_first = cb / CPB;
     const int b_last = (ce - 1) / CPB;
     int wbase = b_first;
     int win_cur = (b_first + lane <= b_last) ? table[b_first + lane] : -1;
     int win_nxt = (b_first + 32 + lane <= b_last) ? table[b_first + 32 + lane] : -1;
-    bool ok_all = true;
+    const uint64_t policy = l2_evict_first_policy();
+    int issued = 0;
     for (int i = 0; i < nchunks; ++i) {
       const int stage = i % NS;
       const uint32_t parity = ((i / NS) & 1) ^ 1;
       if (!mbar_wait(empty_bar(stage), parity)) {
         if (lane == 0) record_error(p.err, DORY_DEVERR_WAIT_TIMEOUT);
-        ok_all = false;
         break;
       }
       const int c = cb + i;
@@ -390,27 +477,59 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
         win_nxt = (wbase + 32 + lane <= b_last) ? table[wbase + 32 + lane] : -1;
       }
       const int phys = __shfl_sync(0xffffffffu, win_cur, blk - wbase);
-      bool phys_ok = phys >= 0 && (p.ncache_blocks <= 0 || phys < p.ncache_blocks) && offset_ok;
+      const bool phys_ok =
+          phys >= 0 && (p.ncache_blocks <= 0 || phys < p.ncache_blocks) && offset_ok;
       if (!phys_ok && lane == 0 && offset_ok) record_error(p.err, DORY_DEVERR_BLOCK_OOB);
-      const int in_block = (c % CPB) * kChunk + row;
-      const int pos = c * kChunk + row;
-      const bool valid = phys_ok && pos >= lo && pos < hi;
-      const uint32_t mask = __ballot_sync(0xffffffffu, valid) & 0xffffu;
-      const uint32_t bytes = __popc(mask) * 2u * HD * 2u;
-      if (lane == 0) {
-        meta[stage] = make_int4(phys, int(mask), c, 0);
-        mbar_arrive_expect_tx(full_bar(stage), bytes);
+      const uint32_t kt = smem_u32(smem + L::kStages + stage * L::kStageBytes);
+      const uint32_t vt = kt + TILE;
+      if (use_tma) {
+        if (lane == 0) {
+          meta[stage] = make_int4(phys_ok ? phys : -1, 0, c, 0);
+          if (phys_ok) {
+            mbar_arrive_expect_tx(full_bar(stage), L::kStageBytes);
+            const int row0 = (c % CPB) * kChunk;
+            const int c1 = p.tm_rowdim == 1 ? row0 : kvh;
+            const int c2 = p.tm_rowdim == 1 ? kvh : row0;
+            const int c3 = int(coff_blocks + phys);
+#pragma unroll
+            for (int b = 0; b < HD / 64; ++b) {
+              tma_load_4d(kt + b * kBoxBytes, &p.tmk, b * 64, c1, c2, c3, full_bar(stage), policy);
+              tma_load_4d(vt + b * kBoxBytes, &p.tmv, b * 64, c1, c2, c3, full_bar(stage), policy);
+            }
+          } else {
+            mbar_arrive(full_bar(stage));  // nothing to load; the consumer zeroes the tile
+          }
+        }
+      } else {
+        const int64_t block_off = int64_t(phys_ok ? phys : 0) * p.sb +
+                                  int64_t((c % CPB) * kChunk) * p.so;
+#pragma unroll
+        for (int k = 0; k < PER_LANE; ++k) {
+          const int j = k * 32 + lane;
+          const bool is_v = j >= kChunk * VEC;
+          const int jj = is_v ? j - kChunk * VEC : j;
+          const int r = jj / VEC, w = jj % VEC;
+          const int pos = c * kChunk + r;
+          const bool valid = phys_ok && pos >= lo && pos < hi;
+          const __nv_bfloat16* src =
+              valid ? (is_v ? vbase : kbase) + block_off + int64_t(r) * p.so + w * 8 : p.kc;
+          cp_async_16((is_v ? vt : kt) + tile_off(r, w * 8), src, valid ? 16u : 0u, policy);
+        }
+        cp_async_arrive_noinc(full_bar(stage));
+        if (lane == 0) {
+          meta[stage] = make_int4(phys_ok ? phys : -1, 0, c, 0);
+          mbar_arrive(full_bar(stage));
+        }
       }
-      __syncwarp();
-      if (valid) {
-        const int64_t off = int64_t(phys) * p.sb + int64_t(in_block) * p.so;
-        const uint32_t dst =
-            smem_u32(smem + L::kStages + stage * L::kStageBytes + (is_v ? kChunk * ROWB : 0) +
-                     row * ROWB);
-        bulk_g2s(dst, (is_v ? vbase : kbase) + off, HD * 2, full_bar(stage));
+      ++issued;
+    }
+    if (!use_tma) {
+      // Stay until this warp's copies have landed (bounded), then leave.
+      for (int s = 0; s < NS && s < issued; ++s) {
+        const int last = s + ((issued - 1 - s) / NS) * NS;
+        mbar_wait(full_bar(s), (last / NS) & 1);
       }
     }
-    (void)ok_all;
     return;
   }
 
@@ -553,20 +672,24 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
     }
     const int4 mt = meta[stage];
     const int phys = mt.x;
-    const uint32_t mask = uint32_t(mt.y);
     const int c = mt.z;
     uint8_t* kst = smem + L::kStages + stage * L::kStageBytes;
-    uint8_t* vst = kst + kChunk * ROWB;
+    uint8_t* vst = kst + TILE;
     bool touched = false;
-    // Rows not copied (outside [lo, hi) or a bad block) hold stale bytes: zero V there so
-    // that p = 0 never multiplies a non-finite value.
-    if (mask != 0xffffu) {
-      constexpr int kVec = HD / 8;
-      for (int idx = lane; idx < kChunk * kVec; idx += 32) {
-        const int r = idx / kVec, w = idx % kVec;
-        if (!((mask >> r) & 1u)) reinterpret_cast<uint4*>(vst + r * ROWB)[w] = make_uint4(0, 0, 0, 0);
+    constexpr int kVec = HD / 8;  // 16-byte pieces per row
+    // Tensor copies bring whole 16-row boxes: zero the V rows outside the attended range
+    // (or the whole tile of a bad block) so that p = 0 never meets a non-finite value.
+    // The copy path zero-filled them in flight.
+    if (use_tma) {
+      const int r_lo = max(lo - c * kChunk, 0), r_hi = min(hi - c * kChunk, kChunk);
+      if (phys < 0 || r_lo > 0 || r_hi < kChunk) {
+        for (int idx = lane; idx < kChunk * kVec; idx += 32) {
+          const int r = idx / kVec, w = idx % kVec;
+          if (phys < 0 || r < r_lo || r >= r_hi)
+            *reinterpret_cast<uint4*>(vst + tile_off(r, w * 8)) = make_uint4(0, 0, 0, 0);
+        }
+        touched = true;
       }
-      touched = true;
     }
     // New entries of this call replace the rows that alias their slots.
     if (p.raw) {
@@ -575,12 +698,11 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
         if (s_len[s] <= 0 || s_phys[s] != phys || s_coff[s] != coff) continue;
         const int r = ((s_len[s] - 1) % B) - in_block0;
         if (r < 0 || r >= kChunk) continue;
-        constexpr int kVec = HD / 8;
         for (int idx = lane; idx < 2 * kVec; idx += 32) {
           const bool is_v = idx >= kVec;
           const int w = is_v ? idx - kVec : idx;
           const uint4 val = reinterpret_cast<const uint4*>(subkv + (s * 2 + (is_v ? 1 : 0)) * HD)[w];
-          reinterpret_cast<uint4*>((is_v ? vst : kst) + r * ROWB)[w] = val;
+          *reinterpret_cast<uint4*>((is_v ? vst : kst) + tile_off(r, w * 8)) = val;
         }
         touched = true;
       }
@@ -592,11 +714,12 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
 #pragma unroll
     for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
     {
-      const uint32_t kaddr = smem_u32(kst) + (lane & 15) * ROWB + (lane >> 4) * 16;
+      const uint32_t kbase_s = smem_u32(kst);
+      const int kr = lane & 15, kd = (lane >> 4) * 8;
 #pragma unroll
       for (int kk = 0; kk < KT; ++kk) {
         uint32_t a0, a1, a2, a3;
-        ldsm_x4(kaddr + kk * 32, a0, a1, a2, a3);
+        ldsm_x4(kbase_s + tile_off(kr, kk * 16 + kd), a0, a1, a2, a3);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) mma_bf16(sc[nt], a0, a1, a2, a3, qb[nt][kk][0], qb[nt][kk][1]);
       }
@@ -640,17 +763,17 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
     }
     // O^T += V^T P^T : [16 dims x 8 rows] per m-tile and n-tile.
     {
-      const uint32_t vaddr =
-          smem_u32(vst) + ((lane & 7) + ((lane >> 4) << 3)) * ROWB + ((lane >> 3) & 1) * 16;
+      const uint32_t vbase_s = smem_u32(vst);
+      const int vr = (lane & 7) + ((lane >> 4) << 3), vd = ((lane >> 3) & 1) * 8;
 #pragma unroll
       for (int kk = 0; kk < KT; ++kk) {
         uint32_t a0, a1, a2, a3;
-        ldsm_x4_t(vaddr + kk * 32, a0, a1, a2, a3);
+        ldsm_x4_t(vbase_s + tile_off(vr, kk * 16 + vd), a0, a1, a2, a3);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) mma_bf16(o[nt][kk], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
       }
     }
-    if (touched) fence_proxy_async_smem();
+    if (touched) fence_proxy_async_smem();  // before tensor copies refill the stage
     __syncwarp();
     if (lane == 0) mbar_arrive(empty_bar(stage));
   }
@@ -756,34 +879,60 @@ __global__ void __launch_bounds__(kThreads) decode_kernel(const __grid_constant_
   named_barrier_consumers();
   if (!s_last) return;
   __threadfence();
-  for (int it = tid; it < items; it += kConsumerWarps * 32) {
-    const int r = it / IPR, k8 = it % IPR;
-    const int t = gstart + r / G;
-    const int head = kvh * G + r % G;
-    float M = -INFINITY, Lsum = 0.0f, acc[8];
+  // Three phases, so that no thread waits on one L2 round trip per split:
+  //  (a) every split's (max, sum) of every row into shared memory, all loads in flight;
+  //  (b) per row, the merged max, each split's weight and 1 / total, one warp per row;
+  //  (c) per (row, 4 dims), the weighted sum over splits with 8 loads in flight.
+  const int active = sp.active;
+  float2* s_stat = reinterpret_cast<float2*>(smem + L::kStages);      // [active][ROWS]
+  float* s_wt = reinterpret_cast<float*>(s_stat + active * ROWS);      // [active][ROWS]
+  float* s_inv = s_wt + active * ROWS;                                  // [ROWS]
+  for (int i = tid; i < active * nrows; i += kConsumerWarps * 32) {
+    const int sidx = i / nrows, r = i % nrows;
+    const int t = gstart + r / G, head = kvh * G + r % G;
+    s_stat[sidx * ROWS + r] = __ldcg(p.pml + (int64_t(t) * S + sidx) * p.NH + head);
+  }
+  named_barrier_consumers();
+  for (int r = warp; r < nrows; r += kConsumerWarps) {
+    float M = -INFINITY;
+    for (int sidx = lane; sidx < active; sidx += 32) M = fmaxf(M, s_stat[sidx * ROWS + r].x);
 #pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
-    for (int s = 0; s < sp.active; ++s) {
-      const int64_t pi = (int64_t(t) * S + s) * p.NH + head;
-      const float2 ml = __ldcg(p.pml + pi);
-      const float4* src = reinterpret_cast<const float4*>(p.po + pi * HD + k8 * 8);
-      const float4 a = __ldcg(src), b = __ldcg(src + 1);
-      const float Mn = fmaxf(M, ml.x);
-      const float Mu = (Mn == -INFINITY) ? 0.0f : Mn;
-      const float wa = fast_exp2(M - Mu), wb = fast_exp2(ml.x - Mu);
-      Lsum = Lsum * wa + ml.y * wb;
-      acc[0] = acc[0] * wa + a.x * wb; acc[1] = acc[1] * wa + a.y * wb;
-      acc[2] = acc[2] * wa + a.z * wb; acc[3] = acc[3] * wa + a.w * wb;
-      acc[4] = acc[4] * wa + b.x * wb; acc[5] = acc[5] * wa + b.y * wb;
-      acc[6] = acc[6] * wa + b.z * wb; acc[7] = acc[7] * wa + b.w * wb;
-      M = Mn;
+    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
+    const float Mu = (M == -INFINITY) ? 0.0f : M;
+    float Lsum = 0.0f;
+    for (int sidx = lane; sidx < active; sidx += 32) {
+      const float2 st = s_stat[sidx * ROWS + r];
+      const float w = fast_exp2(st.x - Mu);
+      s_wt[sidx * ROWS + r] = w;
+      Lsum += w * st.y;
     }
-    const float inv = 1.0f / (Lsum > 0.0f ? Lsum : 1.0f);
-    const int e0 = head * HD + k8 * 8;
-    const float* gt = p.gate + int64_t(t) * Q + e0;
-    float* out = p.out + int64_t(t) * Q + e0 / 8;
 #pragma unroll
-    for (int e = 0; e < 8; ++e) out[e * (Q / 8)] = acc[e] * inv * gt[e];
+    for (int off = 16; off > 0; off >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, off);
+    if (lane == 0) s_inv[r] = 1.0f / (Lsum > 0.0f ? Lsum : 1.0f);
+  }
+  named_barrier_consumers();
+  constexpr int UPR = HD / 4;  // float4 units per row
+  for (int u = tid; u < nrows * UPR; u += kConsumerWarps * 32) {
+    const int r = u / UPR, d4 = u % UPR;
+    const int t = gstart + r / G, head = kvh * G + r % G;
+    const float4* src = reinterpret_cast<const float4*>(p.po) +
+                        ((int64_t(t) * S) * p.NH + head) * UPR + d4;
+    const int64_t sstride = int64_t(p.NH) * UPR;  // float4s between consecutive splits
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll 8
+    for (int sidx = 0; sidx < active; ++sidx) {
+      const float w = s_wt[sidx * ROWS + r];
+      const float4 o = __ldcg(src + sidx * sstride);
+      acc.x += w * o.x; acc.y += w * o.y; acc.z += w * o.z; acc.w += w * o.w;
+    }
+    const float inv = s_inv[r];
+    const int e0 = head * HD + d4 * 4;  // 4 consecutive elements: same e / 8, e % 8 = j0..j0+3
+    const float4 gt = *reinterpret_cast<const float4*>(p.gate + int64_t(t) * Q + e0);
+    float* out = p.out + int64_t(t) * Q + (e0 % 8) * (Q / 8) + e0 / 8;
+    out[0] = acc.x * inv * gt.x;
+    out[Q / 8] = acc.y * inv * gt.y;
+    out[2 * (Q / 8)] = acc.z * inv * gt.z;
+    out[3 * (Q / 8)] = acc.w * inv * gt.w;
   }
 }
 
@@ -820,16 +969,121 @@ int32_t launch(const KParams& kp, dim3 grid, int smem_bytes, cudaStream_t stream
   return DORY_OK;
 }
 
-// Pipeline depth per head_dim: ~70 KB of ring per CTA.
-template <int HD> struct Depth { static constexpr int value = HD >= 256 ? 4 : 8; };
+// Ring stages per instantiation: 32 KB of ring for one query tile (so ~5 CTAs fit an SM
+// and their latency phases overlap), 64 KB for two tiles (whose merge buffer needs it).
+// A multiple of the four consumer warps, so every stage keeps one consumer.
+template <int HD, int NT>
+struct Depth {
+  static constexpr int value = HD == 64 ? 8 : (HD == 128 ? (NT == 1 ? 4 : 8) : 4);
+};
+
+// Largest split count whose merge tables ((max, sum) and weight per split and row) fit in
+// the drained ring of one CTA.
+template <int HD, int NS>
+constexpr int max_splits(int rows) {
+  return (NS * Smem<HD, NS>::kStageBytes - rows * 4) / (rows * 12);
+}
+
+template <int HD, int NT>
+int32_t dispatch(const KParams& kp, dim3 grid, cudaStream_t stream) {
+  constexpr int NS = Depth<HD, NT>::value;
+  static_assert(kConsumerWarps * NT * 8 * (HD + 4) * 4 <= NS * Smem<HD, NS>::kStageBytes,
+                "the warps' merge buffer must fit in the ring");
+  if (kp.S > max_splits<HD, NS>(NT * 8))
+    return fail(DORY_ERR_UNSUPPORTED, "splits %d > %d for head_dim %d", kp.S,
+                max_splits<HD, NS>(NT * 8), HD);
+  return launch<HD, NT, NS>(kp, grid, Smem<HD, NS>::bytes(kp.nsub), stream);
+}
 
 template <int HD>
 int32_t dispatch_nt(const KParams& kp, int nt, dim3 grid, cudaStream_t stream) {
-  constexpr int NS = Depth<HD>::value;
-  const int smem = Smem<HD, NS>::bytes(kp.nsub);
-  if (nt == 1) return launch<HD, 1, NS>(kp, grid, smem, stream);
-  if constexpr (HD <= 128) return launch<HD, 2, NS>(kp, grid, smem, stream);
+  if (nt == 1) return dispatch<HD, 1>(kp, grid, stream);
+  if constexpr (HD <= 128) return dispatch<HD, 2>(kp, grid, stream);
   return fail(DORY_ERR_UNSUPPORTED, "head_dim %d supports at most 8 query rows per tile", HD);
+}
+
+// ---- tensor maps of the cache views ----
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  });
+  return fn;
+}
+
+struct MapKey {
+  const void* base;
+  int64_t blocks, sb, so, sh;
+  int B, NKV, HD;
+  bool operator==(const MapKey& o) const {
+    return base == o.base && blocks == o.blocks && sb == o.sb && so == o.so && sh == o.sh &&
+           B == o.B && NKV == o.NKV && HD == o.HD;
+  }
+};
+struct MapEntry {
+  MapKey key;
+  CUtensorMap map;
+  int rowdim;
+  bool ok;
+};
+
+// 4-D map of one cache view: (dims, rows | heads, heads | rows, blocks), the middle two in
+// order of stride; box 64 dims x 16 rows x 1 head x 1 block, 128-byte swizzle.  Encoded
+// maps are cached per thread (a call sequence revisits the same few caches).
+bool cache_tensor_map(const MapKey& k, CUtensorMap* out, int* rowdim) {
+  constexpr int kSlots = 64;
+  thread_local MapEntry cache[kSlots];
+  thread_local int used = 0, next = 0;
+  for (int i = 0; i < used; ++i)
+    if (cache[i].key == k) {
+      *out = cache[i].map;
+      *rowdim = cache[i].rowdim;
+      return cache[i].ok;
+    }
+  MapEntry e;
+  e.key = k;
+  e.ok = false;
+  e.rowdim = 1;
+  memset(&e.map, 0, sizeof(e.map));
+  auto encode = tensor_map_encoder();
+  if (encode && k.blocks > 0 && k.blocks <= 0x7fffffff) {
+    cuuint64_t dims[4], strides[3];
+    cuuint32_t box[4], estr[4] = {1, 1, 1, 1};
+    dims[0] = cuuint64_t(k.HD);
+    box[0] = 64;
+    if (k.so <= k.sh) {
+      dims[1] = cuuint64_t(k.B); strides[0] = cuuint64_t(k.so) * 2; box[1] = kChunk;
+      dims[2] = cuuint64_t(k.NKV); strides[1] = cuuint64_t(k.sh) * 2; box[2] = 1;
+      e.rowdim = 1;
+    } else {
+      dims[1] = cuuint64_t(k.NKV); strides[0] = cuuint64_t(k.sh) * 2; box[1] = 1;
+      dims[2] = cuuint64_t(k.B); strides[1] = cuuint64_t(k.so) * 2; box[2] = kChunk;
+      e.rowdim = 2;
+    }
+    dims[3] = cuuint64_t(k.blocks);
+    strides[2] = cuuint64_t(k.sb) * 2;
+    box[3] = 1;
+    CUresult r = encode(&e.map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(k.base),
+                        dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    e.ok = r == CUDA_SUCCESS;
+  }
+  if (used < kSlots) {
+    cache[used++] = e;
+  } else {
+    cache[next] = e;
+    next = (next + 1) % kSlots;
+  }
+  *out = e.map;
+  *rowdim = e.rowdim;
+  return e.ok;
 }
 
 }  // namespace
@@ -900,6 +1154,8 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
   if (shared && a.num_tokens > kMaxSub)
     return fail(DORY_ERR_UNSUPPORTED, "shared-cache calls take at most %d tokens", kMaxSub);
   if (a.sqk_dtype < 0 || a.sqk_dtype > 2) return fail(DORY_ERR_INVALID_ARGUMENT, "sqk dtype");
+  if (reinterpret_cast<uintptr_t>(a.gate) & 15)
+    return fail(DORY_ERR_ALIGNMENT, "gate needs a 16-byte aligned base");
   if ((reinterpret_cast<uintptr_t>(a.key_cache) & 15) ||
       (reinterpret_cast<uintptr_t>(a.value_cache) & 15) || (a.stride_block & 7) ||
       (a.stride_offset & 7) || (a.stride_head & 7))
@@ -961,6 +1217,23 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
   kp.shared = shared;
   kp.q_stride = (raw ? a.num_heads + a.num_kv_heads : a.num_heads) * HD;
   kp.nsub = raw ? (shared ? a.num_tokens : 1) : 0;
+  // Tensor maps of the K and V views.  Multi-token calls may shift the cache by whole
+  // blocks (per-loop caches at cache_offsets[t]); the block extent then allows up to 64
+  // caches' worth of blocks past the view.  Other offsets take the copy path.
+  {
+    const int64_t nb = a.num_cache_blocks > 0 ? a.num_cache_blocks : 0;
+    const int64_t extent = multi ? (nb * 64 < 0x7fffffff ? nb * 64 : 0x7fffffff) : nb;
+    MapKey kk{a.key_cache, extent, a.stride_block, a.stride_offset, a.stride_head,
+              a.block_size, a.num_kv_heads, HD};
+    MapKey vk = kk;
+    vk.base = a.value_cache;
+    int rk = 1, rv = 1;
+    const bool okk = nb > 0 && cache_tensor_map(kk, &kp.tmk, &rk);
+    const bool okv = okk && cache_tensor_map(vk, &kp.tmv, &rv);
+    kp.tm_ok = okk && okv && rk == rv;
+    kp.tm_rowdim = rk;
+    kp.tm_blocks = extent;
+  }
 
   dim3 grid(a.splits, a.num_kv_heads, a.num_tokens);
   cudaStream_t s = (cudaStream_t)stream;
