@@ -555,8 +555,8 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", default="config5")
-    ap.add_argument("--splits", type=int, default=16)
-    ap.add_argument("--min-blocks-per-split", type=int, default=8)
+    ap.add_argument("--splits", type=int, default=2)
+    ap.add_argument("--min-blocks-per-split", type=int, default=64)
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     args = ap.parse_args()

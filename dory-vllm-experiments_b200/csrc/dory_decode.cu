@@ -60,8 +60,8 @@ constexpr float kLog2e = 1.4426950408889634f;
 // Kernel parameters (device-side copy of DoryDecodeParams plus derived values).
 // ------------------------------------------------------------------------------------
 struct KParams {
-  CUtensorMap tmk;  // K / V cache views as 4-D tensors (dims sorted by stride), 16x64 boxes,
-  CUtensorMap tmv;  // 128-byte swizzle; valid when tm_ok
+  CUtensorMap tmk;  // cache views as 5-D tensors (64 dims, rows, 64-dim quarters of a row,
+  CUtensorMap tmv;  // KV head, block), one box = a chunk's K (and V) tile, 128-byte swizzle
   const void* q;
   const float* v;
   const void* sqk;
@@ -84,8 +84,7 @@ struct KParams {
   int raw, multi, shared;
   int q_stride;  // elements of q per token
   int nsub;      // new tokens whose k/v this call substitutes (shared: T, raw: 1, else 0)
-  int tm_ok;     // tensor maps usable
-  int tm_rowdim; // tensor dim (1 or 2) that indexes the row within a block (the other: head)
+  int tm_mode;   // 0: no tensor maps; 1: tmk covers K and V (V right after K); 2: tmk, tmv
   int64_t tm_blocks;  // extent of the block dimension of the tensor maps
 };
 
@@ -167,13 +166,13 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
   return policy;
 }// One box of a tensor map into shared memory, completing on `bar` (no multicast).
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
-                                            int c2, int c3, uint32_t bar, uint64_t policy) {
+__device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
+                                            int c2, int c3, int c4, uint32_t bar, uint64_t policy) {
   asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5}], [%6], %7;" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(bar),
-      "l"(policy)
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5, %6}], [%7], %8;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4),
+      "r"(bar), "l"(policy)
       : "memory");
 }
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
@@ -294,6 +293,93 @@ __device__ __forceinline__ Split split_layout(int lo, int hi, int B, int S, int 
 }
 
 // ------------------------------------------------------------------------------------
+// Slow path of a ring stage (taken by few chunks):
+//  * tensor path: zero the V rows outside [lo, hi) (all of them for a bad block);
+//  * put the new k/v of this call's tokens into the rows that hold their slots (by
+//    position for tokens on this CTA's table, by physical block otherwise), as the
+//    reference uses the new token from registers (dory_decode_attention.py:141-145) and
+//    its shared-cache mode caches every token first (:294-301);
+//  * append: the chunk holding a group token's position writes its k/v to the cache
+//    (slot_mapping[0] in single-token calls, the table's slot in multi-token calls).
+// Returns whether the stage was written (the caller then fences before tensor copies).
+// ------------------------------------------------------------------------------------
+// CTA constants the slow path needs, kept in shared memory so that the hot loop does not
+// hold them in registers.
+struct CtaInfo {
+  long long coff, toff;
+  int lo, hi, kvh, nsub, ibase, gcount, offset_ok;
+};
+
+template <int HD>
+__device__ __forceinline__ bool fixup_stage(const KParams& p, uint8_t* kst, uint8_t* vst, int c,
+                                         int phys, bool zero_rows, int lane,
+                                         const CtaInfo& ci, const int* s_len, const int* s_phys,
+                                         const long long* s_coff, const long long* s_toff,
+                                         const __nv_bfloat16* subkv) {
+  const long long coff = ci.coff, toff = ci.toff;
+  const int lo = ci.lo, hi = ci.hi, kvh = ci.kvh, nsub = ci.nsub, ibase = ci.ibase;
+  const int gcount = ci.gcount;
+  const bool offset_ok = ci.offset_ok;
+  constexpr int kVec = HD / 8;  // 16-byte pieces per row
+  const int B = p.B;
+  const int CPB = B / kChunk;
+  bool touched = false;
+  if (zero_rows) {
+    const int r_lo = max(lo - c * kChunk, 0), r_hi = min(hi - c * kChunk, kChunk);
+    for (int idx = lane; idx < kChunk * kVec; idx += 32) {
+      const int r = idx / kVec, w = idx % kVec;
+      if (phys < 0 || r < r_lo || r >= r_hi)
+        *reinterpret_cast<uint4*>(vst + tile_off(r, w * 8)) = make_uint4(0, 0, 0, 0);
+    }
+    touched = true;
+  }
+  if (!p.raw) return touched;
+  for (int s = 0; s < nsub; ++s) {
+    const int len = s_len[s];
+    if (len <= 0) continue;
+    const int pos = len - 1;
+    const bool same = s_coff[s] == coff && s_toff[s] == toff;
+    int r = -1;
+    if (same) {
+      if (pos / kChunk == c) r = pos % kChunk;
+    } else if (phys >= 0 && s_phys[s] == phys && s_coff[s] == coff) {
+      const int rr = pos % B - (c % CPB) * kChunk;
+      if (rr >= 0 && rr < kChunk) r = rr;
+    }
+    if (r < 0) continue;
+    for (int idx = lane; idx < 2 * kVec; idx += 32) {
+      const bool is_v = idx >= kVec;
+      const int w = is_v ? idx - kVec : idx;
+      const uint4 val = reinterpret_cast<const uint4*>(subkv + (s * 2 + (is_v ? 1 : 0)) * HD)[w];
+      *reinterpret_cast<uint4*>((is_v ? vst : kst) + tile_off(r, w * 8)) = val;
+    }
+    touched = true;
+    if (!same || s < ibase || s >= ibase + gcount) continue;  // another CTA appends it
+    long long slot;
+    if (p.multi) {
+      if (phys < 0) continue;  // its block id was out of range (already recorded)
+      slot = (long long)phys * B + pos % B;
+    } else {
+      slot = p.slot_mapping[0];
+      if (slot < 0) continue;  // padding token: vLLM does not cache it
+    }
+    const long long blk = slot / B;
+    if (blk < 0 || (p.ncache_blocks > 0 && blk >= p.ncache_blocks) || !offset_ok) {
+      if (lane == 0) record_error(p.err, DORY_DEVERR_SLOT_OOB);
+      continue;
+    }
+    const long long base = s_coff[s] + blk * p.sb + (slot % B) * p.so + (long long)kvh * p.sh;
+    for (int idx = lane; idx < 2 * kVec; idx += 32) {
+      const bool is_v = idx >= kVec;
+      const int w = is_v ? idx - kVec : idx;
+      const uint4 val = reinterpret_cast<const uint4*>(subkv + (s * 2 + (is_v ? 1 : 0)) * HD)[w];
+      reinterpret_cast<uint4*>((is_v ? p.vc : p.kc) + base)[w] = val;
+    }
+  }
+  return touched;
+}
+
+// ------------------------------------------------------------------------------------
 // The kernel.  grid = (splits, NKV, T); block = 160 threads (4 consumer warps + producer).
 // ------------------------------------------------------------------------------------
 template <int HD, int NT, int NS>
@@ -312,6 +398,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
   __shared__ int s_len[kMaxSub], s_phys[kMaxSub];
   __shared__ long long s_coff[kMaxSub], s_toff[kMaxSub];
   __shared__ int s_grouped, s_last;
+  __shared__ CtaInfo s_ci;
   __shared__ float s_wm[kConsumerWarps][ROWS], s_wl[kConsumerWarps][ROWS];
 
   const int split = blockIdx.x;
@@ -344,9 +431,9 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
       prefetch_range(static_cast<const __nv_bfloat16*>(p.q) + qrow + hq * HD, G * HD * 2, lane);
     }
     prefetch_range(p.gate + int64_t(tok) * Q + hq * HD, G * HD * 4, lane);
-    if (p.tm_ok && lane == 0) {
+    if (p.tm_mode && lane == 0) {
       prefetch_tensormap(&p.tmk);
-      prefetch_tensormap(&p.tmv);
+      if (p.tm_mode == 2) prefetch_tensormap(&p.tmv);
     }
   }
   if (tid == 0) s_grouped = 1;
@@ -425,7 +512,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
 
   const bool offset_ok = (coff & 7) == 0;
   // Tensor copies address the cache by block index, so an offset must be whole blocks.
-  const bool use_tma = p.tm_ok && offset_ok && coff % p.sb == 0 && coff >= 0 &&
+  const bool use_tma = p.tm_mode != 0 && offset_ok && coff % p.sb == 0 && coff >= 0 &&
                        coff / p.sb + p.ncache_blocks <= p.tm_blocks;
   const long long coff_blocks = use_tma ? coff / p.sb : 0;
   if (tid == 0) {
@@ -442,9 +529,10 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
   if (warp == kConsumerWarps) {
     // =============================== producer warp ===============================
     // Tensor path (the usual one): lane 0 publishes the stage's block id, arms full[stage]
-    // with the stage's byte count and issues 2 * HD / 64 box copies (K, then V) through
-    // the tensor maps; 16-row boxes at (row 0 of the chunk, KV head, block).  Rows of the
-    // box outside the attended range are read too and zeroed by the consumer.
+    // with the stage's byte count and issues one box copy of the chunk's K and V tiles
+    // (two, K then V, when V does not directly follow K in memory): 16 rows from row 0 of
+    // the chunk, all 64-dim quarters of each row, at (KV head, block).  Rows of the box
+    // outside the attended range are read too and zeroed by the consumer.
     // Copy path (cache offsets that are not whole blocks): every lane copies 16-byte
     // pieces with cp.async into the same swizzled layout, zero-filling rows outside
     // [lo, hi); completion reaches full[stage] through one cp.async.mbarrier.arrive per
@@ -488,14 +576,9 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
           if (phys_ok) {
             mbar_arrive_expect_tx(full_bar(stage), L::kStageBytes);
             const int row0 = (c % CPB) * kChunk;
-            const int c1 = p.tm_rowdim == 1 ? row0 : kvh;
-            const int c2 = p.tm_rowdim == 1 ? kvh : row0;
-            const int c3 = int(coff_blocks + phys);
-#pragma unroll
-            for (int b = 0; b < HD / 64; ++b) {
-              tma_load_4d(kt + b * kBoxBytes, &p.tmk, b * 64, c1, c2, c3, full_bar(stage), policy);
-              tma_load_4d(vt + b * kBoxBytes, &p.tmv, b * 64, c1, c2, c3, full_bar(stage), policy);
-            }
+            const int blkc = int(coff_blocks + phys);
+            tma_load_5d(kt, &p.tmk, 0, row0, 0, kvh, blkc, full_bar(stage), policy);
+            if (p.tm_mode == 2) tma_load_5d(vt, &p.tmv, 0, row0, 0, kvh, blkc, full_bar(stage), policy);
           } else {
             mbar_arrive(full_bar(stage));  // nothing to load; the consumer zeroes the tile
           }
@@ -534,10 +617,40 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
   }
 
   // =============================== consumer warps ===============================
-  // (0) physical block of each new token's slot (off the producer's dependent-load chain).
+  // (0) New tokens that read this CTA's cache through this CTA's table ("same") alias its
+  //     rows by position.  Others (a shared-cache call whose tokens use different tables)
+  //     alias by physical address, which needs the block id of their slot.
   if (warp == 0 && lane < nsub) {
     const int len = s_len[lane];
-    s_phys[lane] = len > 0 ? p.table[s_toff[lane] + (len - 1) / B] : -1;
+    const bool same = s_coff[lane] == coff && s_toff[lane] == toff;
+    s_phys[lane] = (len > 0 && !same) ? p.table[s_toff[lane] + (len - 1) / B] : -1;
+  }
+  int sub_lo = 0x7fffffff, sub_hi = -1;  // chunks that may hold a same-table new row
+  bool any_foreign = false;
+  if (p.raw) {
+    for (int s2 = 0; s2 < nsub; ++s2) {
+      const int len = s_len[s2];
+      if (len <= 0) continue;
+      if (s_coff[s2] == coff && s_toff[s2] == toff) {
+        sub_lo = min(sub_lo, (len - 1) / kChunk);
+        sub_hi = max(sub_hi, (len - 1) / kChunk);
+      } else {
+        any_foreign = true;
+      }
+    }
+  }
+  const int c_full_lo = (lo + kChunk - 1) / kChunk;  // chunks in [c_full_lo, c_full_hi) have
+  const int c_full_hi = hi / kChunk;                 // every row inside [lo, hi)
+  if (tid == 0) {
+    s_ci.coff = coff;
+    s_ci.toff = toff;
+    s_ci.lo = lo;
+    s_ci.hi = hi;
+    s_ci.kvh = kvh;
+    s_ci.nsub = nsub;
+    s_ci.ibase = ibase;
+    s_ci.gcount = gcount;
+    s_ci.offset_ok = offset_ok;
   }
   // (1) query rows: normalise / scale / round, as the reference, into q2 [16][HD] bf16.
   for (int r = warp; r < 16; r += kConsumerWarps) {
@@ -592,38 +705,6 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
   }
   named_barrier_consumers();
 
-  // (3) append: the CTA whose chunk range holds a group token's position writes its k/v.
-  if (p.raw && warp == 0) {
-    for (int j = 0; j < gcount; ++j) {
-      const int si = ibase + j;
-      const int len = s_len[si];
-      if (len <= 0) continue;
-      const int pos = len - 1;
-      const int c = pos / kChunk;
-      if (c < cb || c >= ce) continue;
-      long long slot;
-      if (p.multi) {
-        slot = (long long)s_phys[si] * B + pos % B;
-      } else {
-        slot = p.slot_mapping[0];
-        if (slot < 0) continue;  // padding token: vLLM does not cache it
-      }
-      const long long blk = slot / B;
-      if (blk < 0 || (p.ncache_blocks > 0 && blk >= p.ncache_blocks) || !offset_ok) {
-        if (lane == 0) record_error(p.err, DORY_DEVERR_SLOT_OOB);
-        continue;
-      }
-      const long long base = s_coff[si] + blk * p.sb + (slot % B) * p.so + (long long)kvh * p.sh;
-      constexpr int kVec = HD / 8;  // 16-byte vectors per row
-      for (int i = lane; i < 2 * kVec; i += 32) {
-        const bool is_v = i >= kVec;
-        const int w = is_v ? i - kVec : i;
-        const uint4 val = reinterpret_cast<const uint4*>(subkv + (si * 2 + (is_v ? 1 : 0)) * HD)[w];
-        reinterpret_cast<uint4*>((is_v ? p.vc : p.kc) + base)[w] = val;
-      }
-    }
-  }
-
   // (4) B fragments of Q^T (k = dims, n = query rows), resident for the whole loop.
   const int g = lane >> 2;
   const int t4 = lane & 3;
@@ -675,38 +756,13 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
     const int c = mt.z;
     uint8_t* kst = smem + L::kStages + stage * L::kStageBytes;
     uint8_t* vst = kst + TILE;
+    // Boundary chunks, bad blocks and chunks holding a new token's row take the slow path
+    // (zeroing, substitution, the append itself); the rest go straight to the math.
     bool touched = false;
-    constexpr int kVec = HD / 8;  // 16-byte pieces per row
-    // Tensor copies bring whole 16-row boxes: zero the V rows outside the attended range
-    // (or the whole tile of a bad block) so that p = 0 never meets a non-finite value.
-    // The copy path zero-filled them in flight.
-    if (use_tma) {
-      const int r_lo = max(lo - c * kChunk, 0), r_hi = min(hi - c * kChunk, kChunk);
-      if (phys < 0 || r_lo > 0 || r_hi < kChunk) {
-        for (int idx = lane; idx < kChunk * kVec; idx += 32) {
-          const int r = idx / kVec, w = idx % kVec;
-          if (phys < 0 || r < r_lo || r >= r_hi)
-            *reinterpret_cast<uint4*>(vst + tile_off(r, w * 8)) = make_uint4(0, 0, 0, 0);
-        }
-        touched = true;
-      }
-    }
-    // New entries of this call replace the rows that alias their slots.
-    if (p.raw) {
-      const int in_block0 = (c % CPB) * kChunk;
-      for (int s = 0; s < nsub; ++s) {
-        if (s_len[s] <= 0 || s_phys[s] != phys || s_coff[s] != coff) continue;
-        const int r = ((s_len[s] - 1) % B) - in_block0;
-        if (r < 0 || r >= kChunk) continue;
-        for (int idx = lane; idx < 2 * kVec; idx += 32) {
-          const bool is_v = idx >= kVec;
-          const int w = is_v ? idx - kVec : idx;
-          const uint4 val = reinterpret_cast<const uint4*>(subkv + (s * 2 + (is_v ? 1 : 0)) * HD)[w];
-          *reinterpret_cast<uint4*>((is_v ? vst : kst) + tile_off(r, w * 8)) = val;
-        }
-        touched = true;
-      }
-    }
+    const bool partial = use_tma && (c < c_full_lo || c >= c_full_hi || phys < 0);
+    if (partial || (c >= sub_lo && c <= sub_hi) || any_foreign)
+      touched = fixup_stage<HD>(p, kst, vst, c, phys, partial, lane, s_ci, s_len, s_phys, s_coff,
+                                s_toff, subkv);
     __syncwarp();
 
     // S^T = K Q^T : [16 tokens x 8 rows] per n-tile.
@@ -1020,56 +1076,45 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 struct MapKey {
   const void* base;
   int64_t blocks, sb, so, sh;
-  int B, NKV, HD;
+  int B, NKV, quarters;
   bool operator==(const MapKey& o) const {
     return base == o.base && blocks == o.blocks && sb == o.sb && so == o.so && sh == o.sh &&
-           B == o.B && NKV == o.NKV && HD == o.HD;
+           B == o.B && NKV == o.NKV && quarters == o.quarters;
   }
 };
 struct MapEntry {
   MapKey key;
   CUtensorMap map;
-  int rowdim;
   bool ok;
 };
 
-// 4-D map of one cache view: (dims, rows | heads, heads | rows, blocks), the middle two in
-// order of stride; box 64 dims x 16 rows x 1 head x 1 block, 128-byte swizzle.  Encoded
-// maps are cached per thread (a call sequence revisits the same few caches).
-bool cache_tensor_map(const MapKey& k, CUtensorMap* out, int* rowdim) {
+// 5-D map of a cache view: (64 dims, rows of a block, 64-dim quarters of a row [stride 128
+// bytes], KV head, block); box 64 x 16 x quarters x 1 x 1 with 128-byte swizzle, so one
+// copy lands a chunk's tile as `quarters` swizzled [16][64] boxes.  quarters = HD / 64 for
+// a K or V tile, twice that for K and V together when V directly follows K.  Encoded maps
+// are cached per thread (a call sequence revisits the same few caches).
+bool cache_tensor_map(const MapKey& k, CUtensorMap* out) {
   constexpr int kSlots = 64;
   thread_local MapEntry cache[kSlots];
   thread_local int used = 0, next = 0;
   for (int i = 0; i < used; ++i)
     if (cache[i].key == k) {
       *out = cache[i].map;
-      *rowdim = cache[i].rowdim;
       return cache[i].ok;
     }
   MapEntry e;
   e.key = k;
   e.ok = false;
-  e.rowdim = 1;
   memset(&e.map, 0, sizeof(e.map));
   auto encode = tensor_map_encoder();
-  if (encode && k.blocks > 0 && k.blocks <= 0x7fffffff) {
-    cuuint64_t dims[4], strides[3];
-    cuuint32_t box[4], estr[4] = {1, 1, 1, 1};
-    dims[0] = cuuint64_t(k.HD);
-    box[0] = 64;
-    if (k.so <= k.sh) {
-      dims[1] = cuuint64_t(k.B); strides[0] = cuuint64_t(k.so) * 2; box[1] = kChunk;
-      dims[2] = cuuint64_t(k.NKV); strides[1] = cuuint64_t(k.sh) * 2; box[2] = 1;
-      e.rowdim = 1;
-    } else {
-      dims[1] = cuuint64_t(k.NKV); strides[0] = cuuint64_t(k.sh) * 2; box[1] = 1;
-      dims[2] = cuuint64_t(k.B); strides[1] = cuuint64_t(k.so) * 2; box[2] = kChunk;
-      e.rowdim = 2;
-    }
-    dims[3] = cuuint64_t(k.blocks);
-    strides[2] = cuuint64_t(k.sb) * 2;
-    box[3] = 1;
-    CUresult r = encode(&e.map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(k.base),
+  if (encode && k.blocks > 0 && k.blocks <= 0x7fffffff && k.quarters <= 8) {
+    cuuint64_t dims[5] = {64, cuuint64_t(k.B), cuuint64_t(k.quarters), cuuint64_t(k.NKV),
+                          cuuint64_t(k.blocks)};
+    cuuint64_t strides[4] = {cuuint64_t(k.so) * 2, 128, cuuint64_t(k.sh) * 2,
+                             cuuint64_t(k.sb) * 2};
+    cuuint32_t box[5] = {64, cuuint32_t(kChunk), cuuint32_t(k.quarters), 1, 1};
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    CUresult r = encode(&e.map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(k.base),
                         dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -1082,7 +1127,6 @@ bool cache_tensor_map(const MapKey& k, CUtensorMap* out, int* rowdim) {
     next = (next + 1) % kSlots;
   }
   *out = e.map;
-  *rowdim = e.rowdim;
   return e.ok;
 }
 
@@ -1223,16 +1267,24 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
   {
     const int64_t nb = a.num_cache_blocks > 0 ? a.num_cache_blocks : 0;
     const int64_t extent = multi ? (nb * 64 < 0x7fffffff ? nb * 64 : 0x7fffffff) : nb;
-    MapKey kk{a.key_cache, extent, a.stride_block, a.stride_offset, a.stride_head,
-              a.block_size, a.num_kv_heads, HD};
-    MapKey vk = kk;
-    vk.base = a.value_cache;
-    int rk = 1, rv = 1;
-    const bool okk = nb > 0 && cache_tensor_map(kk, &kp.tmk, &rk);
-    const bool okv = okk && cache_tensor_map(vk, &kp.tmv, &rv);
-    kp.tm_ok = okk && okv && rk == rv;
-    kp.tm_rowdim = rk;
+    const int q = HD / 64;
+    kp.tm_mode = 0;
     kp.tm_blocks = extent;
+    if (nb > 0) {
+      const bool adjacent = static_cast<const char*>(a.value_cache) ==
+                            static_cast<const char*>(a.key_cache) + HD * 2;
+      MapKey both{a.key_cache, extent, a.stride_block, a.stride_offset, a.stride_head,
+                  a.block_size, a.num_kv_heads, 2 * q};
+      if (adjacent && cache_tensor_map(both, &kp.tmk)) {
+        kp.tm_mode = 1;
+      } else {
+        MapKey kk{a.key_cache, extent, a.stride_block, a.stride_offset, a.stride_head,
+                  a.block_size, a.num_kv_heads, q};
+        MapKey vk = kk;
+        vk.base = a.value_cache;
+        if (cache_tensor_map(kk, &kp.tmk) && cache_tensor_map(vk, &kp.tmv)) kp.tm_mode = 2;
+      }
+    }
   }
 
   dim3 grid(a.splits, a.num_kv_heads, a.num_tokens);
