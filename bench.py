@@ -252,7 +252,8 @@ def make_attention(wl: DeviceWorkload, args):
     from dory_decode_attention import DecodeAttention
     return DecodeAttention(NH, NKV, HD, wl.dev, splits=args.splits,
                            max_tokens=max(wl.tokens, 1),
-                           min_blocks_per_split=args.min_blocks_per_split)
+                           min_blocks_per_split=args.min_blocks_per_split,
+                           overlap_launch=getattr(args, "overlap_launch", False))
 
 
 def layer_call(attn, wl: DeviceWorkload, app: int, layer: int, qk, v, gate, out):
@@ -356,7 +357,8 @@ def bench_ours(args, world, rank, local):
                    "parallelism": f"request partition over {world} GPU(s), no collectives",
                    "distinct_pools_per_rank": wl.num_pools,
                    "l2": "inputs larger than L2 (each pool > 126 MB; pools cycled per layer)",
-                   "splits": args.splits, "min_blocks_per_split": args.min_blocks_per_split},
+                   "splits": args.splits, "min_blocks_per_split": args.min_blocks_per_split,
+                   "overlap_launch": args.overlap_launch},
         "us_per_layer_step": round(us_per_layer, 3),
         "hbm_gbs": round(hbm_gbs, 1),
         "roofline": roofline,
@@ -557,6 +559,8 @@ def main() -> int:
     ap.add_argument("--workload", default="config5")
     ap.add_argument("--splits", type=int, default=2)
     ap.add_argument("--min-blocks-per-split", type=int, default=64)
+    ap.add_argument("--overlap-launch", action="store_true",
+                    help="launch each layer call as a programmatic dependent of the previous one")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     args = ap.parse_args()

@@ -20,7 +20,7 @@ OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_ALIGNMENT, ERR_CUDA = range(5)
 # DoryDType
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = range(3)
 # DORY_FLAG_*
-FLAG_RAW_QKV, FLAG_MULTI_TOKEN, FLAG_SHARED_CACHE = 1, 2, 4
+FLAG_RAW_QKV, FLAG_MULTI_TOKEN, FLAG_SHARED_CACHE, FLAG_OVERLAP_LAUNCH = 1, 2, 4, 8
 # DORY_DEVERR_*
 DEVERR_BLOCK_OOB, DEVERR_SLOT_OOB, DEVERR_OFFSET_ALIGN, DEVERR_WAIT_TIMEOUT = 1, 2, 4, 8
 DEVERR_NAMES = {DEVERR_BLOCK_OOB: "block id out of range", DEVERR_SLOT_OOB: "slot out of range",

@@ -39,6 +39,7 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <stdarg.h>
+#include <stddef.h>
 #include <stdint.h>
 #include <stdio.h>
 #include <string.h>
@@ -59,34 +60,42 @@ constexpr float kLog2e = 1.4426950408889634f;
 // ------------------------------------------------------------------------------------
 // Kernel parameters (device-side copy of DoryDecodeParams plus derived values).
 // ------------------------------------------------------------------------------------
-struct KParams {
-  CUtensorMap tmk;  // cache views as 5-D tensors (64 dims, rows, 64-dim quarters of a row,
-  CUtensorMap tmv;  // KV head, block), one box = a chunk's K (and V) tile, 128-byte swizzle
+// Field order matters: the kernel reads its parameters through the constant cache, and a
+// CTA that is the first on its SM pays one L2 round trip per 64-byte line it touches.  The
+// scalars and pointers of the prologue come first (lines 0-1), the rest next, the tensor
+// maps (read by the copy engine) last; every CTA touches all lines at once on entry.
+struct alignas(64) KParams {
+  // line 0: scalars of the split layout and the prologue
+  int T, NH, NKV, G, B, window, S, bpt;
+  int tps_min, b_shift, cpb_shift, raw, multi, shared, nsub, q_stride;
+  // line 1: the first dependent loads
+  const int32_t* seq_lens;
+  const int64_t* cache_offsets;
+  const int64_t* table_offsets;
+  const int32_t* table;
+  int64_t sb, so, sh, ncache_blocks;
+  // lines 2-3: inputs, outputs, scratch
   const void* q;
   const float* v;
   const void* sqk;
   const int64_t* slot_mapping;
   __nv_bfloat16* kc;
   __nv_bfloat16* vc;
-  const int32_t* table;
-  const int64_t* table_offsets;
-  const int64_t* cache_offsets;
-  const int32_t* seq_lens;
   const float* gate;
   float* out;
   uint32_t* err;
   int32_t* counters;
   float2* pml;  // [max_tokens][S][NH] (max in log2 units, sum)
   float* po;    // [max_tokens][S][NH][HD]
-  int64_t sb, so, sh, ncache_blocks;
-  float scale, sqk_factor, eps;
-  int T, NH, NKV, G, B, window, S, bpt, min_bps, sqk_dtype;
-  int raw, multi, shared;
-  int q_stride;  // elements of q per token
-  int nsub;      // new tokens whose k/v this call substitutes (shared: T, raw: 1, else 0)
-  int tm_mode;   // 0: no tensor maps; 1: tmk covers K and V (V right after K); 2: tmk, tmv
   int64_t tm_blocks;  // extent of the block dimension of the tensor maps
+  float scale, sqk_factor, eps;
+  int min_bps, sqk_dtype, overlap;
+  int tm_mode;   // 0: no tensor maps; 1: tmk covers K and V (V right after K); 2: tmk, tmv
+  CUtensorMap tmk;  // cache views as 5-D tensors (64 dims, rows, 64-dim quarters of a row,
+  CUtensorMap tmv;  // KV head, block), one box = a chunk's K (and V) tile, 128-byte swizzle
 };
+static_assert(offsetof(KParams, seq_lens) == 64, "line 1 starts with the dependent pointers");
+static_assert(offsetof(KParams, tmk) % 64 == 0, "tensor maps are 64-byte aligned");
 
 // Scratch layout (bytes), shared by host and device.
 struct ScratchLayout {
@@ -175,6 +184,14 @@ __device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map
       "r"(bar), "l"(policy)
       : "memory");
 }
+// Programmatic dependent launch: wait for the previous grid on the stream to complete (and
+// its writes to be visible); allow the next grid to launch.  No-ops without the attribute.
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
 __device__ __forceinline__ void prefetch_tensormap(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }
@@ -262,7 +279,22 @@ __device__ __forceinline__ float row_inv_norm(const float (&x)[PER_LANE], float 
   for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
   const float sum32 = __double2float_rn(acc);
   const float t = __fadd_rn(sum32, eps);
-  return __double2float_rn(1.0 / sqrt(double(t)));
+  // 1 / sqrt(t), correctly rounded to FP32: the FP32 estimate refined by two Newton-Raphson
+  // steps in FP64 for f(y) = 1 / y^2 - t, y <- y (3 - t y^2) / 2 (relative error well
+  // below 1e-15 afterwards), then rounded once.
+  const double td = double(t);
+  double y = double(rsqrtf(t));
+  y = y * (1.5 - 0.5 * td * y * y);
+  y = y * (1.5 - 0.5 * td * y * y);
+  return __double2float_rn(y);
+}
+
+// x / d and x % d for x >= 0, by shifting when d is a power of two (shift >= 0).
+__device__ __forceinline__ int div_p2(int x, int d, int shift) {
+  return shift >= 0 ? (x >> shift) : x / d;
+}
+__device__ __forceinline__ int mod_p2(int x, int d, int shift) {
+  return shift >= 0 ? (x & (d - 1)) : x % d;
 }
 
 // Split layout of the reference (_split_layout, dory_decode_attention.py:28-44) applied to
@@ -270,7 +302,8 @@ __device__ __forceinline__ float row_inv_norm(const float (&x)[PER_LANE], float 
 struct Split {
   int first_block, nblocks, tiles, tps, active;
 };
-__device__ __forceinline__ Split split_layout(int lo, int hi, int B, int S, int bpt, int min_bps) {
+__device__ __forceinline__ Split split_layout(int lo, int hi, int B, int b_shift, int S, int bpt,
+                                              int tps_min) {
   Split s;
   if (hi <= 0) {
     s.first_block = 0;
@@ -280,11 +313,10 @@ __device__ __forceinline__ Split split_layout(int lo, int hi, int B, int S, int 
     s.active = 0;
     return s;
   }
-  s.first_block = lo / B;
-  s.nblocks = (hi + B - 1) / B - s.first_block;
-  s.tiles = (s.nblocks + bpt - 1) / bpt;
+  s.first_block = div_p2(lo, B, b_shift);
+  s.nblocks = div_p2(hi + B - 1, B, b_shift) - s.first_block;
+  s.tiles = bpt == 1 ? s.nblocks : (s.nblocks + bpt - 1) / bpt;
   int tps = (s.tiles + S - 1) / S;
-  const int tps_min = (min_bps + bpt - 1) / bpt;
   if (tps < tps_min) tps = tps_min;
   if (tps < 1) tps = 1;
   s.tps = tps;
@@ -343,7 +375,7 @@ __device__ __forceinline__ bool fixup_stage(const KParams& p, uint8_t* kst, uint
     if (same) {
       if (pos / kChunk == c) r = pos % kChunk;
     } else if (phys >= 0 && s_phys[s] == phys && s_coff[s] == coff) {
-      const int rr = pos % B - (c % CPB) * kChunk;
+      const int rr = mod_p2(pos, B, p.b_shift) - mod_p2(c, CPB, p.cpb_shift) * kChunk;
       if (rr >= 0 && rr < kChunk) r = rr;
     }
     if (r < 0) continue;
@@ -358,7 +390,7 @@ __device__ __forceinline__ bool fixup_stage(const KParams& p, uint8_t* kst, uint
     long long slot;
     if (p.multi) {
       if (phys < 0) continue;  // its block id was out of range (already recorded)
-      slot = (long long)phys * B + pos % B;
+      slot = (long long)phys * B + mod_p2(pos, B, p.b_shift);
     } else {
       slot = p.slot_mapping[0];
       if (slot < 0) continue;  // padding token: vLLM does not cache it
@@ -411,6 +443,11 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
   const int B = p.B;
   const int Q = p.NH * HD;
 
+  // Pull every parameter line into the constant cache at once (see KParams).
+  if (warp == 0 && lane * 64 < int(offsetof(KParams, tmk))) {
+    const uint32_t word = reinterpret_cast<const uint32_t*>(&p)[lane * 16];
+    asm volatile("" ::"r"(word));
+  }
   // ---- token info: the group's tokens and the tokens whose new k/v this CTA may have to
   //      substitute (shared-cache: every token of the call; otherwise this token alone).
   const int ninfo = p.shared ? p.T : 1;
@@ -478,12 +515,13 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
   const long long coff = s_coff[ibase];
   const long long toff = s_toff[ibase];
   const int nsub = p.nsub;
-  const Split sp = split_layout(lo, hi, B, p.S, p.bpt, p.min_bps);
+  const Split sp = split_layout(lo, hi, B, p.b_shift, p.S, p.bpt, p.tps_min);
   const int nrows = gcount * G;
 
   if (sp.tiles == 0) {
     // Padding request(s): the reference's combine writes 0 * gate.
     if (split == 0) {
+      grid_dependency_wait();
       for (int i = tid; i < nrows * HD; i += kThreads) {
         const int r = i / HD, d = i % HD;
         const int t = gstart + r / G, head = kvh * G + r % G;
@@ -512,9 +550,9 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
 
   const bool offset_ok = (coff & 7) == 0;
   // Tensor copies address the cache by block index, so an offset must be whole blocks.
-  const bool use_tma = p.tm_mode != 0 && offset_ok && coff % p.sb == 0 && coff >= 0 &&
-                       coff / p.sb + p.ncache_blocks <= p.tm_blocks;
-  const long long coff_blocks = use_tma ? coff / p.sb : 0;
+  const long long coff_blocks = coff == 0 ? 0 : (coff % p.sb == 0 ? coff / p.sb : -1);
+  const bool use_tma = p.tm_mode != 0 && offset_ok && coff_blocks >= 0 &&
+                       coff_blocks + p.ncache_blocks <= p.tm_blocks;
   if (tid == 0) {
     for (int s = 0; s < NS; ++s) {
       // tensor path: the producer's arrive.expect_tx; copy path: 32 lanes' completions + 1
@@ -543,8 +581,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
     constexpr int VEC = HD / 8;                    // 16-byte pieces per row
     constexpr int PER_LANE = 2 * kChunk * VEC / 32;
     // Block-table window of 32 entries, prefetched one window ahead.
-    const int b_first = cb / CPB;
-    const int b_last = (ce - 1) / CPB;
+    const int b_first = div_p2(cb, CPB, p.cpb_shift);
+    const int b_last = div_p2(ce - 1, CPB, p.cpb_shift);
     int wbase = b_first;
     int win_cur = (b_first + lane <= b_last) ? table[b_first + lane] : -1;
     int win_nxt = (b_first + 32 + lane <= b_last) ? table[b_first + 32 + lane] : -1;
@@ -558,7 +596,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
         break;
       }
       const int c = cb + i;
-      const int blk = c / CPB;
+      const int blk = div_p2(c, CPB, p.cpb_shift);
       while (blk >= wbase + 32) {
         wbase += 32;
         win_cur = win_nxt;
@@ -575,7 +613,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
           meta[stage] = make_int4(phys_ok ? phys : -1, 0, c, 0);
           if (phys_ok) {
             mbar_arrive_expect_tx(full_bar(stage), L::kStageBytes);
-            const int row0 = (c % CPB) * kChunk;
+            const int row0 = mod_p2(c, CPB, p.cpb_shift) * kChunk;
             const int blkc = int(coff_blocks + phys);
             tma_load_5d(kt, &p.tmk, 0, row0, 0, kvh, blkc, full_bar(stage), policy);
             if (p.tm_mode == 2) tma_load_5d(vt, &p.tmv, 0, row0, 0, kvh, blkc, full_bar(stage), policy);
@@ -585,7 +623,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
         }
       } else {
         const int64_t block_off = int64_t(phys_ok ? phys : 0) * p.sb +
-                                  int64_t((c % CPB) * kChunk) * p.so;
+                                  int64_t(mod_p2(c, CPB, p.cpb_shift) * kChunk) * p.so;
 #pragma unroll
         for (int k = 0; k < PER_LANE; ++k) {
           const int j = k * 32 + lane;
@@ -606,6 +644,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
       }
       ++issued;
     }
+    grid_launch_dependents();
     if (!use_tma) {
       // Stay until this warp's copies have landed (bounded), then leave.
       for (int s = 0; s < NS && s < issued; ++s) {
@@ -617,6 +656,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
   }
 
   // =============================== consumer warps ===============================
+  // Everything below reads this step's inputs or writes outputs: after the previous grid.
+  grid_dependency_wait();
   // (0) New tokens that read this CTA's cache through this CTA's table ("same") alias its
   //     rows by position.  Others (a shared-cache call whose tokens use different tables)
   //     alias by physical address, which needs the block id of their slot.
@@ -846,6 +887,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
       l[nt][i] = v;
     }
 
+  grid_launch_dependents();  // streaming is done: the next grid may start its prologue
   // Drain: every copy this CTA issued must have landed before its shared memory is reused
   // or released (only matters after a timeout; otherwise these waits return at once).
   named_barrier_consumers();
@@ -938,7 +980,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
   // Three phases, so that no thread waits on one L2 round trip per split:
   //  (a) every split's (max, sum) of every row into shared memory, all loads in flight;
   //  (b) per row, the merged max, each split's weight and 1 / total, one warp per row;
-  //  (c) per (row, 4 dims), the weighted sum over splits with 8 loads in flight.
+  //  (c) per (row, 4 dims), the weighted sum over splits, 16 loads in flight per thread.
   const int active = sp.active;
   float2* s_stat = reinterpret_cast<float2*>(smem + L::kStages);      // [active][ROWS]
   float* s_wt = reinterpret_cast<float*>(s_stat + active * ROWS);      // [active][ROWS]
@@ -968,27 +1010,54 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
   }
   named_barrier_consumers();
   constexpr int UPR = HD / 4;  // float4 units per row
-  for (int u = tid; u < nrows * UPR; u += kConsumerWarps * 32) {
+  constexpr int NTHR = kConsumerWarps * 32;
+  constexpr int UPT = (ROWS * UPR + NTHR - 1) / NTHR;  // units per thread (at most)
+  constexpr int SB = UPT >= 4 ? 4 : 16 / UPT;         // splits per batch: 16 loads in flight
+  const int64_t sstride = int64_t(p.NH) * UPR;         // float4s between consecutive splits
+  const int units = nrows * UPR;
+  const float4* srcs[UPT];
+  float4 acc[UPT];
+  int rowu[UPT];
+#pragma unroll
+  for (int k = 0; k < UPT; ++k) {
+    const int u = tid + k * NTHR;
+    const int r = u < units ? u / UPR : 0, d4 = u % UPR;
+    const int t = gstart + r / G, head = kvh * G + r % G;
+    srcs[k] = reinterpret_cast<const float4*>(p.po) + ((int64_t(t) * S) * p.NH + head) * UPR + d4;
+    rowu[k] = r;
+    acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int s0 = 0; s0 < active; s0 += SB) {
+    float4 v[UPT][SB];
+#pragma unroll
+    for (int k = 0; k < UPT; ++k)
+#pragma unroll
+      for (int j = 0; j < SB; ++j)
+        v[k][j] = (tid + k * NTHR < units && s0 + j < active) ? __ldcg(srcs[k] + (s0 + j) * sstride)
+                                                             : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int k = 0; k < UPT; ++k)
+#pragma unroll
+      for (int j = 0; j < SB; ++j) {
+        const float w = s0 + j < active ? s_wt[(s0 + j) * ROWS + rowu[k]] : 0.0f;
+        acc[k].x += w * v[k][j].x; acc[k].y += w * v[k][j].y;
+        acc[k].z += w * v[k][j].z; acc[k].w += w * v[k][j].w;
+      }
+  }
+#pragma unroll
+  for (int k = 0; k < UPT; ++k) {
+    const int u = tid + k * NTHR;
+    if (u >= units) continue;
     const int r = u / UPR, d4 = u % UPR;
     const int t = gstart + r / G, head = kvh * G + r % G;
-    const float4* src = reinterpret_cast<const float4*>(p.po) +
-                        ((int64_t(t) * S) * p.NH + head) * UPR + d4;
-    const int64_t sstride = int64_t(p.NH) * UPR;  // float4s between consecutive splits
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll 8
-    for (int sidx = 0; sidx < active; ++sidx) {
-      const float w = s_wt[sidx * ROWS + r];
-      const float4 o = __ldcg(src + sidx * sstride);
-      acc.x += w * o.x; acc.y += w * o.y; acc.z += w * o.z; acc.w += w * o.w;
-    }
     const float inv = s_inv[r];
     const int e0 = head * HD + d4 * 4;  // 4 consecutive elements: same e / 8, e % 8 = j0..j0+3
     const float4 gt = *reinterpret_cast<const float4*>(p.gate + int64_t(t) * Q + e0);
     float* out = p.out + int64_t(t) * Q + (e0 % 8) * (Q / 8) + e0 / 8;
-    out[0] = acc.x * inv * gt.x;
-    out[Q / 8] = acc.y * inv * gt.y;
-    out[2 * (Q / 8)] = acc.z * inv * gt.z;
-    out[3 * (Q / 8)] = acc.w * inv * gt.w;
+    out[0] = acc[k].x * inv * gt.x;
+    out[Q / 8] = acc[k].y * inv * gt.y;
+    out[2 * (Q / 8)] = acc[k].z * inv * gt.z;
+    out[3 * (Q / 8)] = acc[k].w * inv * gt.w;
   }
 }
 
@@ -1019,8 +1088,19 @@ int32_t launch(const KParams& kp, dim3 grid, int smem_bytes, cudaStream_t stream
       return fail(DORY_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
     configured[dev] = 1;
   }
-  fn<<<grid, kThreads, smem_bytes, stream>>>(kp);
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = size_t(smem_bytes);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = kp.overlap ? 1 : 0;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, fn, kp);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return fail(DORY_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
   return DORY_OK;
 }
@@ -1171,6 +1251,7 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
   const bool raw = a.flags & DORY_FLAG_RAW_QKV;
   const bool multi = a.flags & DORY_FLAG_MULTI_TOKEN;
   const bool shared = a.flags & DORY_FLAG_SHARED_CACHE;
+  const bool overlap = a.flags & DORY_FLAG_OVERLAP_LAUNCH;
   if (a.num_tokens < 0) return fail(DORY_ERR_INVALID_ARGUMENT, "negative token count");
   if (a.num_tokens > a.max_tokens)
     return fail(DORY_ERR_INVALID_ARGUMENT, "too many tokens for the scratch buffers");
@@ -1255,10 +1336,19 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
   kp.S = a.splits;
   kp.bpt = a.blocks_per_tile;
   kp.min_bps = a.min_blocks_per_split < 1 ? 1 : a.min_blocks_per_split;
+  kp.tps_min = (kp.min_bps + a.blocks_per_tile - 1) / a.blocks_per_tile;
+  auto log2_exact = [](int v) {
+    int k = 0;
+    while ((1 << k) < v) ++k;
+    return (1 << k) == v ? k : -1;
+  };
+  kp.b_shift = log2_exact(a.block_size);
+  kp.cpb_shift = log2_exact(a.block_size / 16);
   kp.sqk_dtype = a.sqk_dtype;
   kp.raw = raw;
   kp.multi = multi;
   kp.shared = shared;
+  kp.overlap = overlap;
   kp.q_stride = (raw ? a.num_heads + a.num_kv_heads : a.num_heads) * HD;
   kp.nsub = raw ? (shared ? a.num_tokens : 1) : 0;
   // Tensor maps of the K and V views.  Multi-token calls may shift the cache by whole

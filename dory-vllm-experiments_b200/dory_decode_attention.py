@@ -50,13 +50,17 @@ class DecodeAttention:
     accepted for signature compatibility and ignored (this kernel's pipeline depth and warp
     roles are fixed per head_dim).  blocks_per_tile keeps its meaning: the granularity, in
     cache blocks, of the split ranges.  min_blocks_per_split (B200 addition) keeps short
-    sequences from being cut into splits of a block or two.
+    sequences from being cut into splits of a block or two.  overlap_launch (B200 addition,
+    off by default) launches each call as a programmatic dependent of the previous kernel on
+    the stream, so its prologue and K/V loads overlap that kernel's tail; the kernel right
+    before a call must then not write the call's seq_lens, block tables, offsets,
+    slot_mapping or the cache rows it attends (q/k/v/gate inputs are still ordered).
     """
 
     def __init__(self, num_heads: int, num_kv_heads: int, head_dim: int, device: torch.device,
                  splits: int = 32, blocks_per_tile: int = 1, num_warps: int = 4,
                  num_stages: int = 2, dim_chunk: int = 64, max_tokens: int = 1,
-                 min_blocks_per_split: int = 1):
+                 min_blocks_per_split: int = 1, overlap_launch: bool = False):
         if num_heads % num_kv_heads:
             raise ValueError("query heads must be a multiple of KV heads")
         self.num_heads, self.num_kv_heads, self.head_dim = num_heads, num_kv_heads, head_dim
@@ -65,6 +69,7 @@ class DecodeAttention:
         self.num_stages, self.dim_chunk = num_stages, dim_chunk
         self.max_tokens = max_tokens
         self.min_blocks_per_split = min_blocks_per_split
+        self.overlap_launch = bool(overlap_launch)
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise RuntimeError("DecodeAttention runs on CUDA devices only (no CPU path)")
@@ -173,7 +178,7 @@ class DecodeAttention:
         if block_table.dtype != torch.int32 or seq_lens.dtype != torch.int32:
             raise ValueError("block tables and seq_lens must be int32")
         p = self._params
-        flags = 0
+        flags = _native.FLAG_OVERLAP_LAUNCH if self.overlap_launch else 0
         if raw is not None:
             v, sqk, sqk_factor, eps, slot_mapping = raw
             if q.dtype != torch.float32 or v.dtype != torch.float32:

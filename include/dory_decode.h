@@ -54,7 +54,13 @@ enum {
   DORY_FLAG_MULTI_TOKEN = 2u,
   /* Tokens of one call share one cache and read each other's new entries
    * (reference shared_cache=True: write-all-first semantics). */
-  DORY_FLAG_SHARED_CACHE = 4u
+  DORY_FLAG_SHARED_CACHE = 4u,
+  /* Launch as a programmatic dependent of the previous kernel on the stream: the next
+   * call's prologue and K/V loads overlap the end of this one.  Contract: the kernel
+   * immediately before this call on the stream must not write this call's seq_lens, block
+   * tables, offsets, slot_mapping or the cache rows it attends (q/k/v/gate and all outputs
+   * are ordered as usual).  No counterpart in the reference (Triton launches). */
+  DORY_FLAG_OVERLAP_LAUNCH = 8u
 };
 
 /* Device error bits, accumulated in the scratch header and read back with

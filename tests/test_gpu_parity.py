@@ -293,3 +293,47 @@ def test_argument_errors_raise_like_reference():
         attn.from_raw(d["qk"][0], d["v"][0], d["sqk"], 0.7, EPS, d["slots"][0:1], d["key"],
                       d["value"].contiguous(), d["tables"][0], d["seq_lens"][0:1], 0,
                       case.scale, d["gate"][0], d["out"][0])
+
+
+@pytest.mark.parametrize("graph", [False, True])
+def test_overlapped_launches_match(graph):
+    """overlap_launch=True (programmatic dependent launch) over a chain of calls on distinct
+    caches gives the same outputs and caches, bit for bit, as ordinary launches."""
+    cases = [W.single(seed=300 + i, context=200 + 97 * i, pool_blocks=40, window=512 * (i % 2))
+             for i in range(5)]
+    results = []
+    for overlap in (False, True):
+        ds = [W.to_device(c, "triton", "cuda") for c in cases]
+        attn = DecodeAttention(32, 8, 128, torch.device("cuda"), splits=16,
+                               overlap_launch=overlap)
+
+        def chain():
+            for c, d in zip(cases, ds):
+                attn.from_raw(d["qk"][0], d["v"][0], d["sqk"], c.sqk_factor, EPS,
+                              d["slots"][0:1], d["key"], d["value"], d["tables"][0],
+                              d["seq_lens"][0:1], c.window, c.scale, d["gate"][0], d["out"][0])
+
+        if graph:
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                chain()
+            torch.cuda.current_stream().wait_stream(s)
+            torch.cuda.synchronize()
+            # replay on the appended caches: outputs of the graph's first replay are compared
+            for d, c in zip(ds, cases):
+                d["raw"].copy_(W.to_device(c, "triton", "cuda")["raw"])
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                chain()
+            g.replay()
+        else:
+            chain()
+        torch.cuda.synchronize()
+        attn.check_errors()
+        results.append([(d["out"].cpu(), d["raw"].cpu()) for d in ds])
+    for (o0, r0), (o1, r1) in zip(*results):
+        assert torch.equal(o0, o1)
+        assert torch.equal(r0.view(torch.int16), r1.view(torch.int16))
+    for c, (o, _) in zip(cases, results[0]):
+        assert_close(o, oracle_out(c))
