@@ -274,6 +274,33 @@ def run_step(attn, wl: DeviceWorkload):
 # our arm
 # ---------------------------------------------------------------------------------------
 
+def subset(lens, k: int):
+    """k sequences evenly spaced by length (keeps the workload's length distribution)."""
+    if k <= 0 or k >= len(lens):
+        return lens
+    order = sorted(range(len(lens)), key=lambda i: lens[i])
+    return [lens[order[int((i + 0.5) * len(order) / k)]] for i in range(k)]
+
+
+def bench_profile(args):
+    """Eager steps of the layer sequence for profilers (no graph, no e2e, no CPU leg)."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    lens_all, tps, shared, layers, pool_factor, notes = workload_spec(args.workload)
+    lens_all = subset(lens_all, args.max_seqs)
+    wl = DeviceWorkload(lens_all, tps, shared, layers, pool_factor, dev, 11,
+                        mem_fraction=args.mem_fraction)
+    attn = make_attention(wl, args)
+    for _ in range(args.profile_steps):
+        run_step(attn, wl)
+    torch.cuda.synchronize(dev)
+    attn.check_errors()
+    print(json.dumps({"profile_steps": args.profile_steps, "launches": args.profile_steps *
+                      len(layers), "sequences": len(lens_all), "pools": wl.num_pools,
+                      "algorithmic_bytes_per_launch": wl.algorithmic_bytes_per_application()}),
+          flush=True)
+
+
 def bench_ours(args, world, rank, local):
     dist = init_dist(world, local)
     dev = torch.device("cuda", local if world > 1 else 0)
@@ -473,67 +500,78 @@ def cpu_sample(workload: str, lens_all, budget_s: float):
     return [lens_all[i] for i in pick], False
 
 
-def cpu_baseline(workload: str, lens_all, budget_s: float, sample_steps: int = 0):
-    """Times the CPU restatement on a bounded sample; repeats the sample until `budget_s`
-    seconds have passed (or exactly `sample_steps` times when that is > 0)."""
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import dory_oracle as O
-    threads = os.cpu_count() or 1
-    torch.set_num_threads(threads)
-    lens, shared = cpu_sample(workload, lens_all, budget_s)
-    if shared:
-        case = W.wavefront(seed=1, prompt=lens[0], generated=0, tokens=4)
-    else:
-        case = W.batched(seed=4, lens=lens)
-    key = case.key.to(torch.bfloat16)
-    value = case.value.to(torch.bfloat16)
-    width = case.tables.shape[1]
+class CpuSample:
+    """A bounded sample of the workload on the host CPU: the reference semantics in PyTorch
+    eager FP32 (oracle/dory_oracle.py) over a spread of the workload's sequences, one layer."""
 
-    def once():
-        k, v = key.clone(), value.clone()
-        O.multi_from_raw(case.qk, case.v, case.sqk, case.sqk_factor, O.EPS,
-                         torch.zeros(case.tokens, dtype=torch.int64), k.view(-1), v.view(-1),
-                         tuple(k.shape), k.stride(), case.tables.reshape(-1),
-                         torch.tensor([r * width for r in case.table_rows]), case.seq_lens,
-                         case.window, case.scale, case.gate, NH, NKV,
-                         shared_cache=case.shared)
+    def __init__(self, workload: str, lens_all, budget_s: float):
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import dory_oracle as O
+        self.O = O
+        self.threads = os.cpu_count() or 1
+        torch.set_num_threads(self.threads)
+        self.lens, shared = cpu_sample(workload, lens_all, budget_s)
+        if shared:
+            self.case = W.wavefront(seed=1, prompt=self.lens[0], generated=0, tokens=4)
+        else:
+            self.case = W.batched(seed=4, lens=self.lens)
+        self.shared = shared
+        self.key = self.case.key.to(torch.bfloat16)
+        self.value = self.case.value.to(torch.bfloat16)
+        _, _, _, layers, _, _ = workload_spec(workload)
+        self.layers = len(layers)
 
-    once()  # warm-up
-    t0 = time.perf_counter()
-    n = 0
-    while True:
-        once()
-        n += 1
-        elapsed = time.perf_counter() - t0
-        if (sample_steps > 0 and n >= sample_steps) or (sample_steps <= 0 and elapsed >= budget_s):
-            break
-    dt = elapsed / n
-    _, tps, _, layers, _, _ = workload_spec(workload)
-    seqs = 1 if shared else len(lens)
-    value_seqs = seqs / (dt * len(layers))
-    return {"value": round(value_seqs, 4), "unit": "seqs/s", "cores": threads, "kind": "port",
-            "sample": f"{len(lens)} sequence(s) (ctx {min(lens)}..{max(lens)}, "
-                      f"mean {sum(lens) / len(lens):.0f}) x 1 layer, {dt:.3f} s each, "
-                      f"{n} repetition(s), scaled to "
-                      f"{len(layers)} layers; PyTorch eager FP32 restatement of the "
-                      "reference semantics (oracle/dory_oracle.py)"}
+    def once(self) -> float:
+        """Seconds for one pass of the sample (one layer, the caches restored first)."""
+        c, O = self.case, self.O
+        k, v = self.key.clone(), self.value.clone()
+        width = c.tables.shape[1]
+        t0 = time.perf_counter()
+        O.multi_from_raw(c.qk, c.v, c.sqk, c.sqk_factor, O.EPS,
+                         torch.zeros(c.tokens, dtype=torch.int64), k.view(-1), v.view(-1),
+                         tuple(k.shape), k.stride(), c.tables.reshape(-1),
+                         torch.tensor([r * width for r in c.table_rows]), c.seq_lens,
+                         c.window, c.scale, c.gate, NH, NKV, shared_cache=c.shared)
+        return time.perf_counter() - t0
+
+    def seqs_per_s(self, seconds: float) -> float:
+        seqs = 1 if self.shared else len(self.lens)
+        return seqs / (seconds * self.layers)
+
+    def describe(self, seconds: float, reps: int) -> str:
+        return (f"{len(self.lens)} sequence(s) (ctx {min(self.lens)}..{max(self.lens)}, mean "
+                f"{sum(self.lens) / len(self.lens):.0f}) x 1 layer, {seconds:.3f} s each, {reps} "
+                f"repetition(s), scaled to {self.layers} layers; PyTorch eager FP32 restatement "
+                "of the reference semantics (oracle/dory_oracle.py)")
+
+
+def cpu_baseline(workload: str, lens_all, budget_s: float):
+    """Times the CPU sample, repeating it until `budget_s` seconds have passed."""
+    sample = CpuSample(workload, lens_all, budget_s)
+    sample.once()  # warm-up
+    total, reps = 0.0, 0
+    while total < budget_s or reps == 0:
+        total += sample.once()
+        reps += 1
+    dt = total / reps
+    return {"value": round(sample.seqs_per_s(dt), 4), "unit": "seqs/s", "cores": sample.threads,
+            "kind": "port", "sample": sample.describe(dt, reps)}
 
 
 def bench_reference(args, world, rank, local):
     if rank != 0:
         return
     lens_all, tps, shared, layers, _, notes = workload_spec(args.workload)
+    # each step is one pass of a bounded sample, sized so the whole run takes minutes
     budget = max(0.05, min(args.cpu_seconds, 120.0 / max(1, args.steps + args.warmup)))
-    # each step is one bounded sample; value is the mean over the timed steps
-    sys.path.insert(0, str(ROOT / "oracle"))
-    results = []
-    for i in range(args.warmup + args.steps):
-        r = cpu_baseline(args.workload, lens_all, budget, sample_steps=1)
-        if i >= args.warmup:
-            results.append(r)
-    value = statistics.mean(r["value"] for r in results)
-    cpu = dict(results[-1])
-    cpu["value"] = round(value, 4)
+    sample = CpuSample(args.workload, lens_all, budget)
+    for _ in range(args.warmup):
+        sample.once()
+    times = [sample.once() for _ in range(args.steps)]
+    dt = statistics.mean(times)
+    value = sample.seqs_per_s(dt)
+    cpu = {"value": round(value, 4), "unit": "seqs/s", "cores": sample.threads, "kind": "port",
+           "sample": sample.describe(dt, len(times))}
     total_seqs = len(lens_all) * (tps if shared else 1)
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "seqs/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -563,13 +601,21 @@ def main() -> int:
                     help="launch each layer call as a programmatic dependent of the previous one")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
+    ap.add_argument("--profile-steps", type=int, default=0,
+                    help="run this many eager steps for a profiler and exit")
+    ap.add_argument("--max-seqs", type=int, default=0,
+                    help="profile mode: a length-spread subset of the workload's sequences")
+    ap.add_argument("--mem-fraction", type=float, default=0.5,
+                    help="profile mode: share of free HBM for the cache pools")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     world, rank, local = dist_env()
     if args.gpus != world and world > 1:
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
-    if args.impl == "reference":
+    if args.profile_steps > 0:
+        bench_profile(args)
+    elif args.impl == "reference":
         bench_reference(args, world, rank, local)
     else:
         bench_ours(args, world, rank, local)
