@@ -54,6 +54,7 @@ constexpr int kConsumerWarps = 4;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;  // + one producer warp
 constexpr int kChunk = 16;                           // cache rows per pipeline stage (MMA M)
 constexpr int kMaxSub = 16;                          // new tokens a CTA can substitute
+constexpr int kTab = 64;                             // block ids staged per producer window
 constexpr long long kWaitLimitCycles = 500000000LL;  // ~0.25 s at 1.9 GHz, then give up
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -430,6 +431,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
   __shared__ int s_len[kMaxSub], s_phys[kMaxSub];
   __shared__ long long s_coff[kMaxSub], s_toff[kMaxSub];
   __shared__ int s_grouped, s_last;
+  __shared__ int s_tab[kTab];  // block ids of the producer's current window
   __shared__ CtaInfo s_ci;
   __shared__ float s_wm[kConsumerWarps][ROWS], s_wl[kConsumerWarps][ROWS];
 
@@ -571,22 +573,68 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
     // (two, K then V, when V does not directly follow K in memory): 16 rows from row 0 of
     // the chunk, all 64-dim quarters of each row, at (KV head, block).  Rows of the box
     // outside the attended range are read too and zeroed by the consumer.
-    // Copy path (cache offsets that are not whole blocks): every lane copies 16-byte
-    // pieces with cp.async into the same swizzled layout, zero-filling rows outside
-    // [lo, hi); completion reaches full[stage] through one cp.async.mbarrier.arrive per
-    // lane, plus lane 0's arrive after publishing the block id.
+    const int b_first = div_p2(cb, CPB, p.cpb_shift);
+    const int b_last = div_p2(ce - 1, CPB, p.cpb_shift);
+    const int32_t* table = p.table + toff;
+    const uint64_t policy = l2_evict_first_policy();
+    if (use_tma) {
+      // Block ids of this CTA's range go to shared memory (kTab per refill), then one lane
+      // runs a lean issue loop: per chunk at most one wait (none on a stage's first use),
+      // one shared load, the stage's block id for the consumer, one arm, one copy.
+      for (int k = lane; k < kTab && b_first + k <= b_last; k += 32) s_tab[k] = table[b_first + k];
+      __syncwarp();
+      if (lane == 0) {
+        const int cpb_shift = p.cpb_shift, tm_mode = p.tm_mode;
+        const long long ncb = p.ncache_blocks;
+        const CUtensorMap* mk = &p.tmk;
+        const CUtensorMap* mv = &p.tmv;
+        const int head = kvh;
+        int tabbase = b_first;
+        for (int i = 0; i < nchunks; ++i) {
+          const int stage = i % NS;
+          if (i >= NS && !mbar_wait(empty_bar(stage), ((i / NS) & 1) ^ 1)) {
+            record_error(p.err, DORY_DEVERR_WAIT_TIMEOUT);
+            break;
+          }
+          const int c = cb + i;
+          const int blk = div_p2(c, CPB, cpb_shift);
+          if (blk - tabbase >= kTab) {  // next window of block ids (independent loads)
+            tabbase += kTab;
+#pragma unroll 8
+            for (int k = 0; k < kTab; ++k)
+              if (tabbase + k <= b_last) s_tab[k] = table[tabbase + k];
+          }
+          const int phys = s_tab[blk - tabbase];
+          const bool phys_ok = phys >= 0 && (ncb <= 0 || phys < ncb);
+          const uint32_t kt = smem_u32(smem + L::kStages + stage * L::kStageBytes);
+          meta[stage] = make_int4(phys_ok ? phys : -1, 0, c, 0);
+          if (phys_ok) {
+            mbar_arrive_expect_tx(full_bar(stage), L::kStageBytes);
+            const int row0 = mod_p2(c, CPB, cpb_shift) * kChunk;
+            const int blkc = int(coff_blocks + phys);
+            tma_load_5d(kt, mk, 0, row0, 0, head, blkc, full_bar(stage), policy);
+            if (tm_mode == 2) tma_load_5d(kt + TILE, mv, 0, row0, 0, head, blkc, full_bar(stage), policy);
+          } else {
+            record_error(p.err, DORY_DEVERR_BLOCK_OOB);
+            mbar_arrive(full_bar(stage));  // nothing to load; the consumer zeroes the tile
+          }
+        }
+      }
+      __syncwarp();
+      grid_launch_dependents();
+      return;
+    }
+    // Copy path: every lane copies 16-byte pieces with cp.async into the same swizzled
+    // layout, zero-filling rows outside [lo, hi); completion reaches full[stage] through one
+    // cp.async.mbarrier.arrive per lane, plus lane 0's arrive after publishing the block id.
     const __nv_bfloat16* kbase = p.kc + coff + int64_t(kvh) * p.sh;
     const __nv_bfloat16* vbase = p.vc + coff + int64_t(kvh) * p.sh;
-    const int32_t* table = p.table + toff;
     constexpr int VEC = HD / 8;                    // 16-byte pieces per row
     constexpr int PER_LANE = 2 * kChunk * VEC / 32;
     // Block-table window of 32 entries, prefetched one window ahead.
-    const int b_first = div_p2(cb, CPB, p.cpb_shift);
-    const int b_last = div_p2(ce - 1, CPB, p.cpb_shift);
     int wbase = b_first;
     int win_cur = (b_first + lane <= b_last) ? table[b_first + lane] : -1;
     int win_nxt = (b_first + 32 + lane <= b_last) ? table[b_first + 32 + lane] : -1;
-    const uint64_t policy = l2_evict_first_policy();
     int issued = 0;
     for (int i = 0; i < nchunks; ++i) {
       const int stage = i % NS;
@@ -608,49 +656,32 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
       if (!phys_ok && lane == 0 && offset_ok) record_error(p.err, DORY_DEVERR_BLOCK_OOB);
       const uint32_t kt = smem_u32(smem + L::kStages + stage * L::kStageBytes);
       const uint32_t vt = kt + TILE;
-      if (use_tma) {
-        if (lane == 0) {
-          meta[stage] = make_int4(phys_ok ? phys : -1, 0, c, 0);
-          if (phys_ok) {
-            mbar_arrive_expect_tx(full_bar(stage), L::kStageBytes);
-            const int row0 = mod_p2(c, CPB, p.cpb_shift) * kChunk;
-            const int blkc = int(coff_blocks + phys);
-            tma_load_5d(kt, &p.tmk, 0, row0, 0, kvh, blkc, full_bar(stage), policy);
-            if (p.tm_mode == 2) tma_load_5d(vt, &p.tmv, 0, row0, 0, kvh, blkc, full_bar(stage), policy);
-          } else {
-            mbar_arrive(full_bar(stage));  // nothing to load; the consumer zeroes the tile
-          }
-        }
-      } else {
-        const int64_t block_off = int64_t(phys_ok ? phys : 0) * p.sb +
-                                  int64_t(mod_p2(c, CPB, p.cpb_shift) * kChunk) * p.so;
+      const int64_t block_off = int64_t(phys_ok ? phys : 0) * p.sb +
+                                int64_t(mod_p2(c, CPB, p.cpb_shift) * kChunk) * p.so;
 #pragma unroll
-        for (int k = 0; k < PER_LANE; ++k) {
-          const int j = k * 32 + lane;
-          const bool is_v = j >= kChunk * VEC;
-          const int jj = is_v ? j - kChunk * VEC : j;
-          const int r = jj / VEC, w = jj % VEC;
-          const int pos = c * kChunk + r;
-          const bool valid = phys_ok && pos >= lo && pos < hi;
-          const __nv_bfloat16* src =
-              valid ? (is_v ? vbase : kbase) + block_off + int64_t(r) * p.so + w * 8 : p.kc;
-          cp_async_16((is_v ? vt : kt) + tile_off(r, w * 8), src, valid ? 16u : 0u, policy);
-        }
-        cp_async_arrive_noinc(full_bar(stage));
-        if (lane == 0) {
-          meta[stage] = make_int4(phys_ok ? phys : -1, 0, c, 0);
-          mbar_arrive(full_bar(stage));
-        }
+      for (int k = 0; k < PER_LANE; ++k) {
+        const int j = k * 32 + lane;
+        const bool is_v = j >= kChunk * VEC;
+        const int jj = is_v ? j - kChunk * VEC : j;
+        const int r = jj / VEC, w = jj % VEC;
+        const int pos = c * kChunk + r;
+        const bool valid = phys_ok && pos >= lo && pos < hi;
+        const __nv_bfloat16* src =
+            valid ? (is_v ? vbase : kbase) + block_off + int64_t(r) * p.so + w * 8 : p.kc;
+        cp_async_16((is_v ? vt : kt) + tile_off(r, w * 8), src, valid ? 16u : 0u, policy);
+      }
+      cp_async_arrive_noinc(full_bar(stage));
+      if (lane == 0) {
+        meta[stage] = make_int4(phys_ok ? phys : -1, 0, c, 0);
+        mbar_arrive(full_bar(stage));
       }
       ++issued;
     }
     grid_launch_dependents();
-    if (!use_tma) {
-      // Stay until this warp's copies have landed (bounded), then leave.
-      for (int s = 0; s < NS && s < issued; ++s) {
-        const int last = s + ((issued - 1 - s) / NS) * NS;
-        mbar_wait(full_bar(s), (last / NS) & 1);
-      }
+    // Stay until this warp's copies have landed (bounded), then leave.
+    for (int s = 0; s < NS && s < issued; ++s) {
+      const int last = s + ((issued - 1 - s) / NS) * NS;
+      mbar_wait(full_bar(s), (last / NS) & 1);
     }
     return;
   }
