@@ -357,7 +357,8 @@ def bench_ours(args, world, rank, local):
     per_launch_bytes = wl.algorithmic_bytes_per_application()
     launch_us = ms_local * 1e3 / (args.steps * apps)
     achieved = per_launch_bytes / (launch_us * 1e-6) / 1e9
-    traffic = read_traffic(args.workload)
+    ratio = read_traffic_ratio(args.workload)
+    traffic = int(ratio * per_launch_bytes) if ratio else None
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks[0],
                 "unit": "GB/s", "frac": round(achieved / peaks[0], 4),
                 "traffic": traffic, "peak_source": peaks[1],
@@ -469,15 +470,16 @@ def load_peaks():
         return 6650.0, "fallback (6.65 TB/s earlier pool measurement)"
 
 
-def read_traffic(workload: str):
-    """DRAM bytes per launch from the committed ncu summary of this workload, if any."""
+def read_traffic_ratio(workload: str):
+    """DRAM traffic / algorithmic bytes of one launch, from the committed ncu summary of this
+    workload (profiles/decode_kernel_<workload>.txt), or None."""
     path = ROOT / "profiles" / f"decode_kernel_{workload}.txt"
     if not path.exists():
         return None
     for line in path.read_text().splitlines():
-        if line.startswith("traffic_bytes_per_launch:"):
+        if line.startswith("traffic_ratio:"):
             try:
-                return int(float(line.split(":", 1)[1].strip()))
+                return float(line.split(":", 1)[1].strip())
             except ValueError:
                 return None
     return None

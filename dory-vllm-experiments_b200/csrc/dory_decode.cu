@@ -54,7 +54,7 @@ constexpr int kConsumerWarps = 4;
 constexpr int kThreads = (kConsumerWarps + 1) * 32;  // + one producer warp
 constexpr int kChunk = 16;                           // cache rows per pipeline stage (MMA M)
 constexpr int kMaxSub = 16;                          // new tokens a CTA can substitute
-constexpr int kTab = 64;                             // block ids staged per producer window
+constexpr int kTab = 512;                            // block ids of a CTA's range kept in smem
 constexpr long long kWaitLimitCycles = 500000000LL;  // ~0.25 s at 1.9 GHz, then give up
 constexpr float kLog2e = 1.4426950408889634f;
 
@@ -431,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
   __shared__ int s_len[kMaxSub], s_phys[kMaxSub];
   __shared__ long long s_coff[kMaxSub], s_toff[kMaxSub];
   __shared__ int s_grouped, s_last;
-  __shared__ int s_tab[kTab];  // block ids of the producer's current window
+  __shared__ int s_tab[kTab];  // block ids of the first kTab blocks of this CTA's range
   __shared__ CtaInfo s_ci;
   __shared__ float s_wm[kConsumerWarps][ROWS], s_wl[kConsumerWarps][ROWS];
 
@@ -551,6 +551,9 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
   __nv_bfloat16* subkv = reinterpret_cast<__nv_bfloat16*>(smem + L::kSub);
 
   const bool offset_ok = (coff & 7) == 0;
+  const int b_first = div_p2(cb, CPB, p.cpb_shift);
+  const int b_last = div_p2(ce - 1, CPB, p.cpb_shift);
+  const int32_t* table = p.table + toff;
   // Tensor copies address the cache by block index, so an offset must be whole blocks.
   const long long coff_blocks = coff == 0 ? 0 : (coff % p.sb == 0 ? coff / p.sb : -1);
   const bool use_tma = p.tm_mode != 0 && offset_ok && coff_blocks >= 0 &&
@@ -566,6 +569,30 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
   }
   __syncthreads();
 
+  const uint64_t policy = l2_evict_first_policy();
+  // Tensor path: arm the chunk's stage and copy its K (and V) tile; one thread.  Records the
+  // stage's block id (-1 for an id outside the cache) and chunk index for the consumer.
+  auto issue_chunk = [&](int i) {
+    const int stage = i % NS;
+    const int c = cb + i;
+    const int blk = div_p2(c, CPB, p.cpb_shift);
+    const int phys = blk - b_first < kTab ? s_tab[blk - b_first] : table[blk];
+    const bool phys_ok = phys >= 0 && (p.ncache_blocks <= 0 || phys < p.ncache_blocks);
+    meta[stage] = make_int4(phys_ok ? phys : -1, 0, c, 0);
+    if (phys_ok) {
+      mbar_arrive_expect_tx(full_bar(stage), L::kStageBytes);
+      const uint32_t kt = smem_u32(smem + L::kStages + stage * L::kStageBytes);
+      const int row0 = mod_p2(c, CPB, p.cpb_shift) * kChunk;
+      const int blkc = int(coff_blocks + phys);
+      tma_load_5d(kt, &p.tmk, 0, row0, 0, kvh, blkc, full_bar(stage), policy);
+      if (p.tm_mode == 2)
+        tma_load_5d(kt + TILE, &p.tmv, 0, row0, 0, kvh, blkc, full_bar(stage), policy);
+    } else {
+      record_error(p.err, DORY_DEVERR_BLOCK_OOB);
+      mbar_arrive(full_bar(stage));  // nothing to load; the consumer zeroes the tile
+    }
+  };
+
   if (warp == kConsumerWarps) {
     // =============================== producer warp ===============================
     // Tensor path (the usual one): lane 0 publishes the stage's block id, arms full[stage]
@@ -573,53 +600,15 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
     // (two, K then V, when V does not directly follow K in memory): 16 rows from row 0 of
     // the chunk, all 64-dim quarters of each row, at (KV head, block).  Rows of the box
     // outside the attended range are read too and zeroed by the consumer.
-    const int b_first = div_p2(cb, CPB, p.cpb_shift);
-    const int b_last = div_p2(ce - 1, CPB, p.cpb_shift);
-    const int32_t* table = p.table + toff;
-    const uint64_t policy = l2_evict_first_policy();
     if (use_tma) {
-      // Block ids of this CTA's range go to shared memory (kTab per refill), then one lane
-      // runs a lean issue loop: per chunk at most one wait (none on a stage's first use),
-      // one shared load, the stage's block id for the consumer, one arm, one copy.
+      // The block ids of this CTA's range go to shared memory; lane 0 then issues the first
+      // ring's worth of chunks.  From there on each consumer warp refills the stage it has
+      // just finished (stages map to fixed warps), so no producer hand-off sits between a
+      // stage falling free and its next copy.
       for (int k = lane; k < kTab && b_first + k <= b_last; k += 32) s_tab[k] = table[b_first + k];
       __syncwarp();
-      if (lane == 0) {
-        const int cpb_shift = p.cpb_shift, tm_mode = p.tm_mode;
-        const long long ncb = p.ncache_blocks;
-        const CUtensorMap* mk = &p.tmk;
-        const CUtensorMap* mv = &p.tmv;
-        const int head = kvh;
-        int tabbase = b_first;
-        for (int i = 0; i < nchunks; ++i) {
-          const int stage = i % NS;
-          if (i >= NS && !mbar_wait(empty_bar(stage), ((i / NS) & 1) ^ 1)) {
-            record_error(p.err, DORY_DEVERR_WAIT_TIMEOUT);
-            break;
-          }
-          const int c = cb + i;
-          const int blk = div_p2(c, CPB, cpb_shift);
-          if (blk - tabbase >= kTab) {  // next window of block ids (independent loads)
-            tabbase += kTab;
-#pragma unroll 8
-            for (int k = 0; k < kTab; ++k)
-              if (tabbase + k <= b_last) s_tab[k] = table[tabbase + k];
-          }
-          const int phys = s_tab[blk - tabbase];
-          const bool phys_ok = phys >= 0 && (ncb <= 0 || phys < ncb);
-          const uint32_t kt = smem_u32(smem + L::kStages + stage * L::kStageBytes);
-          meta[stage] = make_int4(phys_ok ? phys : -1, 0, c, 0);
-          if (phys_ok) {
-            mbar_arrive_expect_tx(full_bar(stage), L::kStageBytes);
-            const int row0 = mod_p2(c, CPB, cpb_shift) * kChunk;
-            const int blkc = int(coff_blocks + phys);
-            tma_load_5d(kt, mk, 0, row0, 0, head, blkc, full_bar(stage), policy);
-            if (tm_mode == 2) tma_load_5d(kt + TILE, mv, 0, row0, 0, head, blkc, full_bar(stage), policy);
-          } else {
-            record_error(p.err, DORY_DEVERR_BLOCK_OOB);
-            mbar_arrive(full_bar(stage));  // nothing to load; the consumer zeroes the tile
-          }
-        }
-      }
+      if (lane == 0)
+        for (int i = 0; i < NS && i < nchunks; ++i) issue_chunk(i);
       __syncwarp();
       grid_launch_dependents();
       return;
@@ -901,9 +890,16 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
         for (int nt = 0; nt < NT; ++nt) mma_bf16(o[nt][kk], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
       }
     }
-    if (touched) fence_proxy_async_smem();  // before tensor copies refill the stage
-    __syncwarp();
-    if (lane == 0) mbar_arrive(empty_bar(stage));
+    if (use_tma) {
+      // This warp's reads (and writes) of the stage, ordered before the copy that refills it.
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && i + NS < nchunks) issue_chunk(i + NS);
+    } else {
+      if (touched) fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(empty_bar(stage));
+    }
   }
 
   // Row sums: lanes with equal t4 hold disjoint token subsets of the same rows.
@@ -1136,12 +1132,13 @@ int32_t launch(const KParams& kp, dim3 grid, int smem_bytes, cudaStream_t stream
   return DORY_OK;
 }
 
-// Ring stages per instantiation: 32 KB of ring for one query tile (so ~5 CTAs fit an SM
-// and their latency phases overlap), 64 KB for two tiles (whose merge buffer needs it).
-// A multiple of the four consumer warps, so every stage keeps one consumer.
+// Ring stages per instantiation: a multiple of the four consumer warps, so every stage keeps
+// one consumer, which refills it; two stages per warp (64 KB of ring for 128-dim heads) let
+// each warp compute one chunk while its next one is in flight.  256-dim heads keep one
+// stage per warp (64 KB as well).
 template <int HD, int NT>
 struct Depth {
-  static constexpr int value = HD == 64 ? 8 : (HD == 128 ? (NT == 1 ? 4 : 8) : 4);
+  static constexpr int value = HD == 256 ? 4 : 8;
 };
 
 // Largest split count whose merge tables ((max, sum) and weight per split and row) fit in
