@@ -416,7 +416,7 @@ __device__ __forceinline__ bool fixup_stage(const KParams& p, uint8_t* kst, uint
 // The kernel.  grid = (splits, NKV, T); block = 160 threads (4 consumer warps + producer).
 // ------------------------------------------------------------------------------------
 template <int HD, int NT, int NS>
-__global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 4 : 1)
+__global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     decode_kernel(const __grid_constant__ KParams p) {
   using L = Smem<HD, NS>;
   constexpr int KT = HD / 16;          // MMA k-steps over head_dim / m-tiles of O^T
