@@ -413,6 +413,83 @@ __device__ __forceinline__ bool fixup_stage(const KParams& p, uint8_t* kst, uint
 }
 
 // ------------------------------------------------------------------------------------
+// Cross-split merge of one (token group, KV head) by its last CTA: thread tid owns output
+// units tid + k * 128 (k < UPT), a unit being 4 consecutive dims of one query row.
+// ------------------------------------------------------------------------------------
+template <int HD, int UPT, int SB>
+__device__ __forceinline__ void merge_splits(const KParams& p, int tid, int nrows, int gstart,
+                                             int kvh, int G, int active) {
+  constexpr int UPR = HD / 4;  // float4 units per row
+  constexpr int NTHR = kConsumerWarps * 32;
+  const int Q = p.NH * HD;
+  const int64_t S = p.S;
+  const int units = nrows * UPR;
+  const int64_t ostride = int64_t(p.NH) * UPR;  // float4s between consecutive splits
+  const float4* osrc[UPT];
+  const float2* ssrc[UPT];
+  float4 acc[UPT], gt[UPT];
+  float Mx[UPT], Ls[UPT];
+#pragma unroll
+  for (int k = 0; k < UPT; ++k) {
+    const int u = tid + k * NTHR;
+    const int r = u < units ? u / UPR : 0, d4 = u % UPR;
+    const int t = gstart + r / G, head = kvh * G + r % G;
+    osrc[k] = reinterpret_cast<const float4*>(p.po) + ((int64_t(t) * S) * p.NH + head) * UPR + d4;
+    ssrc[k] = p.pml + (int64_t(t) * S) * p.NH + head;
+    acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    Mx[k] = -INFINITY;
+    Ls[k] = 0.0f;
+    gt[k] = u < units ? *reinterpret_cast<const float4*>(p.gate + int64_t(t) * Q + head * HD + d4 * 4)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int s0 = 0; s0 < active; s0 += SB) {
+    float4 v[UPT][SB];
+    float2 st[UPT][SB];
+#pragma unroll
+    for (int k = 0; k < UPT; ++k)
+#pragma unroll
+      for (int j = 0; j < SB; ++j) {
+        const bool ok = tid + k * NTHR < units && s0 + j < active;
+        v[k][j] = ok ? __ldcg(osrc[k] + (s0 + j) * ostride) : make_float4(0.f, 0.f, 0.f, 0.f);
+        st[k][j] = ok ? __ldcg(ssrc[k] + (s0 + j) * p.NH) : make_float2(-INFINITY, 0.f);
+      }
+#pragma unroll
+    for (int k = 0; k < UPT; ++k) {
+      float mb = Mx[k];
+#pragma unroll
+      for (int j = 0; j < SB; ++j) mb = fmaxf(mb, st[k][j].x);
+      const float mu = (mb == -INFINITY) ? 0.0f : mb;
+      const float wa = fast_exp2(Mx[k] - mu);
+      float lsum = Ls[k] * wa;
+      float4 a = make_float4(acc[k].x * wa, acc[k].y * wa, acc[k].z * wa, acc[k].w * wa);
+#pragma unroll
+      for (int j = 0; j < SB; ++j) {
+        const float w = fast_exp2(st[k][j].x - mu);
+        lsum += st[k][j].y * w;
+        a.x += v[k][j].x * w; a.y += v[k][j].y * w; a.z += v[k][j].z * w; a.w += v[k][j].w * w;
+      }
+      acc[k] = a;
+      Ls[k] = lsum;
+      Mx[k] = mb;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < UPT; ++k) {
+    const int u = tid + k * NTHR;
+    if (u >= units) continue;
+    const int r = u / UPR, d4 = u % UPR;
+    const int t = gstart + r / G, head = kvh * G + r % G;
+    const float inv = 1.0f / (Ls[k] > 0.0f ? Ls[k] : 1.0f);
+    const int e0 = head * HD + d4 * 4;  // 4 consecutive elements: same e / 8, e % 8 = j0..j0+3
+    float* out = p.out + int64_t(t) * Q + (e0 % 8) * (Q / 8) + e0 / 8;
+    out[0] = acc[k].x * inv * gt[k].x;
+    out[Q / 8] = acc[k].y * inv * gt[k].y;
+    out[2 * (Q / 8)] = acc[k].z * inv * gt[k].z;
+    out[3 * (Q / 8)] = acc[k].w * inv * gt[k].w;
+  }
+}
+
+// ------------------------------------------------------------------------------------
 // The kernel.  grid = (splits, NKV, T); block = 160 threads (4 consumer warps + producer).
 // ------------------------------------------------------------------------------------
 template <int HD, int NT, int NS>
@@ -993,99 +1070,28 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   if (single) return;
 
   // ---- cross-split merge by the last CTA of this (group, KV head) to arrive ----
-  __threadfence();
+  // The barrier orders every consumer thread's partial stores before thread 0's release
+  // add (release is cumulative); its acquire, passed on by the second barrier, makes the
+  // other CTAs' partials visible to this CTA when it is the last.
   named_barrier_consumers();
   if (tid == 0) {
     int32_t* counter = p.counters + gstart * p.NKV + kvh;
-    const int prev = atomicAdd(counter, 1);
+    int prev;
+    asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(prev) : "l"(counter) : "memory");
     s_last = (prev == sp.active - 1);
     if (s_last) *counter = 0;  // self-reset for the next launch
   }
   named_barrier_consumers();
   if (!s_last) return;
-  __threadfence();
-  // Three phases, so that no thread waits on one L2 round trip per split:
-  //  (a) every split's (max, sum) of every row into shared memory, all loads in flight;
-  //  (b) per row, the merged max, each split's weight and 1 / total, one warp per row;
-  //  (c) per (row, 4 dims), the weighted sum over splits, 16 loads in flight per thread.
-  const int active = sp.active;
-  float2* s_stat = reinterpret_cast<float2*>(smem + L::kStages);      // [active][ROWS]
-  float* s_wt = reinterpret_cast<float*>(s_stat + active * ROWS);      // [active][ROWS]
-  float* s_inv = s_wt + active * ROWS;                                  // [ROWS]
-  for (int i = tid; i < active * nrows; i += kConsumerWarps * 32) {
-    const int sidx = i / nrows, r = i % nrows;
-    const int t = gstart + r / G, head = kvh * G + r % G;
-    s_stat[sidx * ROWS + r] = __ldcg(p.pml + (int64_t(t) * S + sidx) * p.NH + head);
-  }
-  named_barrier_consumers();
-  for (int r = warp; r < nrows; r += kConsumerWarps) {
-    float M = -INFINITY;
-    for (int sidx = lane; sidx < active; sidx += 32) M = fmaxf(M, s_stat[sidx * ROWS + r].x);
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, off));
-    const float Mu = (M == -INFINITY) ? 0.0f : M;
-    float Lsum = 0.0f;
-    for (int sidx = lane; sidx < active; sidx += 32) {
-      const float2 st = s_stat[sidx * ROWS + r];
-      const float w = fast_exp2(st.x - Mu);
-      s_wt[sidx * ROWS + r] = w;
-      Lsum += w * st.y;
-    }
-#pragma unroll
-    for (int off = 16; off > 0; off >>= 1) Lsum += __shfl_xor_sync(0xffffffffu, Lsum, off);
-    if (lane == 0) s_inv[r] = 1.0f / (Lsum > 0.0f ? Lsum : 1.0f);
-  }
-  named_barrier_consumers();
-  constexpr int UPR = HD / 4;  // float4 units per row
-  constexpr int NTHR = kConsumerWarps * 32;
-  constexpr int UPT = (ROWS * UPR + NTHR - 1) / NTHR;  // units per thread (at most)
-  constexpr int SB = UPT >= 4 ? 4 : 16 / UPT;         // splits per batch: 16 loads in flight
-  const int64_t sstride = int64_t(p.NH) * UPR;         // float4s between consecutive splits
-  const int units = nrows * UPR;
-  const float4* srcs[UPT];
-  float4 acc[UPT];
-  int rowu[UPT];
-#pragma unroll
-  for (int k = 0; k < UPT; ++k) {
-    const int u = tid + k * NTHR;
-    const int r = u < units ? u / UPR : 0, d4 = u % UPR;
-    const int t = gstart + r / G, head = kvh * G + r % G;
-    srcs[k] = reinterpret_cast<const float4*>(p.po) + ((int64_t(t) * S) * p.NH + head) * UPR + d4;
-    rowu[k] = r;
-    acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  for (int s0 = 0; s0 < active; s0 += SB) {
-    float4 v[UPT][SB];
-#pragma unroll
-    for (int k = 0; k < UPT; ++k)
-#pragma unroll
-      for (int j = 0; j < SB; ++j)
-        v[k][j] = (tid + k * NTHR < units && s0 + j < active) ? __ldcg(srcs[k] + (s0 + j) * sstride)
-                                                             : make_float4(0.f, 0.f, 0.f, 0.f);
-#pragma unroll
-    for (int k = 0; k < UPT; ++k)
-#pragma unroll
-      for (int j = 0; j < SB; ++j) {
-        const float w = s0 + j < active ? s_wt[(s0 + j) * ROWS + rowu[k]] : 0.0f;
-        acc[k].x += w * v[k][j].x; acc[k].y += w * v[k][j].y;
-        acc[k].z += w * v[k][j].z; acc[k].w += w * v[k][j].w;
-      }
-  }
-#pragma unroll
-  for (int k = 0; k < UPT; ++k) {
-    const int u = tid + k * NTHR;
-    if (u >= units) continue;
-    const int r = u / UPR, d4 = u % UPR;
-    const int t = gstart + r / G, head = kvh * G + r % G;
-    const float inv = s_inv[r];
-    const int e0 = head * HD + d4 * 4;  // 4 consecutive elements: same e / 8, e % 8 = j0..j0+3
-    const float4 gt = *reinterpret_cast<const float4*>(p.gate + int64_t(t) * Q + e0);
-    float* out = p.out + int64_t(t) * Q + (e0 % 8) * (Q / 8) + e0 / 8;
-    out[0] = acc[k].x * inv * gt.x;
-    out[Q / 8] = acc[k].y * inv * gt.y;
-    out[2 * (Q / 8)] = acc[k].z * inv * gt.z;
-    out[3 * (Q / 8)] = acc[k].w * inv * gt.w;
-  }
+  // Merge over the splits in registers, per (row, 4 dims) unit: batches of SB splits whose
+  // (max, sum) and partial outputs are all in flight together (one L2 round trip per
+  // batch; the gate rides along the first), each batch folded in with one max, independent
+  // weights and one rescale.
+  if (nrows * (HD / 4) <= kConsumerWarps * 32)
+    merge_splits<HD, 1, 16>(p, tid, nrows, gstart, kvh, G, sp.active);
+  else
+    merge_splits<HD, (ROWS * HD / 4 + kConsumerWarps * 32 - 1) / (kConsumerWarps * 32), 4>(
+        p, tid, nrows, gstart, kvh, G, sp.active);
 }
 
 // ------------------------------------------------------------------------------------
@@ -1141,21 +1147,11 @@ struct Depth {
   static constexpr int value = HD == 256 ? 4 : 8;
 };
 
-// Largest split count whose merge tables ((max, sum) and weight per split and row) fit in
-// the drained ring of one CTA.
-template <int HD, int NS>
-constexpr int max_splits(int rows) {
-  return (NS * Smem<HD, NS>::kStageBytes - rows * 4) / (rows * 12);
-}
-
 template <int HD, int NT>
 int32_t dispatch(const KParams& kp, dim3 grid, cudaStream_t stream) {
   constexpr int NS = Depth<HD, NT>::value;
   static_assert(kConsumerWarps * NT * 8 * (HD + 4) * 4 <= NS * Smem<HD, NS>::kStageBytes,
                 "the warps' merge buffer must fit in the ring");
-  if (kp.S > max_splits<HD, NS>(NT * 8))
-    return fail(DORY_ERR_UNSUPPORTED, "splits %d > %d for head_dim %d", kp.S,
-                max_splits<HD, NS>(NT * 8), HD);
   return launch<HD, NT, NS>(kp, grid, Smem<HD, NS>::bytes(kp.nsub), stream);
 }
 
@@ -1321,9 +1317,10 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
                 (long long)a.scratch_bytes, (long long)SL.total);
   if (a.num_tokens == 0) return DORY_OK;
 
-  // Query rows per tile: one token's group, or up to 16 rows of shared-cache tokens.
-  int rows = shared ? (a.num_tokens * G < 16 ? a.num_tokens * G : 16) : G;
-  int nt = rows > 8 ? 2 : 1;
+  // One 8-row tile per CTA unless one KV head's group alone needs more rows: a shared-cache
+  // wavefront then runs as groups of 8 / G tokens whose reads of the same blocks meet in L2,
+  // which measured faster than 16-row tiles (twice the math and merge per CTA).
+  int nt = G > 8 ? 2 : 1;
   if (HD == 256 && nt == 2) {
     if (G > 8) return fail(DORY_ERR_UNSUPPORTED, "head_dim 256 with more than 8 heads per KV head");
     nt = 1;
