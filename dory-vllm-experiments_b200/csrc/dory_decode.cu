@@ -267,17 +267,12 @@ __device__ __forceinline__ float load_sqk(const void* sqk, int dtype, int64_t i)
 }
 
 // Canonical normalisation factor of one row: Sum x^2 is accumulated in FP64 (every square
-// is exact there, so the FP32 rounding of the sum does not depend on summation order),
+// is exact there and the sum carries 29 more bits than FP32, so its FP32 rounding depends on
+// the summation order only when the sum lies within ~2^-53 of an FP32 rounding boundary),
 // rounded to FP32, eps is added in FP32 (as the reference's `tl.sum(x * x) + eps`) and the
-// inverse square root is the correctly rounded FP32 value, from IEEE double sqrt and
-// division.  The oracle computes the same quantities the same way.
-template <int PER_LANE>
-__device__ __forceinline__ float row_inv_norm(const float (&x)[PER_LANE], float eps) {
-  double acc = 0.0;
-#pragma unroll
-  for (int i = 0; i < PER_LANE; ++i) acc += double(x[i]) * double(x[i]);
-#pragma unroll
-  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+// inverse square root is the correctly rounded FP32 value.  The oracle computes the same
+// quantities the same way.
+__device__ __forceinline__ float inv_norm_from_sum(double acc, float eps) {
   const float sum32 = __double2float_rn(acc);
   const float t = __fadd_rn(sum32, eps);
   // 1 / sqrt(t), correctly rounded to FP32: the FP32 estimate refined by two Newton-Raphson
@@ -288,6 +283,16 @@ __device__ __forceinline__ float row_inv_norm(const float (&x)[PER_LANE], float 
   y = y * (1.5 - 0.5 * td * y * y);
   y = y * (1.5 - 0.5 * td * y * y);
   return __double2float_rn(y);
+}
+// One row spread over the 32 lanes of a warp, PER_LANE elements each.
+template <int PER_LANE>
+__device__ __forceinline__ float row_inv_norm(const float (&x)[PER_LANE], float eps) {
+  double acc = 0.0;
+#pragma unroll
+  for (int i = 0; i < PER_LANE; ++i) acc += double(x[i]) * double(x[i]);
+#pragma unroll
+  for (int off = 16; off > 0; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  return inv_norm_from_sum(acc, eps);
 }
 
 // x / d and x % d for x >= 0, by shifting when d is a power of two (shift >= 0).
@@ -903,10 +908,13 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
                                 s_toff, subkv);
     __syncwarp();
 
-    // S^T = K Q^T : [16 tokens x 8 rows] per n-tile.
-    float sc[NT][4];
+    // S^T = K Q^T : [16 tokens x 8 rows] per n-tile, as two independent MMA chains (even
+    // and odd k-steps) to halve the dependent latency.
+    float sc[NT][4], sc2[NT][4];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.0f;
+    for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[nt][e] = sc2[nt][e] = 0.0f;
     {
       const uint32_t kbase_s = smem_u32(kst);
       const int kr = lane & 15, kd = (lane >> 4) * 8;
@@ -915,8 +923,13 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
         uint32_t a0, a1, a2, a3;
         ldsm_x4(kbase_s + tile_off(kr, kk * 16 + kd), a0, a1, a2, a3);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma_bf16(sc[nt], a0, a1, a2, a3, qb[nt][kk][0], qb[nt][kk][1]);
+        for (int nt = 0; nt < NT; ++nt)
+          mma_bf16((kk & 1) ? sc2[nt] : sc[nt], a0, a1, a2, a3, qb[nt][kk][0], qb[nt][kk][1]);
       }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sc[nt][e] += sc2[nt][e];
     }
     // Online softmax (log2 domain) and P^T operands.
     const int pos0 = c * kChunk + g;
@@ -1402,8 +1415,8 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
     }
   }
 
-  dim3 grid(a.splits, a.num_kv_heads, a.num_tokens);
   cudaStream_t s = (cudaStream_t)stream;
+  dim3 grid(a.splits, a.num_kv_heads, a.num_tokens);
   if (HD == 64) return dispatch_nt<64>(kp, nt, grid, s);
   if (HD == 128) return dispatch_nt<128>(kp, nt, grid, s);
   return dispatch_nt<256>(kp, nt, grid, s);
