@@ -156,6 +156,16 @@ class ClockSampler:
 # workloads on the device
 # ---------------------------------------------------------------------------------------
 
+def tuned_splits(workload: str, world: int):
+    """(splits, min_blocks_per_split) measured fastest on B200 for each workload; config 5
+    uses 4 splits once its 512 sequences are partitioned over 2+ GPUs (fewer, longer
+    sequences per GPU: finer splits even out the last wave)."""
+    if workload == "config5":
+        return (2, 64) if world == 1 else (4, 64)
+    return {"config1": (16, 1), "config2": (16, 1), "config3": (2, 32),
+            "config4": (32, 1)}.get(workload, (2, 64))
+
+
 def workload_spec(name: str):
     """(cached context lengths, tokens per sequence, shared, layer order, pool factor, notes)."""
     if name == "config5":
@@ -597,8 +607,9 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", default="config5")
-    ap.add_argument("--splits", type=int, default=2)
-    ap.add_argument("--min-blocks-per-split", type=int, default=64)
+    ap.add_argument("--splits", type=int, default=None,
+                    help="split count (default: the tuned setting of the workload and GPU count)")
+    ap.add_argument("--min-blocks-per-split", type=int, default=None)
     ap.add_argument("--overlap-launch", action="store_true",
                     help="launch each layer call as a programmatic dependent of the previous one")
     ap.add_argument("--e2e-steps", type=int, default=10)
@@ -613,6 +624,11 @@ def main() -> int:
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     world, rank, local = dist_env()
+    tuned = tuned_splits(args.workload, world)
+    if args.splits is None:
+        args.splits = tuned[0]
+    if args.min_blocks_per_split is None:
+        args.min_blocks_per_split = tuned[1]
     if args.gpus != world and world > 1:
         print(f"warning: --gpus {args.gpus} but WORLD_SIZE {world}", file=sys.stderr)
     if args.profile_steps > 0:

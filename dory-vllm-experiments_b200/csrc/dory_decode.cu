@@ -175,7 +175,8 @@ __device__ __forceinline__ uint64_t l2_evict_first_policy() {
   uint64_t policy;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
   return policy;
-}// One box of a tensor map into shared memory, completing on `bar` (no multicast).
+}
+// One box of a tensor map into this CTA's shared memory, completing on `bar`.
 __device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
                                             int c2, int c3, int c4, uint32_t bar, uint64_t policy) {
   asm volatile(
