@@ -796,41 +796,79 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     s_ci.gcount = gcount;
     s_ci.offset_ok = offset_ok;
   }
-  // (1) query rows: normalise / scale / round, as the reference, into q2 [16][HD] bf16.
-  for (int r = warp; r < 16; r += kConsumerWarps) {
-    if (r >= nrows) {
-      for (int d = lane; d < HD; d += 32) q2[r * HD + d] = __float2bfloat16_rn(0.0f);
-      continue;
-    }
+  // (1) query rows: normalise / scale / round, as the reference, into q2 [ROWS][HD] bf16;
+  // (2) new keys / values of the sub tokens: k = bf16(k * inv_norm(k)), v = bf16(v).
+  // Every load of this warp's rows (q, sqk) and of its first sub token (k, v) is issued
+  // before any of the arithmetic: one L2 round trip, not one per dependent step.
+  constexpr int RPW = ROWS / kConsumerWarps;  // query rows per consumer warp
+  float qv[RPW][PER_LANE], sv[RPW][PER_LANE], kv0[PER_LANE], vv0[PER_LANE];
+#pragma unroll
+  for (int j = 0; j < RPW; ++j) {
+    const int r = warp + j * kConsumerWarps;
+    if (r >= nrows) continue;
     const int t = gstart + r / G;
     const int head = kvh * G + r % G;
-    float qv[PER_LANE];
     if (p.raw) {
       const float* src = static_cast<const float*>(p.q) + int64_t(t) * p.q_stride + head * HD;
 #pragma unroll
-      for (int i = 0; i < PER_LANE; ++i) qv[i] = src[lane * PER_LANE + i];
-      const float rn = row_inv_norm<PER_LANE>(qv, p.eps);
-#pragma unroll
       for (int i = 0; i < PER_LANE; ++i) {
-        const int d = lane * PER_LANE + i;
-        const float s = __fmul_rn(load_sqk(p.sqk, p.sqk_dtype, head * HD + d), p.sqk_factor);
-        const float qn = __fmul_rn(qv[i], rn);
-        const float qb = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(s, s), qn)));
-        q2[r * HD + d] = __float2bfloat16_rn(__fmul_rn(qb, p.scale));
+        qv[j][i] = src[lane * PER_LANE + i];
+        sv[j][i] = load_sqk(p.sqk, p.sqk_dtype, head * HD + lane * PER_LANE + i);
       }
     } else {
       const __nv_bfloat16* src =
           static_cast<const __nv_bfloat16*>(p.q) + int64_t(t) * p.q_stride + head * HD;
 #pragma unroll
-      for (int i = 0; i < PER_LANE; ++i) {
-        const int d = lane * PER_LANE + i;
-        q2[r * HD + d] = __float2bfloat16_rn(__fmul_rn(__bfloat162float(src[d]), p.scale));
-      }
+      for (int i = 0; i < PER_LANE; ++i) qv[j][i] = __bfloat162float(src[lane * PER_LANE + i]);
     }
   }
-  // (2) new keys / values of the sub tokens: k = bf16(k * inv_norm(k)), v = bf16(v).
+  const bool sub0 = p.raw && warp < nsub;
+  if (sub0) {
+    const int t = p.shared ? warp : tok;
+    const float* ksrc =
+        static_cast<const float*>(p.q) + int64_t(t) * p.q_stride + (p.NH + kvh) * HD;
+    const float* vsrc = p.v + int64_t(t) * p.NKV * HD + kvh * HD;
+#pragma unroll
+    for (int i = 0; i < PER_LANE; ++i) {
+      kv0[i] = ksrc[lane * PER_LANE + i];
+      vv0[i] = vsrc[lane * PER_LANE + i];
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < RPW; ++j) {
+    const int r = warp + j * kConsumerWarps;
+    if (r >= nrows) {
+#pragma unroll
+      for (int i = 0; i < PER_LANE; ++i) q2[r * HD + lane * PER_LANE + i] = __float2bfloat16_rn(0.0f);
+      continue;
+    }
+    if (p.raw) {
+      const float rn = row_inv_norm<PER_LANE>(qv[j], p.eps);
+#pragma unroll
+      for (int i = 0; i < PER_LANE; ++i) {
+        const float s = __fmul_rn(sv[j][i], p.sqk_factor);
+        const float qn = __fmul_rn(qv[j][i], rn);
+        const float qb = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(s, s), qn)));
+        q2[r * HD + lane * PER_LANE + i] = __float2bfloat16_rn(__fmul_rn(qb, p.scale));
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < PER_LANE; ++i)
+        q2[r * HD + lane * PER_LANE + i] = __float2bfloat16_rn(__fmul_rn(qv[j][i], p.scale));
+    }
+  }
+  if (sub0) {
+    const float rn = row_inv_norm<PER_LANE>(kv0, p.eps);
+#pragma unroll
+    for (int i = 0; i < PER_LANE; ++i) {
+      const int d = lane * PER_LANE + i;
+      subkv[(warp * 2 + 0) * HD + d] = __float2bfloat16_rn(__fmul_rn(kv0[i], rn));
+      subkv[(warp * 2 + 1) * HD + d] = __float2bfloat16_rn(vv0[i]);
+    }
+  }
+  // Further sub tokens of a shared-cache call (more than four).
   if (p.raw) {
-    for (int s = warp; s < nsub; s += kConsumerWarps) {
+    for (int s = warp + kConsumerWarps; s < nsub; s += kConsumerWarps) {
       const int t = p.shared ? s : tok;
       const float* ksrc =
           static_cast<const float*>(p.q) + int64_t(t) * p.q_stride + (p.NH + kvh) * HD;
