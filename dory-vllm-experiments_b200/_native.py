@@ -13,7 +13,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 LIBRARY = HERE / "libdory_decode.so"
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 # DoryStatus
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_ALIGNMENT, ERR_CUDA = range(5)
@@ -21,6 +21,8 @@ OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_ALIGNMENT, ERR_CUDA = range(5)
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = range(3)
 # DORY_FLAG_*
 FLAG_RAW_QKV, FLAG_MULTI_TOKEN, FLAG_SHARED_CACHE, FLAG_OVERLAP_LAUNCH = 1, 2, 4, 8
+# DORY_QKNORM_*
+QKNORM_WRITE_CACHE = 1
 # DORY_DEVERR_*
 DEVERR_BLOCK_OOB, DEVERR_SLOT_OOB, DEVERR_OFFSET_ALIGN, DEVERR_WAIT_TIMEOUT = 1, 2, 4, 8
 DEVERR_NAMES = {DEVERR_BLOCK_OOB: "block id out of range", DEVERR_SLOT_OOB: "slot out of range",
@@ -30,7 +32,8 @@ DEVERR_NAMES = {DEVERR_BLOCK_OOB: "block id out of range", DEVERR_SLOT_OOB: "slo
 # Every symbol include/dory_decode.h declares (checked by the CPU test suite).
 EXPORTS = ("dory_decode_abi_version", "dory_decode_params_bytes", "dory_decode_scratch_bytes",
            "dory_decode_scratch_init", "dory_decode_attention", "dory_decode_fetch_errors",
-           "dory_decode_last_error", "dory_decode_attention_static_scratch")
+           "dory_decode_last_error", "dory_decode_attention_static_scratch",
+           "dory_qk_norm_params_bytes", "dory_qk_norm_cache")
 
 # Size of the library's static scratch array (DORY_DECODE_STATIC_SCRATCH_BYTES).
 STATIC_SCRATCH_BYTES = 4 << 20
@@ -52,6 +55,18 @@ class DoryDecodeParams(ctypes.Structure):
         ("block_size", _i32), ("window", _i32), ("splits", _i32), ("blocks_per_tile", _i32),
         ("min_blocks_per_split", _i32), ("max_tokens", _i32), ("sqk_dtype", _i32),
         ("flags", _u32),
+    ]
+
+
+class DoryQkNormParams(ctypes.Structure):
+    """Mirror of DoryQkNormParams (include/dory_decode.h); field order is the ABI."""
+    _fields_ = [
+        ("qk", _vp), ("v", _vp), ("sqk", _vp), ("q_out", _vp), ("key_cache", _vp),
+        ("value_cache", _vp), ("slot_mapping", _vp), ("k_out", _vp), ("v_out", _vp),
+        ("error_word", _vp), ("stride_block", _i64), ("stride_offset", _i64),
+        ("stride_head", _i64), ("num_cache_blocks", _i64), ("sqk_factor", _f32), ("eps", _f32),
+        ("num_tokens", _i32), ("num_heads", _i32), ("num_kv_heads", _i32), ("head_dim", _i32),
+        ("block_size", _i32), ("sqk_dtype", _i32), ("flags", _u32),
     ]
 
 
@@ -85,11 +100,18 @@ def load(path: os.PathLike | None = None) -> ctypes.CDLL:
     lib.dory_decode_last_error.argtypes = []
     lib.dory_decode_attention_static_scratch.restype = _i32
     lib.dory_decode_attention_static_scratch.argtypes = [ctypes.POINTER(DoryDecodeParams), _vp]
+    lib.dory_qk_norm_params_bytes.restype = _i64
+    lib.dory_qk_norm_params_bytes.argtypes = []
+    lib.dory_qk_norm_cache.restype = _i32
+    lib.dory_qk_norm_cache.argtypes = [ctypes.POINTER(DoryQkNormParams), _vp]
     if lib.dory_decode_abi_version() != ABI_VERSION:
         raise RuntimeError(f"{path}: ABI version {lib.dory_decode_abi_version()} != {ABI_VERSION}")
     if lib.dory_decode_params_bytes() != ctypes.sizeof(DoryDecodeParams):
         raise RuntimeError(f"{path}: DoryDecodeParams is {lib.dory_decode_params_bytes()} bytes, "
                            f"the binding's is {ctypes.sizeof(DoryDecodeParams)}")
+    if lib.dory_qk_norm_params_bytes() != ctypes.sizeof(DoryQkNormParams):
+        raise RuntimeError(f"{path}: DoryQkNormParams is {lib.dory_qk_norm_params_bytes()} "
+                           f"bytes, the binding's is {ctypes.sizeof(DoryQkNormParams)}")
     _lib = lib
     return lib
 

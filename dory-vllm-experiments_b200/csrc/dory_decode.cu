@@ -1147,6 +1147,82 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
 }
 
 // ------------------------------------------------------------------------------------
+// Separate q/k normalisation and cache write (reference _qk_norm_cache_kernel,
+// kernels/dory_attention.py:69-96): one warp per (token, head) row; q heads give the scaled
+// bf16 query, k heads the normalised key written with the bf16 value at the token's slot (or
+// to k_out / v_out).  Every load of a row is issued before its arithmetic.
+// ------------------------------------------------------------------------------------
+struct QkNormArgs {
+  const float* qk;
+  const float* v;
+  const void* sqk;
+  __nv_bfloat16* q_out;
+  __nv_bfloat16* kc;
+  __nv_bfloat16* vc;
+  const int64_t* slot_mapping;
+  __nv_bfloat16* k_out;
+  __nv_bfloat16* v_out;
+  uint32_t* err;
+  int64_t sb, so, sh, ncache_blocks;
+  float sqk_factor, eps;
+  int NH, NKV, B, sqk_dtype, write_cache;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(128) qk_norm_kernel(const __grid_constant__ QkNormArgs a) {
+  constexpr int PL = HD / 32;  // elements per lane
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * 4 + (threadIdx.x >> 5);  // head index: q heads, then k heads
+  const int t = blockIdx.y;
+  const int heads = a.NH + a.NKV;
+  if (row >= heads) return;
+  const int d0 = lane * PL;
+  float x[PL], y[PL];
+  const float* src = a.qk + (int64_t(t) * heads + row) * HD + d0;
+#pragma unroll
+  for (int i = 0; i < PL; ++i) x[i] = src[i];
+  if (row < a.NH) {
+#pragma unroll
+    for (int i = 0; i < PL; ++i) y[i] = load_sqk(a.sqk, a.sqk_dtype, int64_t(row) * HD + d0 + i);
+    const float rn = row_inv_norm<PL>(x, a.eps);
+    __nv_bfloat16* dst = a.q_out + (int64_t(t) * a.NH + row) * HD + d0;
+#pragma unroll
+    for (int i = 0; i < PL; ++i) {
+      const float sq = __fmul_rn(y[i], a.sqk_factor);
+      dst[i] = __float2bfloat16_rn(__fmul_rn(__fmul_rn(sq, sq), __fmul_rn(x[i], rn)));
+    }
+    return;
+  }
+  const int kvh = row - a.NH;
+  const float* vsrc = a.v + (int64_t(t) * a.NKV + kvh) * HD + d0;
+#pragma unroll
+  for (int i = 0; i < PL; ++i) y[i] = vsrc[i];
+  const float rn = row_inv_norm<PL>(x, a.eps);
+  __nv_bfloat16* kd;
+  __nv_bfloat16* vd;
+  if (a.write_cache) {
+    const long long slot = a.slot_mapping[t];
+    if (slot < 0) return;  // a padding token, which vLLM does not cache
+    const long long blk = slot / a.B;
+    if (a.ncache_blocks > 0 && blk >= a.ncache_blocks) {
+      if (lane == 0 && a.err) record_error(a.err, DORY_DEVERR_SLOT_OOB);
+      return;
+    }
+    const long long base = blk * a.sb + (slot % a.B) * a.so + (long long)kvh * a.sh + d0;
+    kd = a.kc + base;
+    vd = a.vc + base;
+  } else {
+    kd = a.k_out + (int64_t(t) * a.NKV + kvh) * HD + d0;
+    vd = a.v_out + (int64_t(t) * a.NKV + kvh) * HD + d0;
+  }
+#pragma unroll
+  for (int i = 0; i < PL; ++i) {
+    kd[i] = __float2bfloat16_rn(__fmul_rn(x[i], rn));
+    vd[i] = __float2bfloat16_rn(y[i]);
+  }
+}
+
+// ------------------------------------------------------------------------------------
 // Host side
 // ------------------------------------------------------------------------------------
 thread_local char g_last_error[512] = "";
@@ -1318,6 +1394,57 @@ int32_t dory_decode_fetch_errors(void* scratch, uint32_t* flags_out, int32_t cle
 }
 
 const char* dory_decode_last_error(void) { return g_last_error; }
+
+int64_t dory_qk_norm_params_bytes(void) { return int64_t(sizeof(DoryQkNormParams)); }
+
+int32_t dory_qk_norm_cache(const DoryQkNormParams* P, void* stream) {
+  if (!P) return fail(DORY_ERR_INVALID_ARGUMENT, "null params");
+  const DoryQkNormParams& a = *P;
+  const bool write_cache = a.flags & DORY_QKNORM_WRITE_CACHE;
+  if (a.num_tokens < 0 || a.num_heads < 1 || a.num_kv_heads < 1)
+    return fail(DORY_ERR_INVALID_ARGUMENT, "token and head counts must be positive");
+  if (a.head_dim != 64 && a.head_dim != 128 && a.head_dim != 256)
+    return fail(DORY_ERR_UNSUPPORTED, "head_dim %d (supported: 64, 128, 256)", a.head_dim);
+  if (a.sqk_dtype < 0 || a.sqk_dtype > 2) return fail(DORY_ERR_INVALID_ARGUMENT, "sqk dtype");
+  if (!a.qk || !a.v || !a.sqk || !a.q_out)
+    return fail(DORY_ERR_INVALID_ARGUMENT, "null tensor argument");
+  if (write_cache && (!a.key_cache || !a.value_cache || !a.slot_mapping || a.block_size < 1))
+    return fail(DORY_ERR_INVALID_ARGUMENT, "the cache write needs caches, a slot mapping and a block size");
+  if (!write_cache && (!a.k_out || !a.v_out))
+    return fail(DORY_ERR_INVALID_ARGUMENT, "k_out and v_out are needed without the cache write");
+  if (a.num_tokens == 0) return DORY_OK;
+  QkNormArgs k;
+  memset(&k, 0, sizeof(k));
+  k.qk = a.qk;
+  k.v = a.v;
+  k.sqk = a.sqk;
+  k.q_out = static_cast<__nv_bfloat16*>(a.q_out);
+  k.kc = static_cast<__nv_bfloat16*>(a.key_cache);
+  k.vc = static_cast<__nv_bfloat16*>(a.value_cache);
+  k.slot_mapping = a.slot_mapping;
+  k.k_out = static_cast<__nv_bfloat16*>(a.k_out);
+  k.v_out = static_cast<__nv_bfloat16*>(a.v_out);
+  k.err = a.error_word;
+  k.sb = a.stride_block;
+  k.so = a.stride_offset;
+  k.sh = a.stride_head;
+  k.ncache_blocks = a.num_cache_blocks;
+  k.sqk_factor = a.sqk_factor;
+  k.eps = a.eps;
+  k.NH = a.num_heads;
+  k.NKV = a.num_kv_heads;
+  k.B = a.block_size;
+  k.sqk_dtype = a.sqk_dtype;
+  k.write_cache = write_cache;
+  const dim3 grid((a.num_heads + a.num_kv_heads + 3) / 4, a.num_tokens);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (a.head_dim == 64) qk_norm_kernel<64><<<grid, 128, 0, s>>>(k);
+  else if (a.head_dim == 128) qk_norm_kernel<128><<<grid, 128, 0, s>>>(k);
+  else qk_norm_kernel<256><<<grid, 128, 0, s>>>(k);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(DORY_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+  return DORY_OK;
+}
 
 int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
   if (!P) return fail(DORY_ERR_INVALID_ARGUMENT, "null params");

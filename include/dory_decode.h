@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define DORY_DECODE_ABI_VERSION 1
+#define DORY_DECODE_ABI_VERSION 2
 
 /* Status codes returned by every entry point. */
 typedef enum DoryStatus {
@@ -166,6 +166,54 @@ int32_t dory_decode_attention(const DoryDecodeParams* params, void* stream);
  */
 #define DORY_DECODE_STATIC_SCRATCH_BYTES (4ll << 20)
 int32_t dory_decode_attention_static_scratch(const DoryDecodeParams* params, void* stream);
+
+/*
+ * The separate q/k normalisation step of the reference's attention sublayer:
+ * _qk_norm_cache_kernel (kernels/dory_attention.py:69-96) as FusedAttentionSublayer launches
+ * it in pre_attention (WRITE_CACHE, dory_attention.py:218-236) and pre_attention_qkv
+ * (dory_attention.py:238-250), for num_tokens tokens (the reference launches one):
+ *   q_out[t][h] = bf16((float(sqk[h]) * sqk_factor)^2 * q[t][h] * rsqrt(sum q[t][h]^2 + eps))
+ *   k[t][g]     = bf16(k[t][g] * rsqrt(sum k[t][g]^2 + eps)),   v[t][g] = bf16(v[t][g])
+ * with k and v written into the paged cache at slot_mapping[t] (DORY_QKNORM_WRITE_CACHE; a
+ * negative slot is a padding token and writes nothing) or to k_out / v_out.  q_out is the
+ * query dory_decode_attention takes without DORY_FLAG_RAW_QKV (DecodeAttention.__call__),
+ * and the normalisation is the one the fused RAW_QKV kernel applies, so both paths append
+ * the same bits.
+ */
+#define DORY_QKNORM_WRITE_CACHE 1u
+typedef struct DoryQkNormParams {
+  const float* qk;                /* FP32 [T, (NH + NKV) * HD]: q heads then k heads          */
+  const float* v;                 /* FP32 [T, NKV * HD]                                       */
+  const void* sqk;                /* [NH * HD] of sqk_dtype                                   */
+  void* q_out;                    /* BF16 [T, NH * HD]                                        */
+  void* key_cache;                /* WRITE_CACHE: BF16 view [num_cache_blocks, block_size,
+                                   * NKV, HD]                                                 */
+  void* value_cache;              /* WRITE_CACHE: same strides as key_cache, unit last stride */
+  const int64_t* slot_mapping;    /* WRITE_CACHE: int64 [T]                                   */
+  void* k_out;                    /* otherwise: BF16 [T, NKV * HD]                            */
+  void* v_out;                    /* otherwise: BF16 [T, NKV * HD]                            */
+  uint32_t* error_word;           /* optional (NULL: none): DORY_DEVERR_SLOT_OOB is or-ed in
+                                   * for a slot outside the cache, which is then skipped       */
+  int64_t stride_block;           /* key_cache.stride(0) */
+  int64_t stride_offset;          /* key_cache.stride(1) */
+  int64_t stride_head;            /* key_cache.stride(2) */
+  int64_t num_cache_blocks;       /* key_cache.shape[0]; > 0 enables the slot bounds check    */
+  float sqk_factor;
+  float eps;
+  int32_t num_tokens;
+  int32_t num_heads;
+  int32_t num_kv_heads;
+  int32_t head_dim;               /* 64, 128 or 256 */
+  int32_t block_size;             /* key_cache.shape[1] (reference CACHE_BLOCK)               */
+  int32_t sqk_dtype;              /* DoryDType */
+  uint32_t flags;                 /* DORY_QKNORM_WRITE_CACHE */
+} DoryQkNormParams;
+
+/* sizeof(DoryQkNormParams) as compiled into the library. */
+int64_t dory_qk_norm_params_bytes(void);
+
+/* One launch of the q/k normalisation (and cache write) on `stream`. */
+int32_t dory_qk_norm_cache(const DoryQkNormParams* params, void* stream);
 
 /* Copies the device error word (DORY_DEVERR_* bits) to *flags_out, synchronising `stream`;
  * clears it when `clear` is non-zero.  The only entry point that waits on the device. */

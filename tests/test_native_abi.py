@@ -101,3 +101,32 @@ def test_status_maps_to_reference_exceptions(lib):
     p = _params(head_dim=96)
     with pytest.raises(NotImplementedError):
         _native.check(lib.dory_decode_attention(ctypes.byref(p), None))
+
+
+def test_qk_norm_struct_layout(lib):
+    assert lib.dory_qk_norm_params_bytes() == ctypes.sizeof(_native.DoryQkNormParams)
+
+
+def _qk_params(**kw):
+    p = _native.DoryQkNormParams()
+    for f in ("qk", "v", "sqk", "q_out", "key_cache", "value_cache", "slot_mapping"):
+        setattr(p, f, 0x1000)  # never dereferenced: validation fails before any CUDA call
+    p.num_tokens, p.num_heads, p.num_kv_heads, p.head_dim, p.block_size = 1, 32, 8, 128, 16
+    p.flags, p.eps, p.sqk_factor = _native.QKNORM_WRITE_CACHE, 1e-6, 0.7
+    for k, val in kw.items():
+        setattr(p, k, val)
+    return p
+
+
+@pytest.mark.parametrize("kw,status,message", [
+    (dict(head_dim=96), _native.ERR_UNSUPPORTED, "head_dim"),
+    (dict(num_heads=0), _native.ERR_INVALID_ARGUMENT, "positive"),
+    (dict(qk=None), _native.ERR_INVALID_ARGUMENT, "null tensor"),
+    (dict(slot_mapping=None), _native.ERR_INVALID_ARGUMENT, "slot mapping"),
+    (dict(flags=0), _native.ERR_INVALID_ARGUMENT, "k_out and v_out"),
+    (dict(sqk_dtype=7), _native.ERR_INVALID_ARGUMENT, "sqk dtype"),
+])
+def test_qk_norm_host_validation(lib, kw, status, message):
+    p = _qk_params(**kw)
+    assert lib.dory_qk_norm_cache(ctypes.byref(p), None) == status
+    assert message in lib.dory_decode_last_error().decode()
