@@ -223,6 +223,11 @@ class DeviceWorkload:
                                           device=dev)
         self.cache_offsets = torch.zeros(T, dtype=torch.int64, device=dev)
         self.seq_lens = torch.tensor(self.seq_lens_list, dtype=torch.int32, device=dev)
+        # append slot of every token (its table entry at seq_len - 1, as vLLM's slot_mapping)
+        self.slots = torch.tensor([int(tables[rows[t], (n - 1) // BLOCK]) * BLOCK + (n - 1) % BLOCK
+                                   for t, n in enumerate(self.seq_lens_list)],
+                                  dtype=torch.int64, device=dev)
+        self.separate = False  # --path separate: q/k normalisation kernel, then __call__
         self.pool_blocks = blocks
         pool_bytes = blocks * BLOCK * KV_ROW_BYTES
         free, _ = torch.cuda.mem_get_info(dev)
@@ -241,6 +246,7 @@ class DeviceWorkload:
         self.gate = torch.sigmoid(torch.randn(L, T, NH * HD, device=dev, generator=gd))
         self.sqk = (torch.rand(NH * HD, device=dev, generator=gd) + 0.5).to(torch.bfloat16)
         self.out = torch.zeros(L, T, 8, NH * HD // 8, device=dev)
+        self.q_out = torch.empty(T, NH * HD, dtype=torch.bfloat16, device=dev)
 
     def pool(self, layer: int):
         return self.keys[layer % self.num_pools], self.values[layer % self.num_pools]
@@ -269,6 +275,15 @@ def make_attention(wl: DeviceWorkload, args):
 def layer_call(attn, wl: DeviceWorkload, app: int, layer: int, qk, v, gate, out):
     from dory_decode_attention import EPS
     key, value = wl.pool(layer)
+    if wl.separate:
+        # The reference's separate path (bench_decode_attention.py:144-152): the q/k
+        # normalisation kernel writes the cache and the bf16 query, then __call__ attends.
+        from dory_attention import qk_norm_cache
+        qk_norm_cache(qk[0], v[0], wl.sqk, W.SQK_FACTOR, EPS, wl.q_out[0], NH, HD,
+                      key_cache=key, value_cache=value, slot_mapping=wl.slots[0:1])
+        attn(wl.q_out[0], key, value, wl.tables[0], wl.seq_lens[0:1], 0, HD ** -0.5, gate[0],
+             out[0])
+        return
     attn.multi_from_raw(qk, v, wl.sqk, W.SQK_FACTOR, EPS, wl.cache_offsets, key, value,
                         wl.tables, wl.table_offsets, wl.seq_lens, 0, HD ** -0.5, gate, out,
                         shared_cache=wl.shared)
@@ -325,6 +340,10 @@ def bench_ours(args, world, rank, local):
     lens = [lens_all[i] for i in mine]
     seed = {"config5": 4, "config3": 2, "config4": 3, "config1": 0, "config2": 1}[args.workload]
     wl = DeviceWorkload(lens, tps, shared, layers, pool_factor, dev, seed + 1000 * rank)
+    if args.path == "separate":
+        if wl.tokens != 1:
+            raise SystemExit("--path separate takes single-sequence workloads (config1, config4)")
+        wl.separate = True
     attn = make_attention(wl, args)
     apps = len(layers)
 
@@ -396,13 +415,13 @@ def bench_ours(args, world, rank, local):
                    "distinct_pools_per_rank": wl.num_pools,
                    "l2": "inputs larger than L2 (each pool > 126 MB; pools cycled per layer)",
                    "splits": args.splits, "min_blocks_per_split": args.min_blocks_per_split,
-                   "overlap_launch": args.overlap_launch},
+                   "overlap_launch": args.overlap_launch, "path": args.path},
         "us_per_layer_step": round(us_per_layer, 3),
         "hbm_gbs": round(hbm_gbs, 1),
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": args.steps * apps,
+        "gpu_launches": args.steps * apps * (2 if wl.separate else 1),
         "clocks": clocks.summary(),
     }
     if rank == 0:
@@ -612,6 +631,9 @@ def main() -> int:
     ap.add_argument("--min-blocks-per-split", type=int, default=None)
     ap.add_argument("--overlap-launch", action="store_true",
                     help="launch each layer call as a programmatic dependent of the previous one")
+    ap.add_argument("--path", choices=("fused", "separate"), default="fused",
+                    help="separate: the q/k normalisation kernel then the non-raw call "
+                         "(single-sequence workloads; the reference's two-kernel path)")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--profile-steps", type=int, default=0,

@@ -16,23 +16,30 @@
 //     out[e % 8][e / 8] (the layout w4a16_gemv.py:91-93 defines).
 //
 // B200 design:
-//   * K/V rows (head_dim * 2 bytes, contiguous for any of the three cache layouts) are
-//     staged into a multi-stage shared-memory ring by a producer warp with 16-byte cp.async
-//     copies (two whole rows per warp instruction) that complete onto mbarriers; rows are
-//     padded by 16 bytes so ldmatrix reads are bank-conflict free.  Only rows inside the
-//     attended range are read; the others are zero-filled in flight.  (One cp.async.bulk
-//     per 256-byte row was measured first: the copy engine's per-request cost, ~1.3 us per
-//     16-row chunk, capped a CTA at a few GB/s.)
-//   * Four consumer warps each own a ring slot in turn and run the 16-token chunk through
-//     mma.sync m16n8k16 (bf16 in, fp32 accumulate) with tokens on M and the GQA group's query
-//     rows (plus the other tokens of a shared-cache group) on N: S^T = K Q^T, then
-//     O^T += V^T P^T; P^T moves from accumulator to operand layout with movmatrix.
-//   * Softmax is online, in the log2 domain, with warp-shuffle row reductions.
-//   * Split partials go to caller-owned scratch; the last-arriving CTA merges (atomic
-//     counter, self-resetting), so one launch does what the reference does in two or three.
+//   * K/V chunks (16 cache rows of one KV head, K and V) are staged into an 8-stage ring in
+//     shared memory by TMA: one 5-D tensor box (64 dims x 16 rows x 64-dim quarters x head
+//     x block, 128-byte swizzle) per chunk, completing on an mbarrier.  The producer warp
+//     stages the CTA's block ids and issues the first ring's worth; from then on each
+//     consumer warp refills the stage it has just read (stages map to fixed warps), so no
+//     cross-warp hand-off sits between a stage falling free and its next copy.  Offsets that
+//     are not whole cache blocks take a cp.async copy path into the same swizzled layout.
+//   * Four consumer warps run each chunk through mma.sync m16n8k16 (bf16 in, fp32
+//     accumulate) with tokens on M and the GQA group's query rows (plus the other tokens of a
+//     shared-cache group) on N: S^T = K Q^T, then O^T += V^T P^T; P^T moves from accumulator
+//     to operand layout with movmatrix; the swizzle keeps every ldmatrix conflict-free.
+//   * Softmax is online, in the log2 domain, with warp-shuffle row reductions.  Chunks at the
+//     attended range's edges, with a bad block id or holding a new token's row take a slow
+//     path (zeroing, substitution, the append itself).
+//   * Split partials go to caller-owned scratch; the last CTA of a (token group, KV head) to
+//     arrive (acquire-release counter, self-resetting) merges them in registers, applies the
+//     gate and stores nibble-major, so one launch does what the reference does in two or
+//     three.  Opt-in programmatic dependent launch overlaps a call's prologue and K/V copies
+//     with the previous kernel's tail.
 //   * Every wait is bounded: on timeout the kernel records DORY_DEVERR_WAIT_TIMEOUT and
 //     drains its own copies before returning.  Out-of-range block ids / slots are recorded
 //     and skipped, never dereferenced.
+//   * A second small kernel is the reference's separate q/k normalisation + cache write
+//     (_qk_norm_cache_kernel), the input side of the non-raw call.
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
