@@ -247,6 +247,7 @@ class DeviceWorkload:
         self.sqk = (torch.rand(NH * HD, device=dev, generator=gd) + 0.5).to(torch.bfloat16)
         self.out = torch.zeros(L, T, 8, NH * HD // 8, device=dev)
         self.q_out = torch.empty(T, NH * HD, dtype=torch.bfloat16, device=dev)
+        self.sumsq = None  # --sumsq: [layers, T] FP32 sum of squared outputs per token
 
     def pool(self, layer: int):
         return self.keys[layer % self.num_pools], self.values[layer % self.num_pools]
@@ -282,11 +283,12 @@ def layer_call(attn, wl: DeviceWorkload, app: int, layer: int, qk, v, gate, out)
         qk_norm_cache(qk[0], v[0], wl.sqk, W.SQK_FACTOR, EPS, wl.q_out[0], NH, HD,
                       key_cache=key, value_cache=value, slot_mapping=wl.slots[0:1])
         attn(wl.q_out[0], key, value, wl.tables[0], wl.seq_lens[0:1], 0, HD ** -0.5, gate[0],
-             out[0])
+             out[0], out_sumsq=None if wl.sumsq is None else wl.sumsq[layer])
         return
     attn.multi_from_raw(qk, v, wl.sqk, W.SQK_FACTOR, EPS, wl.cache_offsets, key, value,
                         wl.tables, wl.table_offsets, wl.seq_lens, 0, HD ** -0.5, gate, out,
-                        shared_cache=wl.shared)
+                        shared_cache=wl.shared,
+                        out_sumsq=None if wl.sumsq is None else wl.sumsq[layer])
 
 
 def run_step(attn, wl: DeviceWorkload):
@@ -340,6 +342,8 @@ def bench_ours(args, world, rank, local):
     lens = [lens_all[i] for i in mine]
     seed = {"config5": 4, "config3": 2, "config4": 3, "config1": 0, "config2": 1}[args.workload]
     wl = DeviceWorkload(lens, tps, shared, layers, pool_factor, dev, seed + 1000 * rank)
+    if args.sumsq:
+        wl.sumsq = torch.zeros(wl.num_layers, wl.tokens, device=dev)
     if args.path == "separate":
         if wl.tokens != 1:
             raise SystemExit("--path separate takes single-sequence workloads (config1, config4)")
@@ -415,7 +419,8 @@ def bench_ours(args, world, rank, local):
                    "distinct_pools_per_rank": wl.num_pools,
                    "l2": "inputs larger than L2 (each pool > 126 MB; pools cycled per layer)",
                    "splits": args.splits, "min_blocks_per_split": args.min_blocks_per_split,
-                   "overlap_launch": args.overlap_launch, "path": args.path},
+                   "overlap_launch": args.overlap_launch, "path": args.path,
+                   "out_sumsq": bool(args.sumsq)},
         "us_per_layer_step": round(us_per_layer, 3),
         "hbm_gbs": round(hbm_gbs, 1),
         "roofline": roofline,
@@ -634,6 +639,8 @@ def main() -> int:
     ap.add_argument("--path", choices=("fused", "separate"), default="fused",
                     help="separate: the q/k normalisation kernel then the non-raw call "
                          "(single-sequence workloads; the reference's two-kernel path)")
+    ap.add_argument("--sumsq", action="store_true",
+                    help="also produce each token's sum of squared outputs (out_sumsq)")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--profile-steps", type=int, default=0,

@@ -13,7 +13,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 LIBRARY = HERE / "libdory_decode.so"
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 # DoryStatus
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_ALIGNMENT, ERR_CUDA = range(5)
@@ -47,7 +47,7 @@ class DoryDecodeParams(ctypes.Structure):
         ("q", _vp), ("v", _vp), ("sqk", _vp), ("slot_mapping", _vp),
         ("key_cache", _vp), ("value_cache", _vp), ("block_table", _vp),
         ("block_table_offsets", _vp), ("cache_offsets", _vp), ("seq_lens", _vp),
-        ("gate", _vp), ("out_nibble_major", _vp), ("scratch", _vp),
+        ("gate", _vp), ("out_nibble_major", _vp), ("out_sumsq", _vp), ("scratch", _vp),
         ("scratch_bytes", _i64), ("stride_block", _i64), ("stride_offset", _i64),
         ("stride_head", _i64), ("num_cache_blocks", _i64),
         ("softmax_scale", _f32), ("sqk_factor", _f32), ("eps", _f32),

@@ -91,8 +91,11 @@ struct alignas(64) KParams {
   __nv_bfloat16* vc;
   const float* gate;
   float* out;
+  float* sumsq;          // optional [T]: sum over e of out[t][e]^2 (the output's justnorm statistic)
   uint32_t* err;
   int32_t* counters;
+  int32_t* tok_counters;  // [max_tokens]: KV heads whose outputs are stored (sumsq)
+  float* sumsq_part;      // [max_tokens][NKV]: each KV head's share of sumsq
   float2* pml;  // [max_tokens][S][NH] (max in log2 units, sum)
   float* po;    // [max_tokens][S][NH][HD]
   int64_t tm_blocks;  // extent of the block dimension of the tensor maps
@@ -107,14 +110,16 @@ static_assert(offsetof(KParams, tmk) % 64 == 0, "tensor maps are 64-byte aligned
 
 // Scratch layout (bytes), shared by host and device.
 struct ScratchLayout {
-  int64_t counters, pml, po, total;
+  int64_t counters, tok_counters, sumsq_part, pml, po, total;
 };
 __host__ __device__ inline int64_t align256(int64_t x) { return (x + 255) & ~int64_t(255); }
 __host__ __device__ inline ScratchLayout scratch_layout(int max_tokens, int S, int NH, int NKV,
                                                         int HD) {
   ScratchLayout L;
   L.counters = 256;  // [0, 256): header; word 0 = device error flags
-  L.pml = align256(L.counters + int64_t(max_tokens) * NKV * 4);
+  L.tok_counters = align256(L.counters + int64_t(max_tokens) * NKV * 4);
+  L.sumsq_part = align256(L.tok_counters + int64_t(max_tokens) * 4);
+  L.pml = align256(L.sumsq_part + int64_t(max_tokens) * NKV * 4);
   L.po = align256(L.pml + int64_t(max_tokens) * S * NH * 8);
   L.total = align256(L.po + int64_t(max_tokens) * S * NH * HD * 4);
   return L;
@@ -431,7 +436,7 @@ __device__ __forceinline__ bool fixup_stage(const KParams& p, uint8_t* kst, uint
 // ------------------------------------------------------------------------------------
 template <int HD, int UPT, int SB>
 __device__ __forceinline__ void merge_splits(const KParams& p, int tid, int nrows, int gstart,
-                                             int kvh, int G, int active) {
+                                             int kvh, int G, int active, float* sv) {
   constexpr int UPR = HD / 4;  // float4 units per row
   constexpr int NTHR = kConsumerWarps * 32;
   const int Q = p.NH * HD;
@@ -495,10 +500,52 @@ __device__ __forceinline__ void merge_splits(const KParams& p, int tid, int nrow
     const float inv = 1.0f / (Ls[k] > 0.0f ? Ls[k] : 1.0f);
     const int e0 = head * HD + d4 * 4;  // 4 consecutive elements: same e / 8, e % 8 = j0..j0+3
     float* out = p.out + int64_t(t) * Q + (e0 % 8) * (Q / 8) + e0 / 8;
-    out[0] = acc[k].x * inv * gt[k].x;
-    out[Q / 8] = acc[k].y * inv * gt[k].y;
-    out[2 * (Q / 8)] = acc[k].z * inv * gt[k].z;
-    out[3 * (Q / 8)] = acc[k].w * inv * gt[k].w;
+    const float o0 = acc[k].x * inv * gt[k].x, o1 = acc[k].y * inv * gt[k].y;
+    const float o2 = acc[k].z * inv * gt[k].z, o3 = acc[k].w * inv * gt[k].w;
+    out[0] = o0;
+    out[Q / 8] = o1;
+    out[2 * (Q / 8)] = o2;
+    out[3 * (Q / 8)] = o3;
+    if (p.sumsq) sv[u] = o0 * o0 + o1 * o1 + o2 * o2 + o3 * o3;  // unit u = r * UPR + d4
+  }
+}
+
+// ---- the output's justnorm statistic: sumsq[t] = sum over e of out[t][e]^2 ----
+// Every output element is stored by one thread of the CTA that stores its (token group,
+// KV head)'s outputs; `sv` holds the sum of squares of each (row, unit) of them, unit u of
+// row r at [r * units + u].  The sums are taken in a fixed order (units of a row, rows of a
+// token, KV heads of a token), so the statistic does not depend on which CTA finishes last.
+// ALL: every thread of the CTA takes part (block barrier), else the consumer warps.
+template <bool ALL>
+__device__ __forceinline__ void sumsq_tail(const KParams& p, const float* sv, int units, int nrows,
+                                           int gstart, int gcount, int G, int kvh, int tid,
+                                           float* s_rowss) {
+  constexpr int NTHR = ALL ? kThreads : kConsumerWarps * 32;
+  auto sync = [] {
+    if (ALL) __syncthreads();
+    else named_barrier_consumers();
+  };
+  sync();
+  for (int r = tid; r < nrows; r += NTHR) {
+    float acc = 0.0f;
+    for (int u = 0; u < units; ++u) acc += sv[r * units + u];
+    s_rowss[r] = acc;
+  }
+  sync();
+  if (tid < gcount) {
+    const int t = gstart + tid;
+    float part = 0.0f;
+    for (int g = 0; g < G; ++g) part += s_rowss[tid * G + g];
+    p.sumsq_part[int64_t(t) * p.NKV + kvh] = part;
+    int prev;
+    asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(prev) : "l"(p.tok_counters + t)
+                 : "memory");
+    if (prev == p.NKV - 1) {  // the last KV head of this token: sum the heads in order
+      float total = 0.0f;
+      for (int h = 0; h < p.NKV; ++h) total += __ldcg(p.sumsq_part + int64_t(t) * p.NKV + h);
+      p.sumsq[t] = total;
+      p.tok_counters[t] = 0;  // self-reset for the next launch
+    }
   }
 }
 
@@ -524,6 +571,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   __shared__ int s_tab[kTab];  // block ids of the first kTab blocks of this CTA's range
   __shared__ CtaInfo s_ci;
   __shared__ float s_wm[kConsumerWarps][ROWS], s_wl[kConsumerWarps][ROWS];
+  __shared__ float s_rowss[16];  // per-row sums of squared outputs (sumsq)
 
   const int split = blockIdx.x;
   const int kvh = blockIdx.y;
@@ -614,12 +662,16 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     // Padding request(s): the reference's combine writes 0 * gate.
     if (split == 0) {
       grid_dependency_wait();
+      float* sv0 = reinterpret_cast<float*>(smem + L::kStages);  // [nrows][HD] squares
       for (int i = tid; i < nrows * HD; i += kThreads) {
         const int r = i / HD, d = i % HD;
         const int t = gstart + r / G, head = kvh * G + r % G;
         const int e = head * HD + d;
-        p.out[int64_t(t) * Q + (e % 8) * (Q / 8) + e / 8] = 0.0f * p.gate[int64_t(t) * Q + e];
+        const float val = 0.0f * p.gate[int64_t(t) * Q + e];
+        p.out[int64_t(t) * Q + (e % 8) * (Q / 8) + e / 8] = val;
+        if (p.sumsq) sv0[i] = val * val;
       }
+      if (p.sumsq) sumsq_tail<true>(p, sv0, HD, nrows, gstart, gcount, G, kvh, tid, s_rowss);
     }
     return;
   }
@@ -808,7 +860,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   // Every load of this warp's rows (q, sqk) and of its first sub token (k, v) is issued
   // before any of the arithmetic: one L2 round trip, not one per dependent step.
   constexpr int RPW = ROWS / kConsumerWarps;  // query rows per consumer warp
-  float qv[RPW][PER_LANE], sv[RPW][PER_LANE], kv0[PER_LANE], vv0[PER_LANE];
+  float qv[RPW][PER_LANE], sqv[RPW][PER_LANE], kv0[PER_LANE], vv0[PER_LANE];
 #pragma unroll
   for (int j = 0; j < RPW; ++j) {
     const int r = warp + j * kConsumerWarps;
@@ -820,7 +872,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
 #pragma unroll
       for (int i = 0; i < PER_LANE; ++i) {
         qv[j][i] = src[lane * PER_LANE + i];
-        sv[j][i] = load_sqk(p.sqk, p.sqk_dtype, head * HD + lane * PER_LANE + i);
+        sqv[j][i] = load_sqk(p.sqk, p.sqk_dtype, head * HD + lane * PER_LANE + i);
       }
     } else {
       const __nv_bfloat16* src =
@@ -853,7 +905,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
       const float rn = row_inv_norm<PER_LANE>(qv[j], p.eps);
 #pragma unroll
       for (int i = 0; i < PER_LANE; ++i) {
-        const float s = __fmul_rn(sv[j][i], p.sqk_factor);
+        const float s = __fmul_rn(sqv[j][i], p.sqk_factor);
         const float qn = __fmul_rn(qv[j][i], rn);
         const float qb = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(s, s), qn)));
         q2[r * HD + lane * PER_LANE + i] = __float2bfloat16_rn(__fmul_rn(qb, p.scale));
@@ -1091,6 +1143,10 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   const int items = nrows * IPR;
   const bool single = sp.active == 1;
   const int64_t S = p.S;
+  // Squares of the stored outputs (sumsq), after the warps' buffers in the drained ring.
+  constexpr int kSvOff = (kConsumerWarps * ROWS * OST * 4 + 15) & ~15;
+  static_assert(kSvOff + ROWS * (HD / 4) * 4 <= NS * L::kStageBytes, "sumsq buffer fits the ring");
+  float* sv = reinterpret_cast<float*>(smem + L::kStages + kSvOff);
   for (int it = tid; it < items; it += kConsumerWarps * 32) {
     const int r = it / IPR, k8 = it % IPR;
     float M = -INFINITY;
@@ -1116,8 +1172,14 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
       const int e0 = head * HD + k8 * 8;
       const float* gt = p.gate + int64_t(t) * Q + e0;
       float* out = p.out + int64_t(t) * Q + e0 / 8;
+      float ss = 0.0f;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) out[e * (Q / 8)] = acc[e] * inv * gt[e];
+      for (int e = 0; e < 8; ++e) {
+        const float val = acc[e] * inv * gt[e];
+        out[e * (Q / 8)] = val;
+        ss += val * val;
+      }
+      if (p.sumsq) sv[it] = ss;  // item it = r * IPR + k8
     } else {
       const int64_t pi = (int64_t(t) * S + split) * p.NH + head;
       if (k8 == 0) p.pml[pi] = make_float2(M, Lsum);
@@ -1126,7 +1188,10 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
       dst[1] = make_float4(acc[4], acc[5], acc[6], acc[7]);
     }
   }
-  if (single) return;
+  if (single) {
+    if (p.sumsq) sumsq_tail<false>(p, sv, IPR, nrows, gstart, gcount, G, kvh, tid, s_rowss);
+    return;
+  }
 
   // ---- cross-split merge by the last CTA of this (group, KV head) to arrive ----
   // The barrier orders every consumer thread's partial stores before thread 0's release
@@ -1147,10 +1212,11 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   // batch; the gate rides along the first), each batch folded in with one max, independent
   // weights and one rescale.
   if (nrows * (HD / 4) <= kConsumerWarps * 32)
-    merge_splits<HD, 1, 16>(p, tid, nrows, gstart, kvh, G, sp.active);
+    merge_splits<HD, 1, 16>(p, tid, nrows, gstart, kvh, G, sp.active, sv);
   else
     merge_splits<HD, (ROWS * HD / 4 + kConsumerWarps * 32 - 1) / (kConsumerWarps * 32), 4>(
-        p, tid, nrows, gstart, kvh, G, sp.active);
+        p, tid, nrows, gstart, kvh, G, sp.active, sv);
+  if (p.sumsq) sumsq_tail<false>(p, sv, HD / 4, nrows, gstart, gcount, G, kvh, tid, s_rowss);
 }
 
 // ------------------------------------------------------------------------------------
@@ -1526,9 +1592,12 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
   kp.seq_lens = a.seq_lens;
   kp.gate = a.gate;
   kp.out = a.out_nibble_major;
+  kp.sumsq = a.out_sumsq;
   uint8_t* base = static_cast<uint8_t*>(a.scratch);
   kp.err = reinterpret_cast<uint32_t*>(base);
   kp.counters = reinterpret_cast<int32_t*>(base + SL.counters);
+  kp.tok_counters = reinterpret_cast<int32_t*>(base + SL.tok_counters);
+  kp.sumsq_part = reinterpret_cast<float*>(base + SL.sumsq_part);
   kp.pml = reinterpret_cast<float2*>(base + SL.pml);
   kp.po = reinterpret_cast<float*>(base + SL.po);
   kp.sb = a.stride_block;

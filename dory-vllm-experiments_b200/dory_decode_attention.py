@@ -94,25 +94,27 @@ class DecodeAttention:
 
     def __call__(self, q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
                  block_table: torch.Tensor, seq_lens: torch.Tensor, window: int,
-                 softmax_scale: float, gate: torch.Tensor, out_nibble_major: torch.Tensor) -> None:
+                 softmax_scale: float, gate: torch.Tensor, out_nibble_major: torch.Tensor,
+                 out_sumsq: torch.Tensor | None = None) -> None:
         """q: BF16 [heads * head_dim], already in the cache's k and v; block_table:
         [max_blocks] of this sequence; seq_lens: [1] tokens including this one;
         window: 0 for full attention; gate: FP32 [heads * head_dim];
         out_nibble_major: FP32 [8, heads * head_dim / 8]."""
         self._launch(q, key_cache, value_cache, block_table, seq_lens, window, softmax_scale,
-                     gate, out_nibble_major, raw=None, tokens=1, cache_offsets=None)
+                     gate, out_nibble_major, raw=None, tokens=1, cache_offsets=None,
+                     out_sumsq=out_sumsq)
 
     def from_raw(self, qk: torch.Tensor, v: torch.Tensor, sqk: torch.Tensor, sqk_factor: float,
                  eps: float, slot_mapping: torch.Tensor, key_cache: torch.Tensor,
                  value_cache: torch.Tensor, block_table: torch.Tensor, seq_lens: torch.Tensor,
                  window: int, softmax_scale: float, gate: torch.Tensor,
-                 out_nibble_major: torch.Tensor) -> None:
+                 out_nibble_major: torch.Tensor, out_sumsq: torch.Tensor | None = None) -> None:
         """Like __call__, from the rotated, unnormalized q and k heads (FP32
         [(heads + kv_heads) * head_dim]) and v (FP32 [kv_heads * head_dim]); also
         writes this token's k and v into the cache at slot_mapping[0]."""
         self._launch(qk, key_cache, value_cache, block_table, seq_lens, window, softmax_scale,
                      gate, out_nibble_major, raw=(v, sqk, sqk_factor, eps, slot_mapping),
-                     tokens=1, cache_offsets=None)
+                     tokens=1, cache_offsets=None, out_sumsq=out_sumsq)
 
     def multi_from_raw(self, qk: torch.Tensor, v: torch.Tensor, sqk: torch.Tensor,
                        sqk_factor: float, eps: float, cache_offsets: torch.Tensor,
@@ -120,7 +122,7 @@ class DecodeAttention:
                        block_tables: torch.Tensor, block_table_offsets: torch.Tensor,
                        seq_lens: torch.Tensor, window: int, softmax_scale: float,
                        gate: torch.Tensor, out_nibble_major: torch.Tensor,
-                       shared_cache: bool = False) -> None:
+                       shared_cache: bool = False, out_sumsq: torch.Tensor | None = None) -> None:
         """from_raw for T tokens: qk [T, (heads + kv_heads) * head_dim], v [T, kv_heads *
         head_dim], gate [T, heads * head_dim], out_nibble_major [T, 8, heads * head_dim / 8],
         seq_lens [T].  Token t is at position seq_lens[t] - 1 and uses the cache at
@@ -134,7 +136,11 @@ class DecodeAttention:
         shared_cache: tokens may read each other's slots (several loops sharing one cache,
         where an older token's slot holds its latest loop); every token then sees the
         others' new entries, as if all were cached before attention (the reference's
-        write-all-first order), without a second launch."""
+        write-all-first order), without a second launch.
+
+        out_sumsq (optional, all three calls; no counterpart in the reference's signature):
+        FP32 [T] receiving sum over e of out[t][e]^2, the gated output's squared norm that
+        the consumer's output GEMV normalises by (dory_attention.py:114-117)."""
         tokens = qk.shape[0]
         if (tokens > self.max_tokens or cache_offsets.dtype != torch.int64
                 or block_table_offsets.dtype != torch.int64):
@@ -142,7 +148,8 @@ class DecodeAttention:
         self._launch(qk, key_cache, value_cache, block_tables, seq_lens, window, softmax_scale,
                      gate, out_nibble_major, raw=(v, sqk, sqk_factor, eps, None),
                      tokens=tokens, cache_offsets=cache_offsets,
-                     block_table_offsets=block_table_offsets, shared=shared_cache)
+                     block_table_offsets=block_table_offsets, shared=shared_cache,
+                     out_sumsq=out_sumsq)
 
     # ---- diagnostics ----
 
@@ -166,7 +173,7 @@ class DecodeAttention:
 
     def _launch(self, q, key_cache, value_cache, block_table, seq_lens, window, softmax_scale,
                 gate, out_nibble_major, raw, tokens, cache_offsets,
-                block_table_offsets=None, shared=False) -> None:
+                block_table_offsets=None, shared=False, out_sumsq=None) -> None:
         if key_cache.stride() != value_cache.stride() or key_cache.stride(-1) != 1:
             raise ValueError("key and value caches need equal strides and unit last stride")
         if key_cache.dtype != torch.bfloat16 or value_cache.dtype != torch.bfloat16:
@@ -211,6 +218,13 @@ class DecodeAttention:
         p.q, p.key_cache, p.value_cache = q.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr()
         p.block_table, p.seq_lens = block_table.data_ptr(), seq_lens.data_ptr()
         p.gate, p.out_nibble_major = gate.data_ptr(), out_nibble_major.data_ptr()
+        if out_sumsq is not None:
+            if (out_sumsq.dtype != torch.float32 or not out_sumsq.is_contiguous()
+                    or out_sumsq.numel() < tokens):
+                raise ValueError("out_sumsq must be contiguous float32 with one entry per token")
+            p.out_sumsq = out_sumsq.data_ptr()
+        else:
+            p.out_sumsq = None
         p.scratch, p.scratch_bytes = self.scratch.data_ptr(), self.scratch.numel()
         p.stride_block, p.stride_offset, p.stride_head = key_cache.stride(0), key_cache.stride(1), key_cache.stride(2)
         p.num_cache_blocks = key_cache.shape[0]

@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define DORY_DECODE_ABI_VERSION 2
+#define DORY_DECODE_ABI_VERSION 3
 
 /* Status codes returned by every entry point. */
 typedef enum DoryStatus {
@@ -91,6 +91,11 @@ typedef struct DoryDecodeParams {
   const int32_t* seq_lens;        /* int32 [T]: tokens including this one (0 = padding)     */
   const float* gate;              /* FP32 [T, Q], post-sigmoid output gate                  */
   float* out_nibble_major;        /* FP32 [T, 8, Q / 8]: out[t][e % 8][e / 8] = gated attn[e] */
+  float* out_sumsq;               /* optional FP32 [T] (NULL: not computed): sum over e of
+                                   * out[t][e]^2, the statistic the consumer's output GEMV
+                                   * normalises by (justnorm of the gated output,
+                                   * dory_attention.py:114-117 reads all of x for it); summed
+                                   * in a fixed order, so repeated calls agree to the bit   */
   void* scratch;                  /* dory_decode_scratch_bytes() bytes, zeroed once by
                                    * dory_decode_scratch_init(); partials, merge counters and
                                    * the device error word live here                         */
