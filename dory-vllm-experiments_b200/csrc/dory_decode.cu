@@ -1346,6 +1346,10 @@ int32_t launch(const KParams& kp, dim3 grid, int smem_bytes, cudaStream_t stream
 template <int HD, int NT>
 struct Depth {
   static constexpr int value = HD == 256 ? 4 : 8;
+  // Required, not a tuning choice: with another count, the warp that refills stage s is not
+  // the one that reads its next occupant, so a warp can wait on a stage two phases ahead of
+  // the copy still landing there, which a parity wait cannot tell apart.
+  static_assert(value % kConsumerWarps == 0, "ring stages must be a multiple of the consumer warps");
 };
 
 template <int HD, int NT>
