@@ -510,6 +510,89 @@ __device__ __forceinline__ void merge_splits(const KParams& p, int tid, int nrow
   }
 }
 
+// ------------------------------------------------------------------------------------
+// The same merge with several units per thread (8-row tiles of 128-dim heads, 256-dim
+// heads, 16-row tiles): thread tid owns the UPT
+// adjacent output units tid * UPT .. tid * UPT + UPT - 1, a unit being 4 consecutive dims of
+// one query row, all in one row (UPT divides the units per row), so one (max, sum) per split
+// serves all of them.  Batches of SB splits whose statistics and partial outputs are in
+// flight together (one L2 round trip per batch; the gate rides along the first), each
+// folded in with one max, independent weights and one rescale.
+// ------------------------------------------------------------------------------------
+template <int HD, int UPT, int SB, bool SS>
+__device__ __forceinline__ void merge_splits_rows(const KParams& p, int tid, int nrows, int gstart,
+                                             int kvh, int G, int active, float* sv) {
+  constexpr int UPR = HD / 4;  // float4 units per row
+  static_assert(UPR % UPT == 0, "a thread's units share one row");
+  const int Q = p.NH * HD;
+  const int64_t S = p.S;
+  const int units = nrows * UPR;
+  const int u0 = tid * UPT;
+  const bool mine = u0 < units;
+  const int r = mine ? u0 / UPR : 0, d40 = u0 % UPR;
+  const int t = gstart + r / G, head = kvh * G + r % G;
+  const int64_t ostride = int64_t(p.NH) * UPR;  // float4s between consecutive splits
+  const float4* osrc = reinterpret_cast<const float4*>(p.po) + ((int64_t(t) * S) * p.NH + head) * UPR + d40;
+  const float2* ssrc = p.pml + (int64_t(t) * S) * p.NH + head;
+  float4 acc[UPT], gt[UPT];
+  float Mx = -INFINITY, Ls = 0.0f;
+#pragma unroll
+  for (int k = 0; k < UPT; ++k) {
+    acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+    gt[k] = mine ? *reinterpret_cast<const float4*>(p.gate + int64_t(t) * Q + head * HD + (d40 + k) * 4)
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  for (int s0 = 0; s0 < active; s0 += SB) {
+    float4 v[SB][UPT];
+    float2 st[SB];
+#pragma unroll
+    for (int j = 0; j < SB; ++j) {
+      const bool ok = mine && s0 + j < active;
+      st[j] = ok ? __ldcg(ssrc + (s0 + j) * p.NH) : make_float2(-INFINITY, 0.f);
+#pragma unroll
+      for (int k = 0; k < UPT; ++k)
+        v[j][k] = ok ? __ldcg(osrc + (s0 + j) * ostride + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    float mb = Mx;
+#pragma unroll
+    for (int j = 0; j < SB; ++j) mb = fmaxf(mb, st[j].x);
+    const float mu = (mb == -INFINITY) ? 0.0f : mb;
+    const float wa = fast_exp2(Mx - mu);
+    float w[SB];
+#pragma unroll
+    for (int j = 0; j < SB; ++j) w[j] = fast_exp2(st[j].x - mu);
+    float lsum = Ls * wa;
+#pragma unroll
+    for (int j = 0; j < SB; ++j) lsum += st[j].y * w[j];
+#pragma unroll
+    for (int k = 0; k < UPT; ++k) {
+      float4 a = make_float4(acc[k].x * wa, acc[k].y * wa, acc[k].z * wa, acc[k].w * wa);
+#pragma unroll
+      for (int j = 0; j < SB; ++j) {
+        a.x += v[j][k].x * w[j]; a.y += v[j][k].y * w[j];
+        a.z += v[j][k].z * w[j]; a.w += v[j][k].w * w[j];
+      }
+      acc[k] = a;
+    }
+    Ls = lsum;
+    Mx = mb;
+  }
+  if (!mine) return;
+  const float inv = 1.0f / (Ls > 0.0f ? Ls : 1.0f);
+#pragma unroll
+  for (int k = 0; k < UPT; ++k) {
+    const int e0 = head * HD + (d40 + k) * 4;  // 4 consecutive elements: same e / 8, e % 8 = j0..j0+3
+    float* out = p.out + int64_t(t) * Q + (e0 % 8) * (Q / 8) + e0 / 8;
+    const float o0 = acc[k].x * inv * gt[k].x, o1 = acc[k].y * inv * gt[k].y;
+    const float o2 = acc[k].z * inv * gt[k].z, o3 = acc[k].w * inv * gt[k].w;
+    out[0] = o0;
+    out[Q / 8] = o1;
+    out[2 * (Q / 8)] = o2;
+    out[3 * (Q / 8)] = o3;
+    if (SS) sv[u0 + k] = o0 * o0 + o1 * o1 + o2 * o2 + o3 * o3;  // unit u = r * UPR + d4
+  }
+}
+
 // ---- the output's justnorm statistic: sumsq[t] = sum over e of out[t][e]^2 ----
 // Every output element is stored by one thread of the CTA that stores its (token group,
 // KV head)'s outputs; `sv` holds the sum of squares of each (row, unit) of them, unit u of
@@ -1211,11 +1294,19 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   // (max, sum) and partial outputs are all in flight together (one L2 round trip per
   // batch; the gate rides along the first), each batch folded in with one max, independent
   // weights and one rescale.
-  if (nrows * (HD / 4) <= kConsumerWarps * 32)
+  // Instances only for the unit counts this tile can reach (no dead register demand).
+  constexpr int NTHR = kConsumerWarps * 32;
+  constexpr int kMaxUnits = ROWS * (HD / 4);
+  if (nrows * (HD / 4) <= NTHR) {
     merge_splits<HD, 1, 16, SS>(p, tid, nrows, gstart, kvh, G, sp.active, sv);
-  else
-    merge_splits<HD, (ROWS * HD / 4 + kConsumerWarps * 32 - 1) / (kConsumerWarps * 32), 4, SS>(
-        p, tid, nrows, gstart, kvh, G, sp.active, sv);
+  } else if constexpr (kMaxUnits <= 2 * NTHR) {
+    merge_splits_rows<HD, 2, 8, SS>(p, tid, nrows, gstart, kvh, G, sp.active, sv);
+  } else {
+    if (nrows * (HD / 4) <= 2 * NTHR)
+      merge_splits_rows<HD, 2, 8, SS>(p, tid, nrows, gstart, kvh, G, sp.active, sv);
+    else
+      merge_splits_rows<HD, 4, 8, SS>(p, tid, nrows, gstart, kvh, G, sp.active, sv);
+  }
   if (SS) sumsq_tail<false>(p, sv, HD / 4, nrows, gstart, gcount, G, kvh, tid, s_rowss);
 }
 
@@ -1340,12 +1431,12 @@ int32_t launch(const KParams& kp, dim3 grid, int smem_bytes, cudaStream_t stream
 }
 
 // Ring stages per instantiation: a multiple of the four consumer warps, so every stage keeps
-// one consumer, which refills it; two stages per warp (64 KB of ring for 128-dim heads) let
-// each warp compute one chunk while its next one is in flight.  256-dim heads keep one
-// stage per warp (64 KB as well).
+// one consumer, which refills it; two stages per warp let each warp compute one chunk while
+// its next one is in flight (64 KB of ring for 128-dim heads at 3 CTAs/SM; 128 KB for
+// 256-dim heads, which run one CTA per SM).
 template <int HD, int NT>
 struct Depth {
-  static constexpr int value = HD == 256 ? 4 : 8;
+  static constexpr int value = 8;
   // Required, not a tuning choice: with another count, the warp that refills stage s is not
   // the one that reads its next occupant, so a warp can wait on a stage two phases ahead of
   // the copy still landing there, which a parity wait cannot tell apart.
