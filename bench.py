@@ -1,7 +1,8 @@
 """Decode attention + KV append throughput on B200 (one process per GPU).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload config5|config1|config2|config3|config4]
+                    [--workload config5|config1|config2|config3|config4|
+                                dory640|dory2048|dory8192]
 
 Default workload (`config5`, the box-scale request partition): 512 independent sequences,
 cached contexts log-uniform in [128, 8192] (seed 4), 32q/8kv x 128, bf16 paged cache with
@@ -13,10 +14,16 @@ through the 36 attention layers of a Dory-shaped step (8 input + 20 shared + 8 o
 layer reading its own cache pool (distinct pools, cycled when HBM cannot hold 36; every pool
 is far larger than L2, so nothing is reused from L2 between layers).
 
-Our arm: the 36 layer calls are captured in one CUDA graph; K replays are timed with CUDA
-events between barriers (max over ranks).  `e2e` times the same step through the public
-API with host buffers: every layer's q/k/v/gate are copied from pinned host memory and its
-output back, overlapped with the kernels on a second stream.  The reference arm
+The dory640/2048/8192 workloads are the reference benchmark's own shape (16q/4kv x 256, one
+sequence, the 56 applications of the two-loop decode order each on its own cache, window
+1024 on 3 of 4 layers).
+
+Our arm: the step's layer calls are captured in one CUDA graph; K replays are timed with
+CUDA events between barriers (max over ranks).  `e2e` times the same step through the
+public API with host buffers: every application's q/k/v/gate are copied from pinned host
+memory and its output back every step, in chunks overlapped with the kernels on two copy
+streams, the step replayed as one CUDA graph (and, as `eager`, issued from Python).  The
+reference arm
 (`--impl reference`) times the reference semantics on the host CPU (PyTorch eager FP32,
 all cores) on a bounded sample of the same workload; rank 0 only.
 """
@@ -31,6 +38,7 @@ import statistics
 import subprocess
 import sys
 import time
+from dataclasses import dataclass, field
 from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
@@ -41,8 +49,6 @@ import torch  # noqa: E402
 import workloads as W  # noqa: E402
 
 NH, NKV, HD, BLOCK = W.NH, W.NKV, W.HD, W.BLOCK
-KV_ROW_BYTES = NKV * HD * 2 * 2           # K and V of one position, all KV heads: 4096 B
-TOKEN_IO_BYTES = ((NH + NKV) * HD + NKV * HD + NH * HD + NH * HD) * 4  # qk, v, gate, out
 METRIC = ("decode-attn+KV-append µs/layer-step, HBM GB/s vs peak; seqs/s at 1/2/4/8 GPU")
 DORY_LAYERS = 36
 DECODE_ORDER_2_LOOPS = list(range(8)) + list(range(8, 28)) * 2 + list(range(28, 36))
@@ -156,6 +162,10 @@ class ClockSampler:
 # workloads on the device
 # ---------------------------------------------------------------------------------------
 
+WORKLOADS = ("config5", "config1", "config2", "config3", "config4",
+             "dory640", "dory2048", "dory8192")
+
+
 def tuned_splits(workload: str, world: int):
     """(splits, min_blocks_per_split) measured fastest on B200 for each workload; config 5
     uses 4 splits once its 512 sequences are partitioned over 2+ GPUs (fewer, longer
@@ -163,35 +173,102 @@ def tuned_splits(workload: str, world: int):
     if workload == "config5":
         return (2, 64) if world == 1 else (4, 64)
     return {"config1": (16, 1), "config2": (16, 1), "config3": (2, 32),
-            "config4": (32, 1)}.get(workload, (2, 64))
+            "config4": (32, 1), "dory640": (8, 1), "dory2048": (16, 1),
+            "dory8192": (32, 1)}.get(workload, (2, 64))
 
 
-def workload_spec(name: str):
-    """(cached context lengths, tokens per sequence, shared, layer order, pool factor, notes)."""
+@dataclass
+class Spec:
+    """One bench workload.  `layers[a]` is the cache/input set application `a` uses (a
+    layer id; applications that share an id read the same pool); `windows[id]` is that
+    layer's sliding window (0 = full context)."""
+    lens: list            # cached context length of each sequence (the prompt if shared)
+    tokens_per_seq: int
+    shared: bool
+    layers: list
+    pool_factor: float
+    notes: str
+    seed: int
+    nh: int = NH
+    nkv: int = NKV
+    hd: int = HD
+    windows: dict = field(default_factory=dict)
+
+    def window(self, layer: int) -> int:
+        return self.windows.get(layer, 0)
+
+
+def dory_spec(context: int) -> Spec:
+    """The reference benchmark's own shape (kernels/bench_decode_attention.py: 16q/4kv x 256,
+    one token, 56 applications of the two-loop decode order, each application with its own
+    shuffled cache of context // 16 + 1 blocks, sliding window 1024 on the layers with
+    layer % 4 != 3 of the Dory model)."""
+    apps = len(DECODE_ORDER_2_LOOPS)
+    windows = {a: (1024 if layer % 4 != 3 else 0) for a, layer in enumerate(DECODE_ORDER_2_LOOPS)}
+    full = sum(1 for w in windows.values() if w == 0)
+    return Spec([context], 1, False, list(range(apps)), 1.0,
+                f"reference benchmark shape: 16q/4kv x 256, 1 seq, ctx {context}, {apps} "
+                f"decode-order applications each on its own cache, window 1024 on "
+                f"{apps - full} of them, seed 5", 5 + context, nh=16, nkv=4, hd=256,
+                windows=windows)
+
+
+def workload_spec(name: str) -> Spec:
     if name == "config5":
-        return W.config5_lens(), 1, False, list(range(DORY_LAYERS)), 1.0, \
-            "512 seqs, ctx log-uniform [128, 8192], seed 4"
+        return Spec(W.config5_lens(), 1, False, list(range(DORY_LAYERS)), 1.0,
+                    "512 seqs, ctx log-uniform [128, 8192], seed 4", 4)
     if name == "config3":
-        return W.config3_lens(), 1, False, list(range(DORY_LAYERS)), 1.2, \
-            "64 seqs, ctx uniform [128, 1152], seed 2, pool 1.2x tokens"
+        return Spec(W.config3_lens(), 1, False, list(range(DORY_LAYERS)), 1.2,
+                    "64 seqs, ctx uniform [128, 1152], seed 2, pool 1.2x tokens", 2)
     if name == "config4":
-        return [7936], 1, False, DECODE_ORDER_2_LOOPS, 1.0, \
-            "1 seq, ctx 7936, 2 loops: 56 applications over 36 caches, seed 3"
+        return Spec([7936], 1, False, DECODE_ORDER_2_LOOPS, 1.0,
+                    "1 seq, ctx 7936, 2 loops: 56 applications over 36 caches, seed 3", 3)
     if name == "config1":
-        return [640], 1, False, DECODE_ORDER_2_LOOPS, 1.0, \
-            "1 seq, ctx 640, 2 loops: 56 applications over 36 caches, seed 0"
+        return Spec([640], 1, False, DECODE_ORDER_2_LOOPS, 1.0,
+                    "1 seq, ctx 640, 2 loops: 56 applications over 36 caches, seed 0", 0)
     if name == "config2":
-        return [2560 + 150], 4, True, list(range(20)), 1.0, \
-            "wavefront: 4 tokens at positions 2710..2713 (prompt 2560 + 150 generated), " \
-            "20 shared layers, seed 1"
-    raise SystemExit(f"unknown workload {name}")
+        return Spec([2560 + 150], 4, True, list(range(20)), 1.0,
+                    "wavefront: 4 tokens at positions 2710..2713 (prompt 2560 + 150 "
+                    "generated), 20 shared layers, seed 1", 1)
+    if name.startswith("dory") and name[4:] in ("640", "2048", "8192"):
+        return dory_spec(int(name[4:]))
+    raise SystemExit(f"unknown workload {name} (one of {', '.join(WORKLOADS)})")
+
+
+def algorithmic_bytes(seq_lens, shared: bool, window: int, nh: int, nkv: int, hd: int) -> int:
+    """Bytes one launch must move: unique attended positions x the K/V row bytes (the new
+    rows written, the rest read) + per-token q/k/v/gate reads and out writes (FP32) + sqk
+    + the block-table entries of the attended range + seq_lens.  With a sliding window w a
+    token attends [max(seq_len - w, 0), seq_len); a shared-cache group reads the union of
+    its tokens' ranges once."""
+    kv_row = nkv * hd * 2 * 2
+    token_io = ((nh + nkv) * hd + nkv * hd + 2 * nh * hd) * 4
+
+    def span(n):
+        return (max(n - window, 0) if window > 0 else 0), n
+
+    def table_entries(first, last):
+        return (last - 1) // BLOCK - first // BLOCK + 1 if last > first else 0
+
+    if shared:
+        firsts, lasts = zip(*(span(n) for n in seq_lens))
+        spans = [(min(firsts), max(lasts))]
+    else:
+        spans = [span(n) for n in seq_lens]
+    unique = sum(b - a for a, b in spans)
+    table = sum(table_entries(a, b) for a, b in spans) * 4
+    return unique * kv_row + len(seq_lens) * token_io + nh * hd * 2 + table + 4 * len(seq_lens)
 
 
 class DeviceWorkload:
     """Per-rank device tensors: block pools, tables, per-layer inputs and outputs."""
 
-    def __init__(self, lens, tokens_per_seq, shared, layers, pool_factor, dev, seed,
-                 mem_fraction=0.5):
+    def __init__(self, spec: Spec, lens, dev, seed, mem_fraction=0.5):
+        tokens_per_seq, shared, layers = spec.tokens_per_seq, spec.shared, spec.layers
+        pool_factor = spec.pool_factor
+        self.spec = spec
+        self.nh, self.nkv, self.hd = NH_, NKV_, HD_ = spec.nh, spec.nkv, spec.hd
+        self.kv_row_bytes = NKV_ * HD_ * 2 * 2  # K and V of one position, all KV heads
         self.dev = dev
         self.lens = lens
         self.shared = shared
@@ -227,74 +304,104 @@ class DeviceWorkload:
         self.slots = torch.tensor([int(tables[rows[t], (n - 1) // BLOCK]) * BLOCK + (n - 1) % BLOCK
                                    for t, n in enumerate(self.seq_lens_list)],
                                   dtype=torch.int64, device=dev)
-        self.separate = False  # --path separate: q/k normalisation kernel, then __call__
+        # fused: from_raw / multi_from_raw; separate: the q/k normalisation kernel, then
+        # __call__; call: __call__ alone on a prepared bf16 query (prepare_call_path)
+        self.path = "fused"
+        self.q_call = None
         self.pool_blocks = blocks
-        pool_bytes = blocks * BLOCK * KV_ROW_BYTES
+        self.pool_bytes = pool_bytes = blocks * BLOCK * self.kv_row_bytes
         free, _ = torch.cuda.mem_get_info(dev)
         self.num_pools = max(1, min(self.num_layers, int(mem_fraction * free // pool_bytes)))
         gd = torch.Generator(device=dev).manual_seed(seed)
         self.raws, self.keys, self.values = [], [], []
         for _ in range(self.num_pools):
-            raw, key, value = W.cache_views(blocks, BLOCK, NKV, HD, "triton", dev)
+            raw, key, value = W.cache_views(blocks, BLOCK, NKV_, HD_, "triton", dev)
             raw.normal_(generator=gd)
             self.raws.append(raw)
             self.keys.append(key)
             self.values.append(value)
         L = self.num_layers
-        self.qk = torch.randn(L, T, (NH + NKV) * HD, device=dev, generator=gd)
-        self.v = torch.randn(L, T, NKV * HD, device=dev, generator=gd)
-        self.gate = torch.sigmoid(torch.randn(L, T, NH * HD, device=dev, generator=gd))
-        self.sqk = (torch.rand(NH * HD, device=dev, generator=gd) + 0.5).to(torch.bfloat16)
-        self.out = torch.zeros(L, T, 8, NH * HD // 8, device=dev)
-        self.q_out = torch.empty(T, NH * HD, dtype=torch.bfloat16, device=dev)
+        self.qk = torch.randn(L, T, (NH_ + NKV_) * HD_, device=dev, generator=gd)
+        self.v = torch.randn(L, T, NKV_ * HD_, device=dev, generator=gd)
+        self.gate = torch.sigmoid(torch.randn(L, T, NH_ * HD_, device=dev, generator=gd))
+        self.sqk = (torch.rand(NH_ * HD_, device=dev, generator=gd) + 0.5).to(torch.bfloat16)
+        self.out = torch.zeros(L, T, 8, NH_ * HD_ // 8, device=dev)
+        self.q_out = torch.empty(T, NH_ * HD_, dtype=torch.bfloat16, device=dev)
         self.sumsq = None  # --sumsq: [layers, T] FP32 sum of squared outputs per token
 
     def pool(self, layer: int):
         return self.keys[layer % self.num_pools], self.values[layer % self.num_pools]
 
-    def algorithmic_bytes_per_application(self) -> int:
-        """Unique attended positions x 4096 B (new rows written, the rest read) + per-token
-        q/k/v/gate/out bytes + sqk + block-table entries + seq_lens."""
-        if self.shared:
-            unique = max(self.seq_lens_list)
-            table = -(-unique // BLOCK) * 4
-        else:
-            unique = sum(self.seq_lens_list)
-            table = sum(-(-n // BLOCK) for n in self.seq_lens_list) * 4
-        return (unique * KV_ROW_BYTES + self.tokens * TOKEN_IO_BYTES + NH * HD * 2 + table
-                + 4 * self.tokens)
+    def window(self, layer: int) -> int:
+        return self.spec.window(layer)
+
+    def algorithmic_bytes_per_application(self, layer: int = 0) -> int:
+        return algorithmic_bytes(self.seq_lens_list, self.shared, self.window(layer),
+                                 self.nh, self.nkv, self.hd)
+
+    def algorithmic_bytes_per_step(self) -> int:
+        return sum(self.algorithmic_bytes_per_application(layer) for layer in self.layers)
 
 
 def make_attention(wl: DeviceWorkload, args):
     from dory_decode_attention import DecodeAttention
-    return DecodeAttention(NH, NKV, HD, wl.dev, splits=args.splits,
+    return DecodeAttention(wl.nh, wl.nkv, wl.hd, wl.dev, splits=args.splits,
                            max_tokens=max(wl.tokens, 1),
                            min_blocks_per_split=args.min_blocks_per_split,
                            overlap_launch=getattr(args, "overlap_launch", False))
 
 
-def layer_call(attn, wl: DeviceWorkload, app: int, layer: int, qk, v, gate, out):
+def prepare_call_path(wl: DeviceWorkload):
+    """`--path call`: each layer's bf16 query from its raw q/k (the q/k normalisation kernel,
+    which also appends the layer's new k/v), made once before timing; every timed call then
+    finds its K/V already in the cache, as the reference's non-raw `__call__` expects."""
+    from dory_attention import qk_norm_cache
+    from dory_decode_attention import EPS
+    wl.q_call = torch.empty(wl.num_layers, 1, wl.nh * wl.hd, dtype=torch.bfloat16, device=wl.dev)
+    for layer in range(wl.num_layers):
+        key, value = wl.pool(layer)
+        qk_norm_cache(wl.qk[layer][0], wl.v[layer][0], wl.sqk, W.SQK_FACTOR, EPS,
+                      wl.q_call[layer][0], wl.nh, wl.hd, key_cache=key, value_cache=value,
+                      slot_mapping=wl.slots[0:1])
+    wl.path = "call"
+
+
+def step_inputs(wl: DeviceWorkload):
+    """The per-layer input tensors ([layers, T, ...]) the workload's path reads."""
+    if wl.path == "call":
+        return (wl.q_call, wl.gate)
+    return (wl.qk, wl.v, wl.gate)
+
+
+def layer_call(attn, wl: DeviceWorkload, app: int, layer: int, ins, out):
+    """One application: `ins` are this application's slices of step_inputs()."""
     from dory_decode_attention import EPS
     key, value = wl.pool(layer)
-    if wl.separate:
+    window, scale = wl.window(layer), wl.hd ** -0.5
+    sumsq = None if wl.sumsq is None else wl.sumsq[layer]
+    if wl.path == "call":
+        q, gate = ins
+        attn(q[0], key, value, wl.tables[0], wl.seq_lens[0:1], window, scale, gate[0], out[0],
+             out_sumsq=sumsq)
+        return
+    qk, v, gate = ins
+    if wl.path == "separate":
         # The reference's separate path (bench_decode_attention.py:144-152): the q/k
         # normalisation kernel writes the cache and the bf16 query, then __call__ attends.
         from dory_attention import qk_norm_cache
-        qk_norm_cache(qk[0], v[0], wl.sqk, W.SQK_FACTOR, EPS, wl.q_out[0], NH, HD,
+        qk_norm_cache(qk[0], v[0], wl.sqk, W.SQK_FACTOR, EPS, wl.q_out[0], wl.nh, wl.hd,
                       key_cache=key, value_cache=value, slot_mapping=wl.slots[0:1])
-        attn(wl.q_out[0], key, value, wl.tables[0], wl.seq_lens[0:1], 0, HD ** -0.5, gate[0],
-             out[0], out_sumsq=None if wl.sumsq is None else wl.sumsq[layer])
+        attn(wl.q_out[0], key, value, wl.tables[0], wl.seq_lens[0:1], window, scale, gate[0],
+             out[0], out_sumsq=sumsq)
         return
     attn.multi_from_raw(qk, v, wl.sqk, W.SQK_FACTOR, EPS, wl.cache_offsets, key, value,
-                        wl.tables, wl.table_offsets, wl.seq_lens, 0, HD ** -0.5, gate, out,
-                        shared_cache=wl.shared,
-                        out_sumsq=None if wl.sumsq is None else wl.sumsq[layer])
+                        wl.tables, wl.table_offsets, wl.seq_lens, window, scale, gate, out,
+                        shared_cache=wl.shared, out_sumsq=sumsq)
 
 
 def run_step(attn, wl: DeviceWorkload):
     for app, layer in enumerate(wl.layers):
-        layer_call(attn, wl, app, layer, wl.qk[layer], wl.v[layer], wl.gate[layer],
-                   wl.out[layer])
+        layer_call(attn, wl, app, layer, [t[layer] for t in step_inputs(wl)], wl.out[layer])
 
 
 # ---------------------------------------------------------------------------------------
@@ -313,18 +420,18 @@ def bench_profile(args):
     """Eager steps of the layer sequence for profilers (no graph, no e2e, no CPU leg)."""
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
-    lens_all, tps, shared, layers, pool_factor, notes = workload_spec(args.workload)
-    lens_all = subset(lens_all, args.max_seqs)
-    wl = DeviceWorkload(lens_all, tps, shared, layers, pool_factor, dev, 11,
-                        mem_fraction=args.mem_fraction)
+    spec = workload_spec(args.workload)
+    lens_all = subset(spec.lens, args.max_seqs)
+    wl = DeviceWorkload(spec, lens_all, dev, 11, mem_fraction=args.mem_fraction)
     attn = make_attention(wl, args)
     for _ in range(args.profile_steps):
         run_step(attn, wl)
     torch.cuda.synchronize(dev)
     attn.check_errors()
     print(json.dumps({"profile_steps": args.profile_steps, "launches": args.profile_steps *
-                      len(layers), "sequences": len(lens_all), "pools": wl.num_pools,
-                      "algorithmic_bytes_per_launch": wl.algorithmic_bytes_per_application()}),
+                      len(spec.layers), "sequences": len(lens_all), "pools": wl.num_pools,
+                      "algorithmic_bytes_per_launch":
+                          wl.algorithmic_bytes_per_step() / len(spec.layers)}),
           flush=True)
 
 
@@ -332,7 +439,9 @@ def bench_ours(args, world, rank, local):
     dist = init_dist(world, local)
     dev = torch.device("cuda", local if world > 1 else 0)
     torch.cuda.set_device(dev)
-    lens_all, tps, shared, layers, pool_factor, notes = workload_spec(args.workload)
+    spec = workload_spec(args.workload)
+    lens_all, tps, shared, layers, notes = (spec.lens, spec.tokens_per_seq, spec.shared,
+                                            spec.layers, spec.notes)
     if shared or len(lens_all) == 1:
         mine = list(range(len(lens_all)))  # a single sequence does not shard: replicas
         scaling = "replicas"
@@ -340,14 +449,16 @@ def bench_ours(args, world, rank, local):
         mine = W.partition(lens_all, world)[rank]
         scaling = "strong"
     lens = [lens_all[i] for i in mine]
-    seed = {"config5": 4, "config3": 2, "config4": 3, "config1": 0, "config2": 1}[args.workload]
-    wl = DeviceWorkload(lens, tps, shared, layers, pool_factor, dev, seed + 1000 * rank)
+    wl = DeviceWorkload(spec, lens, dev, spec.seed + 1000 * rank)
     if args.sumsq:
         wl.sumsq = torch.zeros(wl.num_layers, wl.tokens, device=dev)
+    if args.path != "fused" and wl.tokens != 1:
+        raise SystemExit(f"--path {args.path} takes single-sequence workloads "
+                         "(config1, config4, dory*)")
     if args.path == "separate":
-        if wl.tokens != 1:
-            raise SystemExit("--path separate takes single-sequence workloads (config1, config4)")
-        wl.separate = True
+        wl.path = "separate"
+    elif args.path == "call":
+        prepare_call_path(wl)
     attn = make_attention(wl, args)
     apps = len(layers)
 
@@ -378,7 +489,7 @@ def bench_ours(args, world, rank, local):
     attn.check_errors()
 
     total_seqs = len(lens_all) * (tps if shared else 1)
-    bytes_rank = wl.algorithmic_bytes_per_application() * apps
+    bytes_rank = wl.algorithmic_bytes_per_step()
     bytes_all = sum_over_ranks(dist, float(bytes_rank), dev)
     ms_per_step = ms / args.steps
     seqs_per_s = (total_seqs * (world if scaling == "replicas" else 1)) / (ms_per_step / 1e3)
@@ -387,7 +498,7 @@ def bench_ours(args, world, rank, local):
 
     # roofline of the one kernel: this rank's bytes per launch / its average launch time
     peaks = load_peaks()
-    per_launch_bytes = wl.algorithmic_bytes_per_application()
+    per_launch_bytes = bytes_rank / apps  # this rank's average launch
     launch_us = ms_local * 1e3 / (args.steps * apps)
     achieved = per_launch_bytes / (launch_us * 1e-6) / 1e9
     ratio = read_traffic_ratio(args.workload)
@@ -395,7 +506,7 @@ def bench_ours(args, world, rank, local):
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks[0],
                 "unit": "GB/s", "frac": round(achieved / peaks[0], 4),
                 "traffic": traffic, "peak_source": peaks[1],
-                "algorithmic_bytes_per_launch": per_launch_bytes,
+                "algorithmic_bytes_per_launch": round(per_launch_bytes),
                 "launch_us": round(launch_us, 3)}
 
     e2e = bench_e2e(attn, wl, args, dist, dev, total_seqs, world, scaling)
@@ -404,7 +515,7 @@ def bench_ours(args, world, rank, local):
 
     cpu = None
     if rank == 0 and world == 1:
-        cpu = cpu_baseline(args.workload, lens_all, args.cpu_seconds)
+        cpu = cpu_baseline(args.workload, args.cpu_seconds)
 
     line = {
         "metric": METRIC, "value": round(seqs_per_s, 2), "unit": "seqs/s", "n_gpus": world,
@@ -412,12 +523,14 @@ def bench_ours(args, world, rank, local):
         "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) K/V, q/k/v, gate; random block-table permutations)",
         "config": {"workload": f"{args.workload}: {notes}", "global_batch": total_seqs,
-                   "layers_per_step": apps, "num_heads": NH, "num_kv_heads": NKV,
-                   "head_dim": HD, "block_size": BLOCK, "cache_layout": "vLLM Triton "
-                   "[blocks, kv_heads, 16, 2*head_dim] viewed via transpose(1,2).split",
+                   "layers_per_step": apps, "num_heads": wl.nh, "num_kv_heads": wl.nkv,
+                   "head_dim": wl.hd, "block_size": BLOCK,
+                   "windows": sorted({wl.window(layer) for layer in layers}),
+                   "cache_layout": "vLLM Triton [blocks, kv_heads, 16, 2*head_dim] viewed "
+                   "via transpose(1,2).split",
                    "parallelism": f"request partition over {world} GPU(s), no collectives",
                    "distinct_pools_per_rank": wl.num_pools,
-                   "l2": "inputs larger than L2 (each pool > 126 MB; pools cycled per layer)",
+                   "l2": l2_note(wl),
                    "splits": args.splits, "min_blocks_per_split": args.min_blocks_per_split,
                    "overlap_launch": args.overlap_launch, "path": args.path,
                    "out_sumsq": bool(args.sumsq)},
@@ -426,7 +539,7 @@ def bench_ours(args, world, rank, local):
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": args.steps * apps * (2 if wl.separate else 1),
+        "gpu_launches": args.steps * apps * (2 if wl.path == "separate" else 1),
         "clocks": clocks.summary(),
     }
     if rank == 0:
@@ -435,64 +548,94 @@ def bench_ours(args, world, rank, local):
         dist.destroy_process_group()
 
 
+def l2_note(wl: DeviceWorkload) -> str:
+    """How the step's inputs relate to the 126 MB L2 (nothing is flushed between steps)."""
+    touched = wl.pool_bytes * wl.num_pools
+    if wl.pool_bytes > 126e6:
+        return "inputs larger than L2 (each pool > 126 MB; pools cycled per layer)"
+    return (f"inputs larger than L2 in total: {wl.num_pools} distinct pools of "
+            f"{wl.pool_bytes / 1e6:.1f} MB cycled per step ({touched / 1e6:.0f} MB > 126 MB)")
+
+
+E2E_CHUNK_BYTES = 1 << 20  # smallest host->device copy of the end-to-end leg
+
+
 def bench_e2e(attn, wl: DeviceWorkload, args, dist, dev, total_seqs, world, scaling):
-    """The same step through the public API with host buffers: per layer, H2D of its q/k,
-    v and gate from pinned memory and D2H of its output into pinned memory, overlapped with
-    the kernels (copy stream + events)."""
-    L = wl.num_layers
-    host_in = [(wl.qk[l].cpu().pin_memory(), wl.v[l].cpu().pin_memory(),
-                wl.gate[l].cpu().pin_memory()) for l in range(L)]
-    host_out = [torch.empty_like(wl.out[l], device="cpu").pin_memory() for l in range(L)]
+    """The same step through the public API with host buffers.  Every step copies each
+    application's q/k, v and gate from pinned host memory and reads each output back into
+    pinned host memory.  Copies run on two copy streams, in chunks of consecutive
+    applications of at least E2E_CHUNK_BYTES (one per application on large workloads), and
+    overlap the kernels: a chunk's kernels wait only for its own inputs.  The reported
+    value replays the step (copies and API calls) as one CUDA graph, as vLLM runs its
+    decode step; `eager` issues the same step from Python every time."""
     apps = len(wl.layers)
-    nbuf = 3  # device staging slots, rotated over the layer applications
-    stage = [(torch.empty_like(wl.qk[0]), torch.empty_like(wl.v[0]),
-              torch.empty_like(wl.gate[0]), torch.empty_like(wl.out[0])) for _ in range(nbuf)]
-    compute = torch.cuda.current_stream(dev)
+    # inputs per application: an application that revisits a layer gets its own copy
+    host_in = [torch.stack([t[layer].cpu() for layer in wl.layers]).pin_memory()
+               for t in step_inputs(wl)]
+    host_out = torch.empty((apps,) + tuple(wl.out.shape[1:])).pin_memory()
+    dev_in = [torch.empty_like(h, device=dev) for h in host_in]
+    dev_out = torch.empty(host_out.shape, device=dev)
+    per_app = sum(h[0].numel() * h.element_size() for h in host_in)
+    k = max(1, min(apps, -(-E2E_CHUNK_BYTES // per_app)))
+    chunks = [(a, min(a + k, apps)) for a in range(0, apps, k)]
     h2d, d2h = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
-    h2d_bytes = sum(t.numel() * t.element_size() for t in host_in[0]) * apps
-    d2h_bytes = host_out[0].numel() * 4 * apps
+    h2d_bytes = per_app * apps
+    d2h_bytes = host_out.numel() * host_out.element_size()
 
     def step():
-        loaded = [torch.cuda.Event() for _ in range(apps)]
-        done = [torch.cuda.Event() for _ in range(apps)]
-        freed = [torch.cuda.Event() for _ in range(apps)]
-        h2d.wait_stream(compute)
-        for a, layer in enumerate(wl.layers):
-            buf = stage[a % nbuf]
+        compute = torch.cuda.current_stream(dev)
+        h2d.wait_stream(compute)  # the previous step's kernels are done with the inputs
+        d2h.wait_stream(compute)
+        for a0, a1 in chunks:
+            loaded, done = torch.cuda.Event(), torch.cuda.Event()
             with torch.cuda.stream(h2d):
-                if a >= nbuf:
-                    h2d.wait_event(done[a - nbuf])  # inputs of this slot consumed
-                for dst, src in zip(buf[:3], host_in[layer]):
-                    dst.copy_(src, non_blocking=True)
-                loaded[a].record(h2d)
-            compute.wait_event(loaded[a])
-            if a >= nbuf:
-                compute.wait_event(freed[a - nbuf])  # output of this slot read back
-            layer_call(attn, wl, a, layer, buf[0], buf[1], buf[2], buf[3])
-            done[a].record(compute)
+                for dst, src in zip(dev_in, host_in):
+                    dst[a0:a1].copy_(src[a0:a1], non_blocking=True)
+                loaded.record(h2d)
+            compute.wait_event(loaded)
+            for a in range(a0, a1):
+                layer_call(attn, wl, a, wl.layers[a], [t[a] for t in dev_in], dev_out[a])
+            done.record(compute)
             with torch.cuda.stream(d2h):
-                d2h.wait_event(done[a])
-                host_out[layer].copy_(buf[3], non_blocking=True)
-                freed[a].record(d2h)
-        compute.wait_stream(d2h)
+                d2h.wait_event(done)
+                host_out[a0:a1].copy_(dev_out[a0:a1], non_blocking=True)
+        compute.wait_stream(h2d)
+        compute.wait_stream(d2h)  # the step ends when its outputs are in host memory
 
+    def timed(run, steps):
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        barrier(dist, dev)
+        start.record()
+        for _ in range(steps):
+            run()
+        end.record()
+        torch.cuda.synchronize(dev)
+        barrier(dist, dev)
+        return max_over_ranks(dist, start.elapsed_time(end), dev) / steps
+
+    steps = max(1, min(args.steps, args.e2e_steps))
     for _ in range(max(1, args.warmup)):
         step()
-    steps = max(1, min(args.steps, args.e2e_steps))
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(dist, dev)
-    start.record(compute)
-    for _ in range(steps):
+    ms_eager = timed(step, steps)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
         step()
-    end.record(compute)
+    for _ in range(max(1, args.warmup)):
+        graph.replay()
+    ms = timed(graph.replay, steps)
     torch.cuda.synchronize(dev)
-    barrier(dist, dev)
-    ms = max_over_ranks(dist, start.elapsed_time(end), dev) / steps
-    value = (total_seqs * (world if scaling == "replicas" else 1)) / (ms / 1e3)
-    return {"value": round(value, 2), "unit": "seqs/s", "h2d_bytes_per_step": h2d_bytes,
+    if not torch.equal(host_out, dev_out.cpu()):
+        raise RuntimeError("end-to-end leg: host outputs differ from the device outputs")
+    del graph
+    seqs = total_seqs * (world if scaling == "replicas" else 1)
+    return {"value": round(seqs / (ms / 1e3), 2), "unit": "seqs/s", "h2d_bytes_per_step": h2d_bytes,
             "d2h_bytes_per_step": d2h_bytes, "steps": steps, "ms_per_step": round(ms, 4),
-            "path": "DecodeAttention.multi_from_raw per layer, pinned host buffers, "
-                    "copies overlapped on a second stream"}
+            "copy_chunks": len(chunks),
+            "eager": {"value": round(seqs / (ms_eager / 1e3), 2), "ms_per_step":
+                      round(ms_eager, 4)},
+            "path": "DecodeAttention.multi_from_raw per application, inputs from and outputs "
+                    "to pinned host memory every step, chunked copies on two copy streams "
+                    "overlapped with the kernels; value: the step as one CUDA graph"}
 
 
 def load_peaks():
@@ -538,52 +681,70 @@ def cpu_sample(workload: str, lens_all, budget_s: float):
 
 class CpuSample:
     """A bounded sample of the workload on the host CPU: the reference semantics in PyTorch
-    eager FP32 (oracle/dory_oracle.py) over a spread of the workload's sequences, one layer."""
+    eager FP32 (oracle/dory_oracle.py) over a spread of the workload's sequences.  One pass
+    times one application per distinct sliding window of the step and weights it by the
+    number of applications with that window."""
 
-    def __init__(self, workload: str, lens_all, budget_s: float):
+    def __init__(self, workload: str, budget_s: float):
         sys.path.insert(0, str(ROOT / "oracle"))
         import dory_oracle as O
         self.O = O
         self.threads = os.cpu_count() or 1
         torch.set_num_threads(self.threads)
-        self.lens, shared = cpu_sample(workload, lens_all, budget_s)
-        if shared:
-            self.case = W.wavefront(seed=1, prompt=self.lens[0], generated=0, tokens=4)
-        else:
-            self.case = W.batched(seed=4, lens=self.lens)
+        spec = self.spec = workload_spec(workload)
+        self.lens, shared = cpu_sample(workload, spec.lens, budget_s)
         self.shared = shared
-        self.key = self.case.key.to(torch.bfloat16)
-        self.value = self.case.value.to(torch.bfloat16)
-        _, _, _, layers, _, _ = workload_spec(workload)
-        self.layers = len(layers)
+        self.layers = len(spec.layers)
+        counts: dict[int, int] = {}
+        for layer in spec.layers:
+            w = spec.window(layer)
+            counts[w] = counts.get(w, 0) + 1
+        shape = dict(num_heads=spec.nh, num_kv_heads=spec.nkv, head_dim=spec.hd)
+        self.cases = []  # (case, bf16 key, bf16 value, applications per step)
+        for w, n in sorted(counts.items()):
+            if shared:
+                case = W.wavefront(seed=1, prompt=self.lens[0], generated=0, tokens=4,
+                                   window=w, **shape)
+            else:
+                case = W.batched(seed=4, lens=self.lens, window=w, **shape)
+            self.cases.append((case, case.key.to(torch.bfloat16), case.value.to(torch.bfloat16),
+                               n))
 
     def once(self) -> float:
-        """Seconds for one pass of the sample (one layer, the caches restored first)."""
-        c, O = self.case, self.O
-        k, v = self.key.clone(), self.value.clone()
-        width = c.tables.shape[1]
-        t0 = time.perf_counter()
-        O.multi_from_raw(c.qk, c.v, c.sqk, c.sqk_factor, O.EPS,
-                         torch.zeros(c.tokens, dtype=torch.int64), k.view(-1), v.view(-1),
-                         tuple(k.shape), k.stride(), c.tables.reshape(-1),
-                         torch.tensor([r * width for r in c.table_rows]), c.seq_lens,
-                         c.window, c.scale, c.gate, NH, NKV, shared_cache=c.shared)
-        return time.perf_counter() - t0
+        """Seconds of one whole step, estimated from one timed application per distinct
+        window (the caches restored before each)."""
+        O, total = self.O, 0.0
+        for c, key, value, n in self.cases:
+            k, v = key.clone(), value.clone()
+            width = c.tables.shape[1]
+            t0 = time.perf_counter()
+            O.multi_from_raw(c.qk, c.v, c.sqk, c.sqk_factor, O.EPS,
+                             torch.zeros(c.tokens, dtype=torch.int64), k.view(-1), v.view(-1),
+                             tuple(k.shape), k.stride(), c.tables.reshape(-1),
+                             torch.tensor([r * width for r in c.table_rows]), c.seq_lens,
+                             c.window, c.scale, c.gate, c.num_heads, c.num_kv_heads,
+                             shared_cache=c.shared)
+            total += n * (time.perf_counter() - t0)
+        return total
 
-    def seqs_per_s(self, seconds: float) -> float:
-        seqs = 1 if self.shared else len(self.lens)
-        return seqs / (seconds * self.layers)
+    def seqs_per_s(self, step_seconds: float) -> float:
+        """Query tokens served per second (a shared-cache group counts each of its tokens,
+        as the GPU arm does)."""
+        return self.cases[0][0].tokens / step_seconds
 
-    def describe(self, seconds: float, reps: int) -> str:
+    def describe(self, step_seconds: float, reps: int) -> str:
+        windows = ", ".join(f"{n} x window {c.window}" if c.window else f"{n} x full context"
+                            for c, _, _, n in self.cases)
         return (f"{len(self.lens)} sequence(s) (ctx {min(self.lens)}..{max(self.lens)}, mean "
-                f"{sum(self.lens) / len(self.lens):.0f}) x 1 layer, {seconds:.3f} s each, {reps} "
-                f"repetition(s), scaled to {self.layers} layers; PyTorch eager FP32 restatement "
-                "of the reference semantics (oracle/dory_oracle.py)")
+                f"{sum(self.lens) / len(self.lens):.0f}), one application per distinct window "
+                f"scaled to the step's {self.layers} ({windows}), {step_seconds:.3f} s per "
+                f"step, {reps} repetition(s); PyTorch eager FP32 restatement of the reference "
+                "semantics (oracle/dory_oracle.py)")
 
 
-def cpu_baseline(workload: str, lens_all, budget_s: float):
+def cpu_baseline(workload: str, budget_s: float):
     """Times the CPU sample, repeating it until `budget_s` seconds have passed."""
-    sample = CpuSample(workload, lens_all, budget_s)
+    sample = CpuSample(workload, budget_s)
     sample.once()  # warm-up
     total, reps = 0.0, 0
     while total < budget_s or reps == 0:
@@ -597,10 +758,12 @@ def cpu_baseline(workload: str, lens_all, budget_s: float):
 def bench_reference(args, world, rank, local):
     if rank != 0:
         return
-    lens_all, tps, shared, layers, _, notes = workload_spec(args.workload)
+    spec = workload_spec(args.workload)
+    lens_all, tps, shared, layers, notes = (spec.lens, spec.tokens_per_seq, spec.shared,
+                                            spec.layers, spec.notes)
     # each step is one pass of a bounded sample, sized so the whole run takes minutes
     budget = max(0.05, min(args.cpu_seconds, 120.0 / max(1, args.steps + args.warmup)))
-    sample = CpuSample(args.workload, lens_all, budget)
+    sample = CpuSample(args.workload, budget)
     for _ in range(args.warmup):
         sample.once()
     times = [sample.once() for _ in range(args.steps)]
@@ -630,14 +793,18 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", default="config5")
+    ap.add_argument("--workload", default="config5", choices=WORKLOADS,
+                    help="config1..5: the 32q/8kv x 128 configurations; dory640/2048/8192: "
+                         "the reference benchmark's 16q/4kv x 256 shape")
     ap.add_argument("--splits", type=int, default=None,
                     help="split count (default: the tuned setting of the workload and GPU count)")
     ap.add_argument("--min-blocks-per-split", type=int, default=None)
     ap.add_argument("--overlap-launch", action="store_true",
                     help="launch each layer call as a programmatic dependent of the previous one")
-    ap.add_argument("--path", choices=("fused", "separate"), default="fused",
-                    help="separate: the q/k normalisation kernel then the non-raw call "
+    ap.add_argument("--path", choices=("fused", "separate", "call"), default="fused",
+                    help="call: the non-raw __call__ alone (q normalised and its k/v cached "
+                         "beforehand); separate: the q/k normalisation kernel then the "
+                         "non-raw call "
                          "(single-sequence workloads; the reference's two-kernel path)")
     ap.add_argument("--sumsq", action="store_true",
                     help="also produce each token's sum of squared outputs (out_sumsq)")

@@ -1,0 +1,91 @@
+"""The bench's workload definitions (CPU only): every named workload resolves, the reference
+benchmark's shape (kernels/bench_decode_attention.py: 16q/4kv x 256, the two-loop decode
+order, window 1024 on layers with layer % 4 != 3) is what the dory workloads run, and the
+algorithmic byte count behind the roofline agrees with an independent count over the
+oracle's attended ranges."""
+
+from __future__ import annotations
+
+import random
+import sys
+from pathlib import Path
+
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+sys.path.insert(0, str(ROOT))
+
+import bench  # noqa: E402
+import dory_oracle as O  # noqa: E402
+import workloads as W  # noqa: E402
+
+
+def independent_bytes(seq_lens, shared, window, nh, nkv, hd, block=16):
+    """Counts attended positions and table entries one by one."""
+    ranges = [range(*O.attended(n, window)) for n in seq_lens]
+    if shared:
+        groups = [set().union(*map(set, ranges))]
+    else:
+        groups = [set(r) for r in ranges]
+    unique = sum(len(g) for g in groups)
+    entries = sum(len({p // block for p in g}) for g in groups)
+    token_io = ((nh + nkv) * hd + nkv * hd + 2 * nh * hd) * 4
+    return (unique * nkv * hd * 4 + len(seq_lens) * token_io + nh * hd * 2 + entries * 4
+            + 4 * len(seq_lens))
+
+
+@pytest.mark.parametrize("name", bench.WORKLOADS)
+def test_every_workload_resolves(name):
+    spec = bench.workload_spec(name)
+    splits, mbs = bench.tuned_splits(name, 1)
+    assert splits >= 1 and mbs >= 1
+    assert spec.lens and spec.layers
+    assert spec.nh % spec.nkv == 0 and spec.hd in (64, 128, 256)
+
+
+def test_unknown_workload_is_an_error():
+    with pytest.raises(SystemExit):
+        bench.workload_spec("dory1000")
+
+
+@pytest.mark.parametrize("context", [640, 2048, 8192])
+def test_dory_shape(context):
+    spec = bench.workload_spec(f"dory{context}")
+    assert (spec.nh, spec.nkv, spec.hd) == (16, 4, 256)
+    assert spec.lens == [context] and not spec.shared
+    order = bench.DECODE_ORDER_2_LOOPS
+    assert len(order) == 56 and order[:8] == list(range(8)) and order[-8:] == list(range(28, 36))
+    # one cache per application, window by the decode-order layer it stands for
+    assert spec.layers == list(range(56))
+    for app, layer in enumerate(order):
+        assert spec.window(app) == (1024 if layer % 4 != 3 else 0)
+    assert sum(1 for a in spec.layers if spec.window(a) == 1024) == 42
+
+
+def test_config5_bytes_pinned():
+    """The per-launch byte count the committed config-5 roofline is quoted on."""
+    lens = [n + 1 for n in W.config5_lens()]
+    assert bench.algorithmic_bytes(lens, False, 0, 32, 8, 128) == 4_287_230_696
+
+
+@pytest.mark.parametrize("window", [0, 1, 15, 16, 17, 1024])
+@pytest.mark.parametrize("shared", [False, True])
+def test_bytes_match_independent_count(window, shared):
+    rng = random.Random(window * 2 + shared)
+    if shared:
+        p = rng.randint(1, 3000)
+        lens = [p + t + 1 for t in range(4)]
+    else:
+        lens = [rng.randint(1, 3000) for _ in range(20)] + [1, 16, 17, 1024, 1025]
+    for nh, nkv, hd in ((32, 8, 128), (16, 4, 256), (8, 8, 64)):
+        assert bench.algorithmic_bytes(lens, shared, window, nh, nkv, hd) == \
+            independent_bytes(lens, shared, window, nh, nkv, hd)
+
+
+def test_cpu_sample_weights_windows():
+    sample = bench.CpuSample("dory640", 0.1)
+    weights = {c.window: n for c, _, _, n in sample.cases}
+    assert weights == {0: 14, 1024: 42}
+    for c, _, _, _ in sample.cases:
+        assert (c.num_heads, c.num_kv_heads, c.head_dim) == (16, 4, 256)
+    assert sample.once() > 0
