@@ -256,6 +256,25 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+
+// O^T += V^T P^T over one 16-row stage (256-dim heads): [16 dims x 8 rows] per m-tile (k-step
+// kk) and n-tile.  Lane l gives ldmatrix the address of V row (l & 7) + 8 * (l >> 4) of its
+// matrix; MASK: a lane whose row is outside the attended range (row_ok false) gives the
+// address of a zeroed 16-byte row instead, so that row enters the MMA as zeros.
+template <int KT, int NT, bool MASK>
+__device__ __forceinline__ void pv_accumulate(float (&o)[NT][KT][4], uint32_t vbase_s, int lane,
+                                              const uint32_t (&pb)[NT][2], bool row_ok,
+                                              uint32_t zero_row) {
+  const int vr = (lane & 7) + ((lane >> 4) << 3), vd = ((lane >> 3) & 1) * 8;
+#pragma unroll
+  for (int kk = 0; kk < KT; ++kk) {
+    uint32_t a0, a1, a2, a3;
+    const uint32_t addr = vbase_s + tile_off(vr, kk * 16 + vd);
+    ldsm_x4_t((MASK && !row_ok) ? zero_row : addr, a0, a1, a2, a3);
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) mma_bf16(o[nt][kk], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+  }
+}
 __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
   uint32_t y;
   asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
@@ -345,13 +364,15 @@ __device__ __forceinline__ Split split_layout(int lo, int hi, int B, int b_shift
 
 // ------------------------------------------------------------------------------------
 // Slow path of a ring stage (taken by few chunks):
-//  * tensor path: zero the V rows outside [lo, hi) (all of them for a bad block);
+//  * tensor path, heads up to 128 dims: zero the V rows outside [lo, hi) (all of them for a
+//    bad block); 256-dim heads mask those rows in the MMA instead (pv_accumulate);
 //  * put the new k/v of this call's tokens into the rows that hold their slots (by
 //    position for tokens on this CTA's table, by physical block otherwise), as the
 //    reference uses the new token from registers (dory_decode_attention.py:141-145) and
 //    its shared-cache mode caches every token first (:294-301);
 //  * append: the chunk holding a group token's position writes its k/v to the cache
-//    (slot_mapping[0] in single-token calls, the table's slot in multi-token calls).
+//    (slot_mapping[0] in single-token calls, read at kernel entry into *s_slot for 256-dim
+//    heads; the table's slot in multi-token calls).
 // Returns whether the stage was written (the caller then fences before tensor copies).
 // ------------------------------------------------------------------------------------
 // CTA constants the slow path needs, kept in shared memory so that the hot loop does not
@@ -366,7 +387,7 @@ __device__ __forceinline__ bool fixup_stage(const KParams& p, uint8_t* kst, uint
                                          int phys, bool zero_rows, int lane,
                                          const CtaInfo& ci, const int* s_len, const int* s_phys,
                                          const long long* s_coff, const long long* s_toff,
-                                         const __nv_bfloat16* subkv) {
+                                         const __nv_bfloat16* subkv, const long long* s_slot) {
   const long long coff = ci.coff, toff = ci.toff;
   const int lo = ci.lo, hi = ci.hi, kvh = ci.kvh, nsub = ci.nsub, ibase = ci.ibase;
   const int gcount = ci.gcount;
@@ -411,7 +432,7 @@ __device__ __forceinline__ bool fixup_stage(const KParams& p, uint8_t* kst, uint
       if (phys < 0) continue;  // its block id was out of range (already recorded)
       slot = (long long)phys * B + mod_p2(pos, B, p.b_shift);
     } else {
-      slot = p.slot_mapping[0];
+      slot = HD == 256 ? *s_slot : p.slot_mapping[0];
       if (slot < 0) continue;  // padding token: vLLM does not cache it
     }
     const long long blk = slot / B;
@@ -651,6 +672,12 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   __shared__ int s_len[kMaxSub], s_phys[kMaxSub];
   __shared__ long long s_coff[kMaxSub], s_toff[kMaxSub];
   __shared__ int s_grouped, s_last;
+  // 256-dim heads: edge stages read a zero row in place of each V row outside the attended
+  // range (pv_accumulate), and a single-token call's slot is read at entry.  Narrower heads
+  // keep the zeroing slow path: that code measured faster for them.
+  constexpr bool kRowMask = HD == 256;
+  __shared__ long long s_slot;
+  __shared__ uint4 s_zero_row;
   __shared__ int s_tab[kTab];  // block ids of the first kTab blocks of this CTA's range
   __shared__ CtaInfo s_ci;
   __shared__ float s_wm[kConsumerWarps][ROWS], s_wl[kConsumerWarps][ROWS];
@@ -702,6 +729,10 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     s_len[tid] = p.seq_lens[t];
     s_coff[tid] = p.multi ? p.cache_offsets[t] : 0;
     s_toff[tid] = p.multi ? p.table_offsets[t] : 0;
+  }
+  if (kRowMask) {
+    if (tid == 32) s_slot = (p.raw && !p.multi) ? p.slot_mapping[0] : -1;
+    if (tid == 64) s_zero_row = make_uint4(0u, 0u, 0u, 0u);
   }
   __syncthreads();
   // ---- token group: shared-cache tokens that read one cache through one table share
@@ -1084,9 +1115,9 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     // (zeroing, substitution, the append itself); the rest go straight to the math.
     bool touched = false;
     const bool partial = use_tma && (c < c_full_lo || c >= c_full_hi || phys < 0);
-    if (partial || (c >= sub_lo && c <= sub_hi) || any_foreign)
-      touched = fixup_stage<HD>(p, kst, vst, c, phys, partial, lane, s_ci, s_len, s_phys, s_coff,
-                                s_toff, subkv);
+    if ((partial && !kRowMask) || (c >= sub_lo && c <= sub_hi) || any_foreign)
+      touched = fixup_stage<HD>(p, kst, vst, c, phys, partial && !kRowMask, lane, s_ci, s_len,
+                                s_phys, s_coff, s_toff, subkv, &s_slot);
     __syncwarp();
 
     // S^T = K Q^T : [16 tokens x 8 rows] per n-tile, as two independent MMA chains (even
@@ -1150,7 +1181,17 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
       pb[nt][1] = movmatrix_t(pack_bf16x2(pv[2], pv[3]));
     }
     // O^T += V^T P^T : [16 dims x 8 rows] per m-tile and n-tile.
-    {
+    if constexpr (kRowMask) {
+      // Rows outside [lo, hi) of an edge stage (every row of a bad block, whose stage was
+      // not loaded) may hold anything, NaN included; P is zero there, but 0 * NaN is not.
+      if (partial) {
+        const int pos = c * kChunk + (lane & 7) + ((lane >> 4) << 3);  // this lane's V row
+        const bool row_ok = phys >= 0 && pos >= s_ci.lo && pos < s_ci.hi;
+        pv_accumulate<KT, NT, true>(o, smem_u32(vst), lane, pb, row_ok, smem_u32(&s_zero_row));
+      } else {
+        pv_accumulate<KT, NT, false>(o, smem_u32(vst), lane, pb, true, 0u);
+      }
+    } else {
       const uint32_t vbase_s = smem_u32(vst);
       const int vr = (lane & 7) + ((lane >> 4) << 3), vd = ((lane >> 3) & 1) * 8;
 #pragma unroll
