@@ -173,7 +173,7 @@ def tuned_splits(workload: str, world: int):
     if workload == "config5":
         return (2, 64) if world == 1 else (4, 64)
     return {"config1": (16, 1), "config2": (16, 1), "config3": (2, 32),
-            "config4": (32, 1), "dory640": (8, 1), "dory2048": (16, 1),
+            "config4": (32, 1), "dory640": (16, 1), "dory2048": (32, 1),
             "dory8192": (32, 1)}.get(workload, (2, 64))
 
 
