@@ -974,69 +974,193 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   // Every load of this warp's rows (q, sqk) and of its first sub token (k, v) is issued
   // before any of the arithmetic: one L2 round trip, not one per dependent step.
   constexpr int RPW = ROWS / kConsumerWarps;  // query rows per consumer warp
-  float qv[RPW][PER_LANE], sqv[RPW][PER_LANE], kv0[PER_LANE], vv0[PER_LANE];
+  if constexpr (HD == 256) {
+    const bool sub0 = p.raw && warp < nsub;
+    // 256-dim heads: 16-byte loads where the bases allow them (every row offset is a
+    // multiple of 16 bytes), and in raw mode the FP64 sums of all of this warp's rows (its
+    // query rows and its new token's k row) taken together, each in row_inv_norm's order
+    // (same bits), so that their shuffle chains overlap.
+    const bool vec = ((reinterpret_cast<uintptr_t>(p.q) | reinterpret_cast<uintptr_t>(p.v)) &
+                      15) == 0;
+    const bool vsqk = p.sqk_dtype == DORY_DTYPE_BF16 &&
+                      (reinterpret_cast<uintptr_t>(p.sqk) & 15) == 0;
+    auto load_f32 = [&](const float* src, float (&x)[PER_LANE]) {
+      if (vec) {
 #pragma unroll
-  for (int j = 0; j < RPW; ++j) {
-    const int r = warp + j * kConsumerWarps;
-    if (r >= nrows) continue;
-    const int t = gstart + r / G;
-    const int head = kvh * G + r % G;
+        for (int i = 0; i < PER_LANE; i += 4) {
+          const float4 a = *reinterpret_cast<const float4*>(src + lane * PER_LANE + i);
+          x[i] = a.x; x[i + 1] = a.y; x[i + 2] = a.z; x[i + 3] = a.w;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < PER_LANE; ++i) x[i] = src[lane * PER_LANE + i];
+      }
+    };
+    auto load_bf16 = [&](const __nv_bfloat16* src, bool v16, float (&x)[PER_LANE]) {
+      if (v16) {
+#pragma unroll
+        for (int i = 0; i < PER_LANE; i += 8) {
+          const uint4 w = *reinterpret_cast<const uint4*>(src + lane * PER_LANE + i);
+          const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            x[i + 2 * k] = __uint_as_float(u[k] << 16);
+            x[i + 2 * k + 1] = __uint_as_float(u[k] & 0xffff0000u);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < PER_LANE; ++i) x[i] = __bfloat162float(src[lane * PER_LANE + i]);
+      }
+    };
+    float qv[RPW][PER_LANE], sqv[RPW][PER_LANE], kv0[PER_LANE], vv0[PER_LANE];
+#pragma unroll
+    for (int j = 0; j < RPW; ++j) {
+      const int r = warp + j * kConsumerWarps;
+#pragma unroll
+      for (int i = 0; i < PER_LANE; ++i) qv[j][i] = sqv[j][i] = 0.0f;
+      if (r >= nrows) continue;
+      const int t = gstart + r / G;
+      const int head = kvh * G + r % G;
+      if (p.raw) {
+        load_f32(static_cast<const float*>(p.q) + int64_t(t) * p.q_stride + head * HD, qv[j]);
+        if (vsqk) {
+          load_bf16(static_cast<const __nv_bfloat16*>(p.sqk) + head * HD, true, sqv[j]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < PER_LANE; ++i)
+            sqv[j][i] = load_sqk(p.sqk, p.sqk_dtype, head * HD + lane * PER_LANE + i);
+        }
+      } else {
+        const __nv_bfloat16* src =
+            static_cast<const __nv_bfloat16*>(p.q) + int64_t(t) * p.q_stride + head * HD;
+#pragma unroll
+        for (int i = 0; i < PER_LANE; ++i) qv[j][i] = __bfloat162float(src[lane * PER_LANE + i]);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < PER_LANE; ++i) kv0[i] = vv0[i] = 0.0f;
+    if (sub0) {
+      const int t = p.shared ? warp : tok;
+      load_f32(static_cast<const float*>(p.q) + int64_t(t) * p.q_stride + (p.NH + kvh) * HD, kv0);
+      load_f32(p.v + int64_t(t) * p.NKV * HD + kvh * HD, vv0);
+    }
     if (p.raw) {
-      const float* src = static_cast<const float*>(p.q) + int64_t(t) * p.q_stride + head * HD;
+      double acc[RPW + 1];
 #pragma unroll
-      for (int i = 0; i < PER_LANE; ++i) {
-        qv[j][i] = src[lane * PER_LANE + i];
-        sqv[j][i] = load_sqk(p.sqk, p.sqk_dtype, head * HD + lane * PER_LANE + i);
+      for (int j = 0; j <= RPW; ++j) {
+        acc[j] = 0.0;
+#pragma unroll
+        for (int i = 0; i < PER_LANE; ++i) {
+          const float x = j < RPW ? qv[j][i] : kv0[i];
+          acc[j] += double(x) * double(x);
+        }
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1)
+#pragma unroll
+        for (int j = 0; j <= RPW; ++j) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], off);
+#pragma unroll
+      for (int j = 0; j < RPW; ++j) {
+        const int r = warp + j * kConsumerWarps;
+        const float rn = inv_norm_from_sum(acc[j], p.eps);
+#pragma unroll
+        for (int i = 0; i < PER_LANE; ++i) {
+          const float s = __fmul_rn(sqv[j][i], p.sqk_factor);
+          const float qn = __fmul_rn(qv[j][i], rn);
+          const float qb = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(s, s), qn)));
+          q2[r * HD + lane * PER_LANE + i] =
+              __float2bfloat16_rn(r < nrows ? __fmul_rn(qb, p.scale) : 0.0f);
+        }
+      }
+      if (sub0) {
+        const float rn = inv_norm_from_sum(acc[RPW], p.eps);
+#pragma unroll
+        for (int i = 0; i < PER_LANE; ++i) {
+          const int d = lane * PER_LANE + i;
+          subkv[(warp * 2 + 0) * HD + d] = __float2bfloat16_rn(__fmul_rn(kv0[i], rn));
+          subkv[(warp * 2 + 1) * HD + d] = __float2bfloat16_rn(vv0[i]);
+        }
       }
     } else {
-      const __nv_bfloat16* src =
-          static_cast<const __nv_bfloat16*>(p.q) + int64_t(t) * p.q_stride + head * HD;
 #pragma unroll
-      for (int i = 0; i < PER_LANE; ++i) qv[j][i] = __bfloat162float(src[lane * PER_LANE + i]);
+      for (int j = 0; j < RPW; ++j) {
+        const int r = warp + j * kConsumerWarps;
+        if (r >= nrows) {
+#pragma unroll
+          for (int i = 0; i < PER_LANE; ++i) q2[r * HD + lane * PER_LANE + i] = __float2bfloat16_rn(0.0f);
+          continue;
+        }
+#pragma unroll
+        for (int i = 0; i < PER_LANE; ++i)
+          q2[r * HD + lane * PER_LANE + i] = __float2bfloat16_rn(__fmul_rn(qv[j][i], p.scale));
+      }
     }
-  }
-  const bool sub0 = p.raw && warp < nsub;
-  if (sub0) {
-    const int t = p.shared ? warp : tok;
-    const float* ksrc =
-        static_cast<const float*>(p.q) + int64_t(t) * p.q_stride + (p.NH + kvh) * HD;
-    const float* vsrc = p.v + int64_t(t) * p.NKV * HD + kvh * HD;
+  } else {
+    float qv[RPW][PER_LANE], sqv[RPW][PER_LANE], kv0[PER_LANE], vv0[PER_LANE];
 #pragma unroll
-    for (int i = 0; i < PER_LANE; ++i) {
-      kv0[i] = ksrc[lane * PER_LANE + i];
-      vv0[i] = vsrc[lane * PER_LANE + i];
+    for (int j = 0; j < RPW; ++j) {
+      const int r = warp + j * kConsumerWarps;
+      if (r >= nrows) continue;
+      const int t = gstart + r / G;
+      const int head = kvh * G + r % G;
+      if (p.raw) {
+        const float* src = static_cast<const float*>(p.q) + int64_t(t) * p.q_stride + head * HD;
+#pragma unroll
+        for (int i = 0; i < PER_LANE; ++i) {
+          qv[j][i] = src[lane * PER_LANE + i];
+          sqv[j][i] = load_sqk(p.sqk, p.sqk_dtype, head * HD + lane * PER_LANE + i);
+        }
+      } else {
+        const __nv_bfloat16* src =
+            static_cast<const __nv_bfloat16*>(p.q) + int64_t(t) * p.q_stride + head * HD;
+#pragma unroll
+        for (int i = 0; i < PER_LANE; ++i) qv[j][i] = __bfloat162float(src[lane * PER_LANE + i]);
+      }
     }
-  }
-#pragma unroll
-  for (int j = 0; j < RPW; ++j) {
-    const int r = warp + j * kConsumerWarps;
-    if (r >= nrows) {
-#pragma unroll
-      for (int i = 0; i < PER_LANE; ++i) q2[r * HD + lane * PER_LANE + i] = __float2bfloat16_rn(0.0f);
-      continue;
-    }
-    if (p.raw) {
-      const float rn = row_inv_norm<PER_LANE>(qv[j], p.eps);
+    const bool sub0 = p.raw && warp < nsub;
+    if (sub0) {
+      const int t = p.shared ? warp : tok;
+      const float* ksrc =
+          static_cast<const float*>(p.q) + int64_t(t) * p.q_stride + (p.NH + kvh) * HD;
+      const float* vsrc = p.v + int64_t(t) * p.NKV * HD + kvh * HD;
 #pragma unroll
       for (int i = 0; i < PER_LANE; ++i) {
-        const float s = __fmul_rn(sqv[j][i], p.sqk_factor);
-        const float qn = __fmul_rn(qv[j][i], rn);
-        const float qb = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(s, s), qn)));
-        q2[r * HD + lane * PER_LANE + i] = __float2bfloat16_rn(__fmul_rn(qb, p.scale));
+        kv0[i] = ksrc[lane * PER_LANE + i];
+        vv0[i] = vsrc[lane * PER_LANE + i];
       }
-    } else {
-#pragma unroll
-      for (int i = 0; i < PER_LANE; ++i)
-        q2[r * HD + lane * PER_LANE + i] = __float2bfloat16_rn(__fmul_rn(qv[j][i], p.scale));
     }
-  }
-  if (sub0) {
-    const float rn = row_inv_norm<PER_LANE>(kv0, p.eps);
 #pragma unroll
-    for (int i = 0; i < PER_LANE; ++i) {
-      const int d = lane * PER_LANE + i;
-      subkv[(warp * 2 + 0) * HD + d] = __float2bfloat16_rn(__fmul_rn(kv0[i], rn));
-      subkv[(warp * 2 + 1) * HD + d] = __float2bfloat16_rn(vv0[i]);
+    for (int j = 0; j < RPW; ++j) {
+      const int r = warp + j * kConsumerWarps;
+      if (r >= nrows) {
+#pragma unroll
+        for (int i = 0; i < PER_LANE; ++i) q2[r * HD + lane * PER_LANE + i] = __float2bfloat16_rn(0.0f);
+        continue;
+      }
+      if (p.raw) {
+        const float rn = row_inv_norm<PER_LANE>(qv[j], p.eps);
+#pragma unroll
+        for (int i = 0; i < PER_LANE; ++i) {
+          const float s = __fmul_rn(sqv[j][i], p.sqk_factor);
+          const float qn = __fmul_rn(qv[j][i], rn);
+          const float qb = __bfloat162float(__float2bfloat16_rn(__fmul_rn(__fmul_rn(s, s), qn)));
+          q2[r * HD + lane * PER_LANE + i] = __float2bfloat16_rn(__fmul_rn(qb, p.scale));
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < PER_LANE; ++i)
+          q2[r * HD + lane * PER_LANE + i] = __float2bfloat16_rn(__fmul_rn(qv[j][i], p.scale));
+      }
+    }
+    if (sub0) {
+      const float rn = row_inv_norm<PER_LANE>(kv0, p.eps);
+#pragma unroll
+      for (int i = 0; i < PER_LANE; ++i) {
+        const int d = lane * PER_LANE + i;
+        subkv[(warp * 2 + 0) * HD + d] = __float2bfloat16_rn(__fmul_rn(kv0[i], rn));
+        subkv[(warp * 2 + 1) * HD + d] = __float2bfloat16_rn(vv0[i]);
+      }
     }
   }
   // Further sub tokens of a shared-cache call (more than four).
