@@ -2,7 +2,7 @@
 
 Run here (where the reference checkout is readable), not on the GPU box:
 
-    python tests/golden/make_golden.py [--reference /path/to/dory-vllm-experiments]
+    python tests/golden/make_golden.py --reference /path/to/dory-vllm-experiments
 
 For every case of specs.py it rebuilds the seeded inputs and evaluates them with
 chrisbennight/dory-vllm-experiments' own PyTorch code:
@@ -40,7 +40,8 @@ import specs  # noqa: E402
 
 def main() -> int:
     parser = argparse.ArgumentParser(description=__doc__)
-    parser.add_argument("--reference", default="/root/reference")
+    parser.add_argument("--reference", required=True,
+                        help="checkout of chrisbennight/dory-vllm-experiments (read only)")
     parser.add_argument("--only", default=None)
     args = parser.parse_args()
     sys.path.insert(0, str(Path(args.reference) / "kernels"))
