@@ -168,10 +168,11 @@ WORKLOADS = ("config5", "config1", "config2", "config3", "config4",
 
 def tuned_splits(workload: str, world: int):
     """(splits, min_blocks_per_split) measured fastest on B200 for each workload; config 5
-    uses 4 splits once its 512 sequences are partitioned over 2+ GPUs (fewer, longer
-    sequences per GPU: finer splits even out the last wave)."""
+    uses 4 splits once its 512 sequences are partitioned over 2+ GPUs, and 8 splits of at
+    least 96 blocks at 8+ GPUs (fewer, longer sequences per GPU: finer splits of the long
+    ones even out the last wave; measured on one GPU's share of each partition)."""
     if workload == "config5":
-        return (2, 64) if world == 1 else (4, 64)
+        return (2, 64) if world == 1 else (4, 64) if world < 8 else (8, 96)
     return {"config1": (16, 1), "config2": (16, 1), "config3": (2, 32),
             "config4": (32, 1), "dory640": (16, 1), "dory2048": (32, 1),
             "dory8192": (32, 1)}.get(workload, (2, 64))
