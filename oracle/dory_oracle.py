@@ -19,6 +19,8 @@ chrisbennight/dory-vllm-experiments:
 * padding: seq_len 0 gives a zero output (:218-219), slot < 0 writes nothing (:118);
 * gate product and the nibble-major store out[e % 8][e / 8] (:220-222,
   kernels/w4a16_gemv.py:91-93);
+* the multi-token path's q/k/v/gate epilogue (kernels/dory_multi_token.py:53-80): split-K
+  sum, rotary embedding on adjacent row pairs, the scaled sigmoid output gate;
 * multi-token calls (:270-305): token t uses cache_offsets[t] and block_table_offsets[t];
   shared_cache=True caches every token's k/v before any attention (:294-301), which the
   reference's own test checks against single-token calls in position order
@@ -253,6 +255,52 @@ def split_layout(seq_len: int, window: int, block_size: int, splits: int,
     num_blocks = -(-seq_len // block_size) - first_block
     tiles = -(-num_blocks // blocks_per_tile)
     return seq_len, first, first_block, tiles, max(-(-tiles // splits), 1)
+
+
+# ---------------------------------------------------------------------------------------
+# the multi-token q/k/v/gate epilogue (kernels/dory_multi_token.py:53-80,
+# _qkvg_epilogue_kernel): the producer of multi_from_raw's inputs in the wavefront path
+# ---------------------------------------------------------------------------------------
+
+def qkvg_epilogue(partials: torch.Tensor, positions, cos_sin: torch.Tensor,
+                  s_gate: torch.Tensor, s_gate_factor: float, num_heads: int,
+                  num_kv_heads: int, head_dim: int):
+    """Split-K GEMV partials FP32 [split_k, T, 2 * (Q + KV)] (rows: q heads, k heads,
+    v heads, output gate; Q = heads * head_dim, KV = kv_heads * head_dim) ->
+    (qk FP32 [T, Q + KV], v FP32 [T, KV], gate FP32 [T, Q]).
+
+    y = 0 + p_0 + p_1 + ... in split order (:63-65).  Rows 2i and 2i + 1 of a q or k head
+    hold rotary dims i and i + head_dim / 2 (:66-76): out[i] = first * cos - second * sin,
+    out[i + half] = second * cos + first * sin, cos = cos_sin[position, i], sin =
+    cos_sin[position, half + i] as FP32; every product and sum rounded on its own (FP32,
+    no fused multiply-add).  v = y (:77-78); gate = sigmoid(y * s * s) with s =
+    float(s_gate) * s_gate_factor (:79-82)."""
+    p = np.asarray(partials, dtype=np.float32)
+    split_k, T, rows = p.shape
+    Q, KV, HD = num_heads * head_dim, num_kv_heads * head_dim, head_dim
+    if rows != 2 * (Q + KV):
+        raise ValueError("partials rows must be 2 * (Q + KV)")
+    y = np.zeros((T, rows), dtype=np.float32)
+    for k in range(split_k):
+        y = (y + p[k]).astype(np.float32)
+    half = HD // 2
+    cs = np.asarray(cos_sin.float() if isinstance(cos_sin, torch.Tensor) else cos_sin,
+                    dtype=np.float32)
+    pos = np.asarray(positions, dtype=np.int64).reshape(T)
+    heads = num_heads + num_kv_heads
+    pairs = y[:, :Q + KV].reshape(T, heads, half, 2)
+    first, second = pairs[..., 0], pairs[..., 1]
+    cos = cs[pos, :half][:, None, :]
+    sin = cs[pos, half:HD][:, None, :]
+    lo = ((first * cos).astype(np.float32) - (second * sin).astype(np.float32)).astype(np.float32)
+    hi = ((second * cos).astype(np.float32) + (first * sin).astype(np.float32)).astype(np.float32)
+    qk = np.concatenate([lo, hi], axis=-1).reshape(T, Q + KV)
+    v = y[:, Q + KV:Q + 2 * KV]
+    s = (np.asarray(s_gate.float() if isinstance(s_gate, torch.Tensor) else s_gate,
+                    dtype=np.float32) * np.float32(s_gate_factor)).astype(np.float32)
+    z = ((y[:, Q + 2 * KV:] * s).astype(np.float32) * s).astype(np.float32)
+    gate = torch.sigmoid(torch.from_numpy(z)).numpy()
+    return torch.from_numpy(qk.copy()), torch.from_numpy(v.copy()), torch.from_numpy(gate)
 
 
 def relative_error(x: torch.Tensor, reference: torch.Tensor) -> float:

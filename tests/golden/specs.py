@@ -52,3 +52,46 @@ def digest(case: W.Case) -> str:
     h.update(np.asarray(case.seq_lens, dtype=np.int64).tobytes())
     h.update(np.asarray(case.table_rows, dtype=np.int64).tobytes())
     return h.hexdigest()
+
+
+# ---- the multi-token q/k/v/gate epilogue (kernels/dory_multi_token.py:53-80) ----
+
+class QkvgCase:
+    """Seeded inputs of the epilogue: split-K partials FP32 [split_k, T, 2 * (Q + KV)],
+    positions int64 [T], cos_sin [max_position, head_dim] (FP32 or BF16), s_gate BF16 [Q]."""
+
+    def __init__(self, seed: int, num_heads: int, num_kv_heads: int, head_dim: int,
+                 split_k: int, tokens: int, cos_dtype=torch.float32, max_position: int = 4096,
+                 s_gate_factor: float = 0.9):
+        g = torch.Generator().manual_seed(seed)
+        self.num_heads, self.num_kv_heads, self.head_dim = num_heads, num_kv_heads, head_dim
+        Q, KV = num_heads * head_dim, num_kv_heads * head_dim
+        self.partials = torch.randn(split_k, tokens, 2 * (Q + KV), generator=g)
+        self.positions = torch.randint(0, max_position, (tokens,), generator=g)
+        self.cos_sin = torch.randn(max_position, head_dim, generator=g).to(cos_dtype)
+        self.s_gate = (torch.rand(Q, generator=g) + 0.5).to(torch.bfloat16)
+        self.s_gate_factor = s_gate_factor
+
+    @property
+    def tokens(self) -> int:
+        return self.partials.shape[1]
+
+
+def qkvg_specs() -> dict:
+    """name -> zero-argument builder of a QkvgCase."""
+    return {
+        "qkvg_128": lambda: QkvgCase(41, 4, 2, 128, 2, 3),
+        "qkvg_256_bf16cos": lambda: QkvgCase(42, 2, 1, 256, 3, 2, cos_dtype=torch.bfloat16),
+        "qkvg_64_t1": lambda: QkvgCase(43, 4, 4, 64, 1, 1),
+        "qkvg_gqa8_split4": lambda: QkvgCase(44, 8, 1, 128, 4, 2, max_position=9000),
+        # the real model's shape: 16q/4kv x 256, four wavefront rows
+        "qkvg_dory": lambda: QkvgCase(45, 16, 4, 256, 2, 4, cos_dtype=torch.bfloat16,
+                                      max_position=8300),
+    }
+
+
+def qkvg_digest(case: QkvgCase) -> str:
+    h = hashlib.sha256()
+    for t in (case.partials, case.positions, case.cos_sin.float(), case.s_gate.float()):
+        h.update(t.contiguous().numpy().tobytes())
+    return h.hexdigest()
