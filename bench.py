@@ -356,7 +356,7 @@ def prepare_call_path(wl: DeviceWorkload):
     """`--path call`: each layer's bf16 query from its raw q/k (the q/k normalisation kernel,
     which also appends the layer's new k/v), made once before timing; every timed call then
     finds its K/V already in the cache, as the reference's non-raw `__call__` expects."""
-    from dory_attention import qk_norm_cache
+    from dory_sublayer_steps import qk_norm_cache
     from dory_decode_attention import EPS
     wl.q_call = torch.empty(wl.num_layers, 1, wl.nh * wl.hd, dtype=torch.bfloat16, device=wl.dev)
     for layer in range(wl.num_layers):
@@ -389,7 +389,7 @@ def layer_call(attn, wl: DeviceWorkload, app: int, layer: int, ins, out):
     if wl.path == "separate":
         # The reference's separate path (bench_decode_attention.py:144-152): the q/k
         # normalisation kernel writes the cache and the bf16 query, then __call__ attends.
-        from dory_attention import qk_norm_cache
+        from dory_sublayer_steps import qk_norm_cache
         qk_norm_cache(qk[0], v[0], wl.sqk, W.SQK_FACTOR, EPS, wl.q_out[0], wl.nh, wl.hd,
                       key_cache=key, value_cache=value, slot_mapping=wl.slots[0:1])
         attn(wl.q_out[0], key, value, wl.tables[0], wl.seq_lens[0:1], window, scale, gate[0],

@@ -13,7 +13,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 LIBRARY = HERE / "libdory_decode.so"
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 # DoryStatus
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_ALIGNMENT, ERR_CUDA = range(5)
@@ -21,19 +21,23 @@ OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_ALIGNMENT, ERR_CUDA = range(5)
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = range(3)
 # DORY_FLAG_*
 FLAG_RAW_QKV, FLAG_MULTI_TOKEN, FLAG_SHARED_CACHE, FLAG_OVERLAP_LAUNCH = 1, 2, 4, 8
+FLAG_QKVG_PARTIALS = 16
 # DORY_QKNORM_*
 QKNORM_WRITE_CACHE = 1
 # DORY_DEVERR_*
 DEVERR_BLOCK_OOB, DEVERR_SLOT_OOB, DEVERR_OFFSET_ALIGN, DEVERR_WAIT_TIMEOUT = 1, 2, 4, 8
+DEVERR_POSITION_OOB = 16
 DEVERR_NAMES = {DEVERR_BLOCK_OOB: "block id out of range", DEVERR_SLOT_OOB: "slot out of range",
                 DEVERR_OFFSET_ALIGN: "cache offset not 16-byte aligned",
-                DEVERR_WAIT_TIMEOUT: "pipeline wait timed out"}
+                DEVERR_WAIT_TIMEOUT: "pipeline wait timed out",
+                DEVERR_POSITION_OOB: "rotary position outside the cos/sin table"}
 
 # Every symbol include/dory_decode.h declares (checked by the CPU test suite).
 EXPORTS = ("dory_decode_abi_version", "dory_decode_params_bytes", "dory_decode_scratch_bytes",
            "dory_decode_scratch_init", "dory_decode_attention", "dory_decode_fetch_errors",
            "dory_decode_last_error", "dory_decode_attention_static_scratch",
-           "dory_qk_norm_params_bytes", "dory_qk_norm_cache")
+           "dory_qk_norm_params_bytes", "dory_qk_norm_cache", "dory_qkvg_params_bytes",
+           "dory_qkvg_epilogue")
 
 # Size of the library's static scratch array (DORY_DECODE_STATIC_SCRATCH_BYTES).
 STATIC_SCRATCH_BYTES = 4 << 20
@@ -55,6 +59,9 @@ class DoryDecodeParams(ctypes.Structure):
         ("block_size", _i32), ("window", _i32), ("splits", _i32), ("blocks_per_tile", _i32),
         ("min_blocks_per_split", _i32), ("max_tokens", _i32), ("sqk_dtype", _i32),
         ("flags", _u32),
+        ("qkvg_partials", _vp), ("positions", _vp), ("cos_sin", _vp), ("s_gate", _vp),
+        ("s_gate_factor", _f32), ("split_k", _i32), ("max_position", _i32),
+        ("positions_dtype", _i32), ("cos_sin_dtype", _i32), ("s_gate_dtype", _i32),
     ]
 
 
@@ -67,6 +74,17 @@ class DoryQkNormParams(ctypes.Structure):
         ("stride_head", _i64), ("num_cache_blocks", _i64), ("sqk_factor", _f32), ("eps", _f32),
         ("num_tokens", _i32), ("num_heads", _i32), ("num_kv_heads", _i32), ("head_dim", _i32),
         ("block_size", _i32), ("sqk_dtype", _i32), ("flags", _u32),
+    ]
+
+
+class DoryQkvgParams(ctypes.Structure):
+    """Mirror of DoryQkvgParams (include/dory_decode.h); field order is the ABI."""
+    _fields_ = [
+        ("partials", _vp), ("positions", _vp), ("cos_sin", _vp), ("s_gate", _vp),
+        ("qk_out", _vp), ("v_out", _vp), ("gate_out", _vp), ("error_word", _vp),
+        ("s_gate_factor", _f32), ("num_tokens", _i32), ("num_heads", _i32),
+        ("num_kv_heads", _i32), ("head_dim", _i32), ("split_k", _i32), ("max_position", _i32),
+        ("positions_dtype", _i32), ("cos_sin_dtype", _i32), ("s_gate_dtype", _i32),
     ]
 
 
@@ -104,6 +122,10 @@ def load(path: os.PathLike | None = None) -> ctypes.CDLL:
     lib.dory_qk_norm_params_bytes.argtypes = []
     lib.dory_qk_norm_cache.restype = _i32
     lib.dory_qk_norm_cache.argtypes = [ctypes.POINTER(DoryQkNormParams), _vp]
+    lib.dory_qkvg_params_bytes.restype = _i64
+    lib.dory_qkvg_params_bytes.argtypes = []
+    lib.dory_qkvg_epilogue.restype = _i32
+    lib.dory_qkvg_epilogue.argtypes = [ctypes.POINTER(DoryQkvgParams), _vp]
     if lib.dory_decode_abi_version() != ABI_VERSION:
         raise RuntimeError(f"{path}: ABI version {lib.dory_decode_abi_version()} != {ABI_VERSION}")
     if lib.dory_decode_params_bytes() != ctypes.sizeof(DoryDecodeParams):
@@ -112,6 +134,9 @@ def load(path: os.PathLike | None = None) -> ctypes.CDLL:
     if lib.dory_qk_norm_params_bytes() != ctypes.sizeof(DoryQkNormParams):
         raise RuntimeError(f"{path}: DoryQkNormParams is {lib.dory_qk_norm_params_bytes()} "
                            f"bytes, the binding's is {ctypes.sizeof(DoryQkNormParams)}")
+    if lib.dory_qkvg_params_bytes() != ctypes.sizeof(DoryQkvgParams):
+        raise RuntimeError(f"{path}: DoryQkvgParams is {lib.dory_qkvg_params_bytes()} "
+                           f"bytes, the binding's is {ctypes.sizeof(DoryQkvgParams)}")
     _lib = lib
     return lib
 

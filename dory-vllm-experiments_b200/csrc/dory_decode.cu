@@ -102,6 +102,13 @@ struct alignas(64) KParams {
   float scale, sqk_factor, eps;
   int min_bps, sqk_dtype, overlap;
   int tm_mode;   // 0: no tensor maps; 1: tmk covers K and V (V right after K); 2: tmk, tmv
+  // QK mode (DORY_FLAG_QKVG_PARTIALS): q, k, v and the gate from the split-K GEMV partials
+  const float* pq;        // [split_k][T][prow]
+  const void* positions;  // [T] int64 (pos_dtype 0) or int32
+  const void* cos_sin;    // [max_position][HD]: cos, then sin
+  const void* s_gate;     // [Q]
+  float s_gate_factor;
+  int split_k, prow, max_position, pos_dtype, cos_dtype, sgate_dtype, qk;
   CUtensorMap tmk;  // cache views as 5-D tensors (64 dims, rows, 64-dim quarters of a row,
   CUtensorMap tmv;  // KV head, block), one box = a chunk's K (and V) tile, 128-byte swizzle
 };
@@ -298,6 +305,88 @@ __device__ __forceinline__ float load_sqk(const void* sqk, int dtype, int64_t i)
   return static_cast<const float*>(sqk)[i];
 }
 
+// ---- QK mode: the multi-token path's q/k/v/gate epilogue (reference _qkvg_epilogue_kernel,
+//      kernels/dory_multi_token.py:53-80), computed where each value is used ----
+// Rotary position of token t, or -1 (recorded) outside the cos/sin table.
+__device__ __forceinline__ int64_t token_position(const KParams& p, int t) {
+  const int64_t pos = p.pos_dtype == 0 ? static_cast<const int64_t*>(p.positions)[t]
+                                       : int64_t(static_cast<const int32_t*>(p.positions)[t]);
+  if (pos < 0 || pos >= p.max_position) {
+    record_error(p.err, DORY_DEVERR_POSITION_OOB);
+    return -1;
+  }
+  return pos;
+}
+// y[i] = 0 + p_0[row + i] + p_1[row + i] + ... over the split-K partials in order (the
+// reference's `y += tl.load(...)` from zeros).  row is a multiple of N (N = 2, 4, 8, 16), the
+// partials 16-byte aligned, so the loads are vectors.
+template <int N>
+__device__ __forceinline__ void partial_rows(const KParams& p, int t, int64_t row,
+                                             float (&y)[N]) {
+#pragma unroll
+  for (int i = 0; i < N; ++i) y[i] = 0.0f;
+  for (int k = 0; k < p.split_k; ++k) {
+    const float* src = p.pq + (int64_t(k) * p.T + t) * p.prow + row;
+    if constexpr (N % 4 == 0) {
+#pragma unroll
+      for (int i = 0; i < N; i += 4) {
+        const float4 a = __ldg(reinterpret_cast<const float4*>(src + i));
+        y[i] = __fadd_rn(y[i], a.x);
+        y[i + 1] = __fadd_rn(y[i + 1], a.y);
+        y[i + 2] = __fadd_rn(y[i + 2], a.z);
+        y[i + 3] = __fadd_rn(y[i + 3], a.w);
+      }
+    } else {
+      static_assert(N == 2, "row runs of 2 or a multiple of 4");
+      const float2 a = __ldg(reinterpret_cast<const float2*>(src));
+      y[0] = __fadd_rn(y[0], a.x);
+      y[1] = __fadd_rn(y[1], a.y);
+    }
+  }
+}
+// This lane's PER_LANE natural dims [lane * PER_LANE, +PER_LANE) of q or k head `head` of
+// token t with the rotary embedding applied: rows 2i, 2i + 1 of the head are dims i and
+// i + HD / 2, out[i] = first * cos - second * sin and out[i + HD / 2] = second * cos +
+// first * sin, each product and sum rounded on its own.
+template <int PER_LANE, int HD>
+__device__ __forceinline__ void rope_row(const KParams& p, int t, int64_t pos, int head,
+                                         int lane, float (&out)[PER_LANE]) {
+  constexpr int HALF = HD / 2;
+  static_assert(HALF % PER_LANE == 0, "a lane's dims lie in one half of the head");
+  const int d0 = lane * PER_LANE;
+  const bool hi = d0 >= HALF;
+  const int j0 = hi ? d0 - HALF : d0;
+  float y[2 * PER_LANE];
+  partial_rows<2 * PER_LANE>(p, t, int64_t(head) * HD + 2 * j0, y);
+#pragma unroll
+  for (int i = 0; i < PER_LANE; ++i) {
+    if (pos < 0) {
+      out[i] = 0.0f;
+      continue;
+    }
+    const float c = load_sqk(p.cos_sin, p.cos_dtype, pos * HD + j0 + i);
+    const float sn = load_sqk(p.cos_sin, p.cos_dtype, pos * HD + HALF + j0 + i);
+    const float first = y[2 * i], second = y[2 * i + 1];
+    out[i] = hi ? __fadd_rn(__fmul_rn(second, c), __fmul_rn(first, sn))
+                : __fsub_rn(__fmul_rn(first, c), __fmul_rn(second, sn));
+  }
+}
+// The output gate of elements e0 .. e0 + 3 (e0 a multiple of 4) of token t: sigmoid((y * s)
+// * s), s = s_gate[e] * s_gate_factor; the gate rows are the last Q rows of the partials.
+template <int HD>
+__device__ __forceinline__ float4 gate4_partials(const KParams& p, int t, int e0) {
+  float y[4];
+  partial_rows<4>(p, t, int64_t(p.prow) - int64_t(p.NH) * HD + e0, y);
+  float g[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float s = __fmul_rn(load_sqk(p.s_gate, p.sgate_dtype, e0 + i), p.s_gate_factor);
+    const float z = __fmul_rn(__fmul_rn(y[i], s), s);
+    g[i] = 1.0f / (1.0f + expf(-z));
+  }
+  return make_float4(g[0], g[1], g[2], g[3]);
+}
+
 // Canonical normalisation factor of one row: Sum x^2 is accumulated in FP64 (every square
 // is exact there and the sum carries 29 more bits than FP32, so its FP32 rounding depends on
 // the summation order only when the sum lies within ~2^-53 of an FP32 rounding boundary),
@@ -455,7 +544,7 @@ __device__ __forceinline__ bool fixup_stage(const KParams& p, uint8_t* kst, uint
 // Cross-split merge of one (token group, KV head) by its last CTA: thread tid owns output
 // units tid + k * 128 (k < UPT), a unit being 4 consecutive dims of one query row.
 // ------------------------------------------------------------------------------------
-template <int HD, int UPT, int SB, bool SS>
+template <int HD, int UPT, int SB, bool SS, bool QK>
 __device__ __forceinline__ void merge_splits(const KParams& p, int tid, int nrows, int gstart,
                                              int kvh, int G, int active, float* sv) {
   constexpr int UPR = HD / 4;  // float4 units per row
@@ -478,8 +567,11 @@ __device__ __forceinline__ void merge_splits(const KParams& p, int tid, int nrow
     acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
     Mx[k] = -INFINITY;
     Ls[k] = 0.0f;
-    gt[k] = u < units ? *reinterpret_cast<const float4*>(p.gate + int64_t(t) * Q + head * HD + d4 * 4)
-                      : make_float4(0.f, 0.f, 0.f, 0.f);
+    if constexpr (QK)
+      gt[k] = u < units ? gate4_partials<HD>(p, t, head * HD + d4 * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    else
+      gt[k] = u < units ? *reinterpret_cast<const float4*>(p.gate + int64_t(t) * Q + head * HD + d4 * 4)
+                        : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   for (int s0 = 0; s0 < active; s0 += SB) {
     float4 v[UPT][SB];
@@ -540,7 +632,7 @@ __device__ __forceinline__ void merge_splits(const KParams& p, int tid, int nrow
 // flight together (one L2 round trip per batch; the gate rides along the first), each
 // folded in with one max, independent weights and one rescale.
 // ------------------------------------------------------------------------------------
-template <int HD, int UPT, int SB, bool SS>
+template <int HD, int UPT, int SB, bool SS, bool QK>
 __device__ __forceinline__ void merge_splits_rows(const KParams& p, int tid, int nrows, int gstart,
                                              int kvh, int G, int active, float* sv) {
   constexpr int UPR = HD / 4;  // float4 units per row
@@ -560,8 +652,11 @@ __device__ __forceinline__ void merge_splits_rows(const KParams& p, int tid, int
 #pragma unroll
   for (int k = 0; k < UPT; ++k) {
     acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    gt[k] = mine ? *reinterpret_cast<const float4*>(p.gate + int64_t(t) * Q + head * HD + (d40 + k) * 4)
-                 : make_float4(0.f, 0.f, 0.f, 0.f);
+    if constexpr (QK)
+      gt[k] = mine ? gate4_partials<HD>(p, t, head * HD + (d40 + k) * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
+    else
+      gt[k] = mine ? *reinterpret_cast<const float4*>(p.gate + int64_t(t) * Q + head * HD + (d40 + k) * 4)
+                   : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   for (int s0 = 0; s0 < active; s0 += SB) {
     float4 v[SB][UPT];
@@ -656,7 +751,7 @@ __device__ __forceinline__ void sumsq_tail(const KParams& p, const float* sv, in
 // ------------------------------------------------------------------------------------
 // The kernel.  grid = (splits, NKV, T); block = 160 threads (4 consumer warps + producer).
 // ------------------------------------------------------------------------------------
-template <int HD, int NT, int NS, bool SS>
+template <int HD, int NT, int NS, bool SS, bool QK>
 __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     decode_kernel(const __grid_constant__ KParams p) {
   using L = Smem<HD, NS>;
@@ -706,7 +801,17 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     // pulling them into L2 now, while that first load is in flight.
     const int hq = kvh * G;
     const int64_t qrow = int64_t(tok) * p.q_stride;
-    if (p.raw) {
+    if constexpr (QK) {
+      // This token's q rows, k and v rows and gate rows in every split-K slice.
+      const int KV = p.NKV * HD;
+      for (int k = 0; k < p.split_k; ++k) {
+        const float* sl = p.pq + (int64_t(k) * p.T + tok) * p.prow;
+        prefetch_range(sl + hq * HD, G * HD * 4, lane);
+        prefetch_range(sl + Q + kvh * HD, HD * 4, lane);
+        prefetch_range(sl + Q + KV + kvh * HD, HD * 4, lane);
+        prefetch_range(sl + Q + 2 * KV + hq * HD, G * HD * 4, lane);
+      }
+    } else if (p.raw) {
       const float* qf = static_cast<const float*>(p.q) + qrow;
       prefetch_range(qf + hq * HD, G * HD * 4, lane);
       prefetch_range(qf + (p.NH + kvh) * HD, HD * 4, lane);
@@ -717,7 +822,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     } else {
       prefetch_range(static_cast<const __nv_bfloat16*>(p.q) + qrow + hq * HD, G * HD * 2, lane);
     }
-    prefetch_range(p.gate + int64_t(tok) * Q + hq * HD, G * HD * 4, lane);
+    if constexpr (!QK) prefetch_range(p.gate + int64_t(tok) * Q + hq * HD, G * HD * 4, lane);
     if (p.tm_mode && lane == 0) {
       prefetch_tensormap(&p.tmk);
       if (p.tm_mode == 2) prefetch_tensormap(&p.tmv);
@@ -781,7 +886,14 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
         const int r = i / HD, d = i % HD;
         const int t = gstart + r / G, head = kvh * G + r % G;
         const int e = head * HD + d;
-        const float val = 0.0f * p.gate[int64_t(t) * Q + e];
+        float gv;
+        if constexpr (QK) {
+          const float4 g4 = gate4_partials<HD>(p, t, e & ~3);
+          gv = (e & 3) == 0 ? g4.x : (e & 3) == 1 ? g4.y : (e & 3) == 2 ? g4.z : g4.w;
+        } else {
+          gv = p.gate[int64_t(t) * Q + e];
+        }
+        const float val = 0.0f * gv;
         p.out[int64_t(t) * Q + (e % 8) * (Q / 8) + e / 8] = val;
         if (SS) sv0[i] = val * val;
       }
@@ -974,7 +1086,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   // Every load of this warp's rows (q, sqk) and of its first sub token (k, v) is issued
   // before any of the arithmetic: one L2 round trip, not one per dependent step.
   constexpr int RPW = ROWS / kConsumerWarps;  // query rows per consumer warp
-  if constexpr (HD == 256) {
+  if constexpr (HD == 256 || QK) {
     const bool sub0 = p.raw && warp < nsub;
     // 256-dim heads: 16-byte loads where the bases allow them (every row offset is a
     // multiple of 16 bytes), and in raw mode the FP64 sums of all of this warp's rows (its
@@ -982,7 +1094,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     // (same bits), so that their shuffle chains overlap.
     const bool vec = ((reinterpret_cast<uintptr_t>(p.q) | reinterpret_cast<uintptr_t>(p.v)) &
                       15) == 0;
-    const bool vsqk = p.sqk_dtype == DORY_DTYPE_BF16 &&
+    const bool vsqk = PER_LANE % 8 == 0 && p.sqk_dtype == DORY_DTYPE_BF16 &&
                       (reinterpret_cast<uintptr_t>(p.sqk) & 15) == 0;
     auto load_f32 = [&](const float* src, float (&x)[PER_LANE]) {
       if (vec) {
@@ -997,18 +1109,22 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
       }
     };
     auto load_bf16 = [&](const __nv_bfloat16* src, bool v16, float (&x)[PER_LANE]) {
-      if (v16) {
+      if constexpr (PER_LANE % 8 == 0) {
+        if (v16) {
 #pragma unroll
-        for (int i = 0; i < PER_LANE; i += 8) {
-          const uint4 w = *reinterpret_cast<const uint4*>(src + lane * PER_LANE + i);
-          const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+          for (int i = 0; i < PER_LANE; i += 8) {
+            const uint4 w = *reinterpret_cast<const uint4*>(src + lane * PER_LANE + i);
+            const uint32_t u[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-          for (int k = 0; k < 4; ++k) {
-            x[i + 2 * k] = __uint_as_float(u[k] << 16);
-            x[i + 2 * k + 1] = __uint_as_float(u[k] & 0xffff0000u);
+            for (int k = 0; k < 4; ++k) {
+              x[i + 2 * k] = __uint_as_float(u[k] << 16);
+              x[i + 2 * k + 1] = __uint_as_float(u[k] & 0xffff0000u);
+            }
           }
+          return;
         }
-      } else {
+      }
+      {
 #pragma unroll
         for (int i = 0; i < PER_LANE; ++i) x[i] = __bfloat162float(src[lane * PER_LANE + i]);
       }
@@ -1022,7 +1138,12 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
       if (r >= nrows) continue;
       const int t = gstart + r / G;
       const int head = kvh * G + r % G;
-      if (p.raw) {
+      if constexpr (QK) {
+        rope_row<PER_LANE, HD>(p, t, token_position(p, t), head, lane, qv[j]);
+#pragma unroll
+        for (int i = 0; i < PER_LANE; ++i)
+          sqv[j][i] = load_sqk(p.sqk, p.sqk_dtype, head * HD + lane * PER_LANE + i);
+      } else if (p.raw) {
         load_f32(static_cast<const float*>(p.q) + int64_t(t) * p.q_stride + head * HD, qv[j]);
         if (vsqk) {
           load_bf16(static_cast<const __nv_bfloat16*>(p.sqk) + head * HD, true, sqv[j]);
@@ -1042,8 +1163,13 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     for (int i = 0; i < PER_LANE; ++i) kv0[i] = vv0[i] = 0.0f;
     if (sub0) {
       const int t = p.shared ? warp : tok;
-      load_f32(static_cast<const float*>(p.q) + int64_t(t) * p.q_stride + (p.NH + kvh) * HD, kv0);
-      load_f32(p.v + int64_t(t) * p.NKV * HD + kvh * HD, vv0);
+      if constexpr (QK) {
+        rope_row<PER_LANE, HD>(p, t, token_position(p, t), p.NH + kvh, lane, kv0);
+        partial_rows<PER_LANE>(p, t, int64_t(p.NH + p.NKV + kvh) * HD + lane * PER_LANE, vv0);
+      } else {
+        load_f32(static_cast<const float*>(p.q) + int64_t(t) * p.q_stride + (p.NH + kvh) * HD, kv0);
+        load_f32(p.v + int64_t(t) * p.NKV * HD + kvh * HD, vv0);
+      }
     }
     if (p.raw) {
       double acc[RPW + 1];
@@ -1167,18 +1293,31 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   if (p.raw) {
     for (int s = warp + kConsumerWarps; s < nsub; s += kConsumerWarps) {
       const int t = p.shared ? s : tok;
-      const float* ksrc =
-          static_cast<const float*>(p.q) + int64_t(t) * p.q_stride + (p.NH + kvh) * HD;
-      const float* vsrc = p.v + int64_t(t) * p.NKV * HD + kvh * HD;
-      float kv[PER_LANE];
+      if constexpr (QK) {
+        float kv[PER_LANE], vv[PER_LANE];
+        rope_row<PER_LANE, HD>(p, t, token_position(p, t), p.NH + kvh, lane, kv);
+        partial_rows<PER_LANE>(p, t, int64_t(p.NH + p.NKV + kvh) * HD + lane * PER_LANE, vv);
+        const float rn = row_inv_norm<PER_LANE>(kv, p.eps);
 #pragma unroll
-      for (int i = 0; i < PER_LANE; ++i) kv[i] = ksrc[lane * PER_LANE + i];
-      const float rn = row_inv_norm<PER_LANE>(kv, p.eps);
+        for (int i = 0; i < PER_LANE; ++i) {
+          const int d = lane * PER_LANE + i;
+          subkv[(s * 2 + 0) * HD + d] = __float2bfloat16_rn(__fmul_rn(kv[i], rn));
+          subkv[(s * 2 + 1) * HD + d] = __float2bfloat16_rn(vv[i]);
+        }
+      } else {
+        const float* ksrc =
+            static_cast<const float*>(p.q) + int64_t(t) * p.q_stride + (p.NH + kvh) * HD;
+        const float* vsrc = p.v + int64_t(t) * p.NKV * HD + kvh * HD;
+        float kv[PER_LANE];
 #pragma unroll
-      for (int i = 0; i < PER_LANE; ++i) {
-        const int d = lane * PER_LANE + i;
-        subkv[(s * 2 + 0) * HD + d] = __float2bfloat16_rn(__fmul_rn(kv[i], rn));
-        subkv[(s * 2 + 1) * HD + d] = __float2bfloat16_rn(vsrc[d]);
+        for (int i = 0; i < PER_LANE; ++i) kv[i] = ksrc[lane * PER_LANE + i];
+        const float rn = row_inv_norm<PER_LANE>(kv, p.eps);
+#pragma unroll
+        for (int i = 0; i < PER_LANE; ++i) {
+          const int d = lane * PER_LANE + i;
+          subkv[(s * 2 + 0) * HD + d] = __float2bfloat16_rn(__fmul_rn(kv[i], rn));
+          subkv[(s * 2 + 1) * HD + d] = __float2bfloat16_rn(vsrc[d]);
+        }
       }
     }
   }
@@ -1418,14 +1557,25 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     if (single) {
       const float inv = 1.0f / (Lsum > 0.0f ? Lsum : 1.0f);
       const int e0 = head * HD + k8 * 8;
-      const float* gt = p.gate + int64_t(t) * Q + e0;
       float* out = p.out + int64_t(t) * Q + e0 / 8;
       float ss = 0.0f;
+      if constexpr (QK) {
+        const float4 ga = gate4_partials<HD>(p, t, e0), gb = gate4_partials<HD>(p, t, e0 + 4);
+        const float gt[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
 #pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        const float val = acc[e] * inv * gt[e];
-        out[e * (Q / 8)] = val;
-        ss += val * val;
+        for (int e = 0; e < 8; ++e) {
+          const float val = acc[e] * inv * gt[e];
+          out[e * (Q / 8)] = val;
+          ss += val * val;
+        }
+      } else {
+        const float* gt = p.gate + int64_t(t) * Q + e0;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          const float val = acc[e] * inv * gt[e];
+          out[e * (Q / 8)] = val;
+          ss += val * val;
+        }
       }
       if (SS) sv[it] = ss;  // item it = r * IPR + k8
     } else {
@@ -1463,14 +1613,14 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   constexpr int NTHR = kConsumerWarps * 32;
   constexpr int kMaxUnits = ROWS * (HD / 4);
   if (nrows * (HD / 4) <= NTHR) {
-    merge_splits<HD, 1, 16, SS>(p, tid, nrows, gstart, kvh, G, sp.active, sv);
+    merge_splits<HD, 1, 16, SS, QK>(p, tid, nrows, gstart, kvh, G, sp.active, sv);
   } else if constexpr (kMaxUnits <= 2 * NTHR) {
-    merge_splits_rows<HD, 2, 8, SS>(p, tid, nrows, gstart, kvh, G, sp.active, sv);
+    merge_splits_rows<HD, 2, 8, SS, QK>(p, tid, nrows, gstart, kvh, G, sp.active, sv);
   } else {
     if (nrows * (HD / 4) <= 2 * NTHR)
-      merge_splits_rows<HD, 2, 8, SS>(p, tid, nrows, gstart, kvh, G, sp.active, sv);
+      merge_splits_rows<HD, 2, 8, SS, QK>(p, tid, nrows, gstart, kvh, G, sp.active, sv);
     else
-      merge_splits_rows<HD, 4, 8, SS>(p, tid, nrows, gstart, kvh, G, sp.active, sv);
+      merge_splits_rows<HD, 4, 8, SS, QK>(p, tid, nrows, gstart, kvh, G, sp.active, sv);
   }
   if (SS) sumsq_tail<false>(p, sv, HD / 4, nrows, gstart, gcount, G, kvh, tid, s_rowss);
 }
@@ -1552,6 +1702,72 @@ __global__ void __launch_bounds__(128) qk_norm_kernel(const __grid_constant__ Qk
 }
 
 // ------------------------------------------------------------------------------------
+// The multi-token path's q/k/v/gate epilogue as its own launch (reference
+// _qkvg_epilogue_kernel, kernels/dory_multi_token.py:53-80): grid (rows / HD, T), one thread
+// per pair of rows.  Same arithmetic as the attention kernel's QK mode (split-K sum in
+// order, unfused rotary products, the same gate expression), so both give the same bits.
+// ------------------------------------------------------------------------------------
+struct QkvgArgs {
+  const float* partials;
+  const void* positions;
+  const void* cos_sin;
+  const void* s_gate;
+  float* qk;
+  float* v;
+  float* gate;
+  uint32_t* err;
+  float s_gate_factor;
+  int T, NH, NKV, split_k, max_position, pos_dtype, cos_dtype, sgate_dtype;
+};
+
+template <int HD>
+__global__ void __launch_bounds__(HD / 2) qkvg_epilogue_kernel(const __grid_constant__ QkvgArgs a) {
+  constexpr int HALF = HD / 2;
+  const int b = blockIdx.x, t = blockIdx.y, i = threadIdx.x;
+  const int64_t prow = 2 * int64_t(a.NH + a.NKV) * HD;
+  const int64_t row = int64_t(b) * HD + 2 * i;
+  float y0 = 0.0f, y1 = 0.0f;
+  for (int k = 0; k < a.split_k; ++k) {
+    const float2 v = __ldg(reinterpret_cast<const float2*>(a.partials + (int64_t(k) * a.T + t) * prow + row));
+    y0 = __fadd_rn(y0, v.x);
+    y1 = __fadd_rn(y1, v.y);
+  }
+  if (b < a.NH + a.NKV) {  // q or k head b: rows 2i, 2i + 1 are rotary dims i, i + HALF
+    const int64_t pos = a.pos_dtype == 0 ? static_cast<const int64_t*>(a.positions)[t]
+                                         : int64_t(static_cast<const int32_t*>(a.positions)[t]);
+    float lo = 0.0f, hi = 0.0f;
+    if (pos >= 0 && pos < a.max_position) {
+      const float c = load_sqk(a.cos_sin, a.cos_dtype, pos * HD + i);
+      const float sn = load_sqk(a.cos_sin, a.cos_dtype, pos * HD + HALF + i);
+      lo = __fsub_rn(__fmul_rn(y0, c), __fmul_rn(y1, sn));
+      hi = __fadd_rn(__fmul_rn(y1, c), __fmul_rn(y0, sn));
+    } else if (a.err && i == 0) {
+      atomicOr(a.err, DORY_DEVERR_POSITION_OOB);
+    }
+    float* q = a.qk + int64_t(t) * (a.NH + a.NKV) * HD + int64_t(b) * HD;
+    q[i] = lo;
+    q[i + HALF] = hi;
+  } else if (b < a.NH + 2 * a.NKV) {
+    float* v = a.v + int64_t(t) * a.NKV * HD + int64_t(b - a.NH - a.NKV) * HD + 2 * i;
+    v[0] = y0;
+    v[1] = y1;
+  } else {
+    const int e = (b - a.NH - 2 * a.NKV) * HD + 2 * i;
+    float g[2];
+    const float y[2] = {y0, y1};
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const float s = __fmul_rn(load_sqk(a.s_gate, a.sgate_dtype, e + j), a.s_gate_factor);
+      const float z = __fmul_rn(__fmul_rn(y[j], s), s);
+      g[j] = 1.0f / (1.0f + expf(-z));
+    }
+    float* gp = a.gate + int64_t(t) * a.NH * HD + e;
+    gp[0] = g[0];
+    gp[1] = g[1];
+  }
+}
+
+// ------------------------------------------------------------------------------------
 // Host side
 // ------------------------------------------------------------------------------------
 thread_local char g_last_error[512] = "";
@@ -1564,9 +1780,9 @@ int32_t fail(int32_t status, const char* fmt, ...) {
   return status;
 }
 
-template <int HD, int NT, int NS, bool SS>
+template <int HD, int NT, int NS, bool SS, bool QK>
 int32_t launch(const KParams& kp, dim3 grid, int smem_bytes, cudaStream_t stream) {
-  auto fn = decode_kernel<HD, NT, NS, SS>;
+  auto fn = decode_kernel<HD, NT, NS, SS, QK>;
   static int configured[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return fail(DORY_ERR_CUDA, "cudaGetDevice failed");
@@ -1615,8 +1831,15 @@ int32_t dispatch(const KParams& kp, dim3 grid, cudaStream_t stream) {
                 "the warps' merge buffer must fit in the ring");
   // The sum-of-squares epilogue is a separate instantiation: compiled in, even unused, it
   // measured ~0.5 us slower on single-sequence calls.
-  if (kp.sumsq) return launch<HD, NT, NS, true>(kp, grid, Smem<HD, NS>::bytes(kp.nsub), stream);
-  return launch<HD, NT, NS, false>(kp, grid, Smem<HD, NS>::bytes(kp.nsub), stream);
+  // Reading q/k/v/gate from the GEMV partials (QK) is one more: the other instantiations
+  // keep their code.
+  const int bytes = Smem<HD, NS>::bytes(kp.nsub);
+  if (kp.qk) {
+    if (kp.sumsq) return launch<HD, NT, NS, true, true>(kp, grid, bytes, stream);
+    return launch<HD, NT, NS, false, true>(kp, grid, bytes, stream);
+  }
+  if (kp.sumsq) return launch<HD, NT, NS, true, false>(kp, grid, bytes, stream);
+  return launch<HD, NT, NS, false, false>(kp, grid, bytes, stream);
 }
 
 template <int HD>
@@ -1733,6 +1956,54 @@ const char* dory_decode_last_error(void) { return g_last_error; }
 
 int64_t dory_qk_norm_params_bytes(void) { return int64_t(sizeof(DoryQkNormParams)); }
 
+int64_t dory_qkvg_params_bytes(void) { return int64_t(sizeof(DoryQkvgParams)); }
+
+int32_t dory_qkvg_epilogue(const DoryQkvgParams* P, void* stream) {
+  if (!P) return fail(DORY_ERR_INVALID_ARGUMENT, "null params");
+  const DoryQkvgParams& a = *P;
+  if (a.num_tokens < 0 || a.num_heads < 1 || a.num_kv_heads < 1 || a.split_k < 1 ||
+      a.max_position < 1)
+    return fail(DORY_ERR_INVALID_ARGUMENT, "counts must be positive");
+  if (a.head_dim != 64 && a.head_dim != 128 && a.head_dim != 256)
+    return fail(DORY_ERR_UNSUPPORTED, "head_dim %d (supported: 64, 128, 256)", a.head_dim);
+  if (a.positions_dtype < 0 || a.positions_dtype > 1 || a.cos_sin_dtype < 0 ||
+      a.cos_sin_dtype > 2 || a.s_gate_dtype < 0 || a.s_gate_dtype > 2)
+    return fail(DORY_ERR_INVALID_ARGUMENT, "positions / cos_sin / s_gate dtype");
+  if (!a.partials || !a.positions || !a.cos_sin || !a.s_gate || !a.qk_out || !a.v_out ||
+      !a.gate_out)
+    return fail(DORY_ERR_INVALID_ARGUMENT, "null tensor argument");
+  if (reinterpret_cast<uintptr_t>(a.partials) & 15)
+    return fail(DORY_ERR_ALIGNMENT, "partials need a 16-byte aligned base");
+  if (a.num_tokens == 0) return DORY_OK;
+  QkvgArgs k;
+  memset(&k, 0, sizeof(k));
+  k.partials = a.partials;
+  k.positions = a.positions;
+  k.cos_sin = a.cos_sin;
+  k.s_gate = a.s_gate;
+  k.qk = a.qk_out;
+  k.v = a.v_out;
+  k.gate = a.gate_out;
+  k.err = a.error_word;
+  k.s_gate_factor = a.s_gate_factor;
+  k.T = a.num_tokens;
+  k.NH = a.num_heads;
+  k.NKV = a.num_kv_heads;
+  k.split_k = a.split_k;
+  k.max_position = a.max_position;
+  k.pos_dtype = a.positions_dtype;
+  k.cos_dtype = a.cos_sin_dtype;
+  k.sgate_dtype = a.s_gate_dtype;
+  const dim3 grid(2 * (a.num_heads + a.num_kv_heads), a.num_tokens);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (a.head_dim == 64) qkvg_epilogue_kernel<64><<<grid, 32, 0, s>>>(k);
+  else if (a.head_dim == 128) qkvg_epilogue_kernel<128><<<grid, 64, 0, s>>>(k);
+  else qkvg_epilogue_kernel<256><<<grid, 128, 0, s>>>(k);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(DORY_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+  return DORY_OK;
+}
+
 int32_t dory_qk_norm_cache(const DoryQkNormParams* P, void* stream) {
   if (!P) return fail(DORY_ERR_INVALID_ARGUMENT, "null params");
   const DoryQkNormParams& a = *P;
@@ -1791,7 +2062,21 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
   const bool multi = a.flags & DORY_FLAG_MULTI_TOKEN;
   const bool shared = a.flags & DORY_FLAG_SHARED_CACHE;
   const bool overlap = a.flags & DORY_FLAG_OVERLAP_LAUNCH;
+  const bool qkp = a.flags & DORY_FLAG_QKVG_PARTIALS;
   if (a.num_tokens < 0) return fail(DORY_ERR_INVALID_ARGUMENT, "negative token count");
+  if (qkp) {
+    if (!raw || !multi)
+      return fail(DORY_ERR_INVALID_ARGUMENT, "q/k/v/gate partials need a raw multi-token call");
+    if (!a.qkvg_partials || !a.positions || !a.cos_sin || !a.s_gate)
+      return fail(DORY_ERR_INVALID_ARGUMENT, "partials, positions, cos_sin and s_gate are required");
+    if (a.split_k < 1 || a.max_position < 1)
+      return fail(DORY_ERR_INVALID_ARGUMENT, "split_k and max_position must be positive");
+    if (a.positions_dtype < 0 || a.positions_dtype > 1 || a.cos_sin_dtype < 0 ||
+        a.cos_sin_dtype > 2 || a.s_gate_dtype < 0 || a.s_gate_dtype > 2)
+      return fail(DORY_ERR_INVALID_ARGUMENT, "positions / cos_sin / s_gate dtype");
+    if (reinterpret_cast<uintptr_t>(a.qkvg_partials) & 15)
+      return fail(DORY_ERR_ALIGNMENT, "q/k/v/gate partials need a 16-byte aligned base");
+  }
   if (a.num_tokens > a.max_tokens)
     return fail(DORY_ERR_INVALID_ARGUMENT, "too many tokens for the scratch buffers");
   if (!multi && a.num_tokens != 1)
@@ -1800,10 +2085,10 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
     return fail(DORY_ERR_INVALID_ARGUMENT, "shared_cache needs a raw multi-token call");
   if (multi && (!a.cache_offsets || !a.block_table_offsets))
     return fail(DORY_ERR_INVALID_ARGUMENT, "multi-token calls need int64 cache/table offsets");
-  if (raw && (!a.v || !a.sqk || (!multi && !a.slot_mapping)))
+  if (raw && ((!qkp && !a.v) || !a.sqk || (!multi && !a.slot_mapping)))
     return fail(DORY_ERR_INVALID_ARGUMENT, "raw calls need v, sqk and a slot mapping");
-  if (!a.q || !a.key_cache || !a.value_cache || !a.block_table || !a.seq_lens || !a.gate ||
-      !a.out_nibble_major || !a.scratch)
+  if ((!qkp && (!a.q || !a.gate)) || !a.key_cache || !a.value_cache || !a.block_table ||
+      !a.seq_lens || !a.out_nibble_major || !a.scratch)
     return fail(DORY_ERR_INVALID_ARGUMENT, "null tensor argument");
   if (a.splits < 1 || a.blocks_per_tile < 1)
     return fail(DORY_ERR_INVALID_ARGUMENT, "splits and blocks_per_tile must be positive");
@@ -1818,7 +2103,7 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
   if (shared && a.num_tokens > kMaxSub)
     return fail(DORY_ERR_UNSUPPORTED, "shared-cache calls take at most %d tokens", kMaxSub);
   if (a.sqk_dtype < 0 || a.sqk_dtype > 2) return fail(DORY_ERR_INVALID_ARGUMENT, "sqk dtype");
-  if (reinterpret_cast<uintptr_t>(a.gate) & 15)
+  if (!qkp && (reinterpret_cast<uintptr_t>(a.gate) & 15))
     return fail(DORY_ERR_ALIGNMENT, "gate needs a 16-byte aligned base");
   if ((reinterpret_cast<uintptr_t>(a.key_cache) & 15) ||
       (reinterpret_cast<uintptr_t>(a.value_cache) & 15) || (a.stride_block & 7) ||
@@ -1894,6 +2179,20 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
   kp.overlap = overlap;
   kp.q_stride = (raw ? a.num_heads + a.num_kv_heads : a.num_heads) * HD;
   kp.nsub = raw ? (shared ? a.num_tokens : 1) : 0;
+  if (qkp) {
+    kp.qk = 1;
+    kp.pq = a.qkvg_partials;
+    kp.positions = a.positions;
+    kp.cos_sin = a.cos_sin;
+    kp.s_gate = a.s_gate;
+    kp.s_gate_factor = a.s_gate_factor;
+    kp.split_k = a.split_k;
+    kp.prow = 2 * (a.num_heads + a.num_kv_heads) * HD;
+    kp.max_position = a.max_position;
+    kp.pos_dtype = a.positions_dtype;
+    kp.cos_dtype = a.cos_sin_dtype;
+    kp.sgate_dtype = a.s_gate_dtype;
+  }
   // Tensor maps of the K and V views.  Multi-token calls may shift the cache by whole
   // blocks (per-loop caches at cache_offsets[t]); the block extent then allows up to 64
   // caches' worth of blocks past the view.  Other offsets take the copy path.

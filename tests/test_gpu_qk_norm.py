@@ -17,7 +17,7 @@ import torch
 
 import dory_oracle as O
 import workloads as W
-from dory_attention import _qk_norm_cache_kernel, qk_norm_cache
+from dory_sublayer_steps import _qk_norm_cache_kernel, qk_norm_cache
 from dory_decode_attention import EPS, DecodeAttention
 
 pytestmark = pytest.mark.gpu
