@@ -236,7 +236,8 @@ def workload_spec(name: str) -> Spec:
     raise SystemExit(f"unknown workload {name} (one of {', '.join(WORKLOADS)})")
 
 
-def algorithmic_bytes(seq_lens, shared: bool, window: int, nh: int, nkv: int, hd: int) -> int:
+def algorithmic_bytes(seq_lens, shared: bool, window: int, nh: int, nkv: int, hd: int,
+                      split_k: int = 0) -> int:
     """Bytes one launch must move: unique attended positions x the K/V row bytes (the new
     rows written, the rest read) + per-token q/k/v/gate reads and out writes (FP32) + sqk
     + the block-table entries of the attended range + seq_lens.  With a sliding window w a
@@ -244,6 +245,12 @@ def algorithmic_bytes(seq_lens, shared: bool, window: int, nh: int, nkv: int, hd
     its tokens' ranges once."""
     kv_row = nkv * hd * 2 * 2
     token_io = ((nh + nkv) * hd + nkv * hd + 2 * nh * hd) * 4
+    extra = 0
+    if split_k:
+        # q/k/v/gate GEMV partials in (2 * (Q + KV) rows per split), output out, the token's
+        # position and bf16 cos/sin row; the bf16 gate scales once per launch
+        token_io = (split_k * 2 * (nh + nkv) * hd + nh * hd) * 4 + 8 + hd * 2
+        extra = nh * hd * 2
 
     def span(n):
         return (max(n - window, 0) if window > 0 else 0), n
@@ -258,7 +265,8 @@ def algorithmic_bytes(seq_lens, shared: bool, window: int, nh: int, nkv: int, hd
         spans = [span(n) for n in seq_lens]
     unique = sum(b - a for a, b in spans)
     table = sum(table_entries(a, b) for a, b in spans) * 4
-    return unique * kv_row + len(seq_lens) * token_io + nh * hd * 2 + table + 4 * len(seq_lens)
+    return (unique * kv_row + len(seq_lens) * token_io + nh * hd * 2 + table + 4 * len(seq_lens)
+            + extra)
 
 
 class DeviceWorkload:
@@ -338,7 +346,8 @@ class DeviceWorkload:
 
     def algorithmic_bytes_per_application(self, layer: int = 0) -> int:
         return algorithmic_bytes(self.seq_lens_list, self.shared, self.window(layer),
-                                 self.nh, self.nkv, self.hd)
+                                 self.nh, self.nkv, self.hd,
+                                 QKVG_SPLIT_K if self.path == "qkvg" else 0)
 
     def algorithmic_bytes_per_step(self) -> int:
         return sum(self.algorithmic_bytes_per_application(layer) for layer in self.layers)
@@ -367,10 +376,34 @@ def prepare_call_path(wl: DeviceWorkload):
     wl.path = "call"
 
 
+QKVG_SPLIT_K = 2  # the reference's q/k/v/gate GEMV configuration (dory_multi_token.py:44)
+
+
+def prepare_qkvg_path(wl: DeviceWorkload):
+    """`--path qkvg`: each layer's input is the multi-token path's q/k/v/gate GEMV output,
+    split-K partial sums FP32 [split_k, T, 2 * (Q + KV)], with the tokens' rotary positions
+    (seq_len - 1), a cos/sin table and the gate scales; a layer is the epilogue kernel, then
+    multi_from_raw (the reference's two launches, dory_multi_token.py:196-205)."""
+    T, L = wl.tokens, wl.num_layers
+    rows = 2 * (wl.nh + wl.nkv) * wl.hd
+    gd = torch.Generator(device=wl.dev).manual_seed(77)
+    wl.partials = torch.randn(L, QKVG_SPLIT_K, T, rows, device=wl.dev, generator=gd) * 0.5
+    wl.positions = (wl.seq_lens.to(torch.int64) - 1).clamp(min=0)
+    wl.cos_sin = torch.randn(int(wl.seq_lens.max()) + 1, wl.hd, device=wl.dev,
+                             generator=gd).to(torch.bfloat16)
+    wl.s_gate = (torch.rand(wl.nh * wl.hd, device=wl.dev, generator=gd) + 0.5).to(torch.bfloat16)
+    wl.qkvg_bufs = (torch.empty(T, (wl.nh + wl.nkv) * wl.hd, device=wl.dev),
+                    torch.empty(T, wl.nkv * wl.hd, device=wl.dev),
+                    torch.empty(T, wl.nh * wl.hd, device=wl.dev))
+    wl.path = "qkvg"
+
+
 def step_inputs(wl: DeviceWorkload):
     """The per-layer input tensors ([layers, T, ...]) the workload's path reads."""
     if wl.path == "call":
         return (wl.q_call, wl.gate)
+    if wl.path.startswith("qkvg"):
+        return (wl.partials,)
     return (wl.qk, wl.v, wl.gate)
 
 
@@ -384,6 +417,15 @@ def layer_call(attn, wl: DeviceWorkload, app: int, layer: int, ins, out):
         q, gate = ins
         attn(q[0], key, value, wl.tables[0], wl.seq_lens[0:1], window, scale, gate[0], out[0],
              out_sumsq=sumsq)
+        return
+    if wl.path == "qkvg":
+        from dory_sublayer_steps import qkvg_epilogue
+        qk_b, v_b, gate_b = wl.qkvg_bufs
+        qkvg_epilogue(ins[0], wl.positions, wl.cos_sin, wl.s_gate, 0.9, qk_b, v_b, gate_b,
+                      wl.nh, wl.nkv, wl.hd)
+        attn.multi_from_raw(qk_b, v_b, wl.sqk, W.SQK_FACTOR, EPS, wl.cache_offsets, key, value,
+                            wl.tables, wl.table_offsets, wl.seq_lens, window, scale, gate_b, out,
+                            shared_cache=wl.shared, out_sumsq=sumsq)
         return
     qk, v, gate = ins
     if wl.path == "separate":
@@ -453,13 +495,15 @@ def bench_ours(args, world, rank, local):
     wl = DeviceWorkload(spec, lens, dev, spec.seed + 1000 * rank)
     if args.sumsq:
         wl.sumsq = torch.zeros(wl.num_layers, wl.tokens, device=dev)
-    if args.path != "fused" and wl.tokens != 1:
+    if args.path in ("separate", "call") and wl.tokens != 1:
         raise SystemExit(f"--path {args.path} takes single-sequence workloads "
                          "(config1, config4, dory*)")
     if args.path == "separate":
         wl.path = "separate"
     elif args.path == "call":
         prepare_call_path(wl)
+    elif args.path == "qkvg":
+        prepare_qkvg_path(wl)
     attn = make_attention(wl, args)
     apps = len(layers)
 
@@ -540,7 +584,7 @@ def bench_ours(args, world, rank, local):
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": args.steps * apps * (2 if wl.path == "separate" else 1),
+        "gpu_launches": args.steps * apps * (2 if wl.path in ("separate", "qkvg") else 1),
         "clocks": clocks.summary(),
     }
     if rank == 0:
@@ -802,8 +846,11 @@ def main() -> int:
     ap.add_argument("--min-blocks-per-split", type=int, default=None)
     ap.add_argument("--overlap-launch", action="store_true",
                     help="launch each layer call as a programmatic dependent of the previous one")
-    ap.add_argument("--path", choices=("fused", "separate", "call"), default="fused",
-                    help="call: the non-raw __call__ alone (q normalised and its k/v cached "
+    ap.add_argument("--path", choices=("fused", "separate", "call", "qkvg"),
+                    default="fused",
+                    help="qkvg: the multi-token q/k/v/gate epilogue kernel on the GEMV's "
+                         "split-K partials, then multi_from_raw; "
+                         "call: the non-raw __call__ alone (q normalised and its k/v cached "
                          "beforehand); separate: the q/k normalisation kernel then the "
                          "non-raw call "
                          "(single-sequence workloads; the reference's two-kernel path)")

@@ -21,7 +21,6 @@ OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_ALIGNMENT, ERR_CUDA = range(5)
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = range(3)
 # DORY_FLAG_*
 FLAG_RAW_QKV, FLAG_MULTI_TOKEN, FLAG_SHARED_CACHE, FLAG_OVERLAP_LAUNCH = 1, 2, 4, 8
-FLAG_QKVG_PARTIALS = 16
 # DORY_QKNORM_*
 QKNORM_WRITE_CACHE = 1
 # DORY_DEVERR_*
@@ -59,9 +58,6 @@ class DoryDecodeParams(ctypes.Structure):
         ("block_size", _i32), ("window", _i32), ("splits", _i32), ("blocks_per_tile", _i32),
         ("min_blocks_per_split", _i32), ("max_tokens", _i32), ("sqk_dtype", _i32),
         ("flags", _u32),
-        ("qkvg_partials", _vp), ("positions", _vp), ("cos_sin", _vp), ("s_gate", _vp),
-        ("s_gate_factor", _f32), ("split_k", _i32), ("max_position", _i32),
-        ("positions_dtype", _i32), ("cos_sin_dtype", _i32), ("s_gate_dtype", _i32),
     ]
 
 

@@ -39,7 +39,9 @@
 //     drains its own copies before returning.  Out-of-range block ids / slots are recorded
 //     and skipped, never dereferenced.
 //   * A second small kernel is the reference's separate q/k normalisation + cache write
-//     (_qk_norm_cache_kernel), the input side of the non-raw call.
+//     (_qk_norm_cache_kernel), the input side of the non-raw call; a third is the
+//     multi-token path's q/k/v/gate epilogue (_qkvg_epilogue_kernel), the input side of the
+//     raw multi-token call.
 
 #include <cuda.h>
 #include <cudaTypedefs.h>
@@ -102,13 +104,6 @@ struct alignas(64) KParams {
   float scale, sqk_factor, eps;
   int min_bps, sqk_dtype, overlap;
   int tm_mode;   // 0: no tensor maps; 1: tmk covers K and V (V right after K); 2: tmk, tmv
-  // QK mode (DORY_FLAG_QKVG_PARTIALS): q, k, v and the gate from the split-K GEMV partials
-  const float* pq;        // [split_k][T][prow]
-  const void* positions;  // [T] int64 (pos_dtype 0) or int32
-  const void* cos_sin;    // [max_position][HD]: cos, then sin
-  const void* s_gate;     // [Q]
-  float s_gate_factor;
-  int split_k, prow, max_position, pos_dtype, cos_dtype, sgate_dtype, qk;
   CUtensorMap tmk;  // cache views as 5-D tensors (64 dims, rows, 64-dim quarters of a row,
   CUtensorMap tmv;  // KV head, block), one box = a chunk's K (and V) tile, 128-byte swizzle
 };
@@ -305,88 +300,6 @@ __device__ __forceinline__ float load_sqk(const void* sqk, int dtype, int64_t i)
   return static_cast<const float*>(sqk)[i];
 }
 
-// ---- QK mode: the multi-token path's q/k/v/gate epilogue (reference _qkvg_epilogue_kernel,
-//      kernels/dory_multi_token.py:53-80), computed where each value is used ----
-// Rotary position of token t, or -1 (recorded) outside the cos/sin table.
-__device__ __forceinline__ int64_t token_position(const KParams& p, int t) {
-  const int64_t pos = p.pos_dtype == 0 ? static_cast<const int64_t*>(p.positions)[t]
-                                       : int64_t(static_cast<const int32_t*>(p.positions)[t]);
-  if (pos < 0 || pos >= p.max_position) {
-    record_error(p.err, DORY_DEVERR_POSITION_OOB);
-    return -1;
-  }
-  return pos;
-}
-// y[i] = 0 + p_0[row + i] + p_1[row + i] + ... over the split-K partials in order (the
-// reference's `y += tl.load(...)` from zeros).  row is a multiple of N (N = 2, 4, 8, 16), the
-// partials 16-byte aligned, so the loads are vectors.
-template <int N>
-__device__ __forceinline__ void partial_rows(const KParams& p, int t, int64_t row,
-                                             float (&y)[N]) {
-#pragma unroll
-  for (int i = 0; i < N; ++i) y[i] = 0.0f;
-  for (int k = 0; k < p.split_k; ++k) {
-    const float* src = p.pq + (int64_t(k) * p.T + t) * p.prow + row;
-    if constexpr (N % 4 == 0) {
-#pragma unroll
-      for (int i = 0; i < N; i += 4) {
-        const float4 a = __ldg(reinterpret_cast<const float4*>(src + i));
-        y[i] = __fadd_rn(y[i], a.x);
-        y[i + 1] = __fadd_rn(y[i + 1], a.y);
-        y[i + 2] = __fadd_rn(y[i + 2], a.z);
-        y[i + 3] = __fadd_rn(y[i + 3], a.w);
-      }
-    } else {
-      static_assert(N == 2, "row runs of 2 or a multiple of 4");
-      const float2 a = __ldg(reinterpret_cast<const float2*>(src));
-      y[0] = __fadd_rn(y[0], a.x);
-      y[1] = __fadd_rn(y[1], a.y);
-    }
-  }
-}
-// This lane's PER_LANE natural dims [lane * PER_LANE, +PER_LANE) of q or k head `head` of
-// token t with the rotary embedding applied: rows 2i, 2i + 1 of the head are dims i and
-// i + HD / 2, out[i] = first * cos - second * sin and out[i + HD / 2] = second * cos +
-// first * sin, each product and sum rounded on its own.
-template <int PER_LANE, int HD>
-__device__ __forceinline__ void rope_row(const KParams& p, int t, int64_t pos, int head,
-                                         int lane, float (&out)[PER_LANE]) {
-  constexpr int HALF = HD / 2;
-  static_assert(HALF % PER_LANE == 0, "a lane's dims lie in one half of the head");
-  const int d0 = lane * PER_LANE;
-  const bool hi = d0 >= HALF;
-  const int j0 = hi ? d0 - HALF : d0;
-  float y[2 * PER_LANE];
-  partial_rows<2 * PER_LANE>(p, t, int64_t(head) * HD + 2 * j0, y);
-#pragma unroll
-  for (int i = 0; i < PER_LANE; ++i) {
-    if (pos < 0) {
-      out[i] = 0.0f;
-      continue;
-    }
-    const float c = load_sqk(p.cos_sin, p.cos_dtype, pos * HD + j0 + i);
-    const float sn = load_sqk(p.cos_sin, p.cos_dtype, pos * HD + HALF + j0 + i);
-    const float first = y[2 * i], second = y[2 * i + 1];
-    out[i] = hi ? __fadd_rn(__fmul_rn(second, c), __fmul_rn(first, sn))
-                : __fsub_rn(__fmul_rn(first, c), __fmul_rn(second, sn));
-  }
-}
-// The output gate of elements e0 .. e0 + 3 (e0 a multiple of 4) of token t: sigmoid((y * s)
-// * s), s = s_gate[e] * s_gate_factor; the gate rows are the last Q rows of the partials.
-template <int HD>
-__device__ __forceinline__ float4 gate4_partials(const KParams& p, int t, int e0) {
-  float y[4];
-  partial_rows<4>(p, t, int64_t(p.prow) - int64_t(p.NH) * HD + e0, y);
-  float g[4];
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const float s = __fmul_rn(load_sqk(p.s_gate, p.sgate_dtype, e0 + i), p.s_gate_factor);
-    const float z = __fmul_rn(__fmul_rn(y[i], s), s);
-    g[i] = 1.0f / (1.0f + expf(-z));
-  }
-  return make_float4(g[0], g[1], g[2], g[3]);
-}
-
 // Canonical normalisation factor of one row: Sum x^2 is accumulated in FP64 (every square
 // is exact there and the sum carries 29 more bits than FP32, so its FP32 rounding depends on
 // the summation order only when the sum lies within ~2^-53 of an FP32 rounding boundary),
@@ -544,7 +457,7 @@ __device__ __forceinline__ bool fixup_stage(const KParams& p, uint8_t* kst, uint
 // Cross-split merge of one (token group, KV head) by its last CTA: thread tid owns output
 // units tid + k * 128 (k < UPT), a unit being 4 consecutive dims of one query row.
 // ------------------------------------------------------------------------------------
-template <int HD, int UPT, int SB, bool SS, bool QK>
+template <int HD, int UPT, int SB, bool SS>
 __device__ __forceinline__ void merge_splits(const KParams& p, int tid, int nrows, int gstart,
                                              int kvh, int G, int active, float* sv) {
   constexpr int UPR = HD / 4;  // float4 units per row
@@ -567,11 +480,8 @@ __device__ __forceinline__ void merge_splits(const KParams& p, int tid, int nrow
     acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
     Mx[k] = -INFINITY;
     Ls[k] = 0.0f;
-    if constexpr (QK)
-      gt[k] = u < units ? gate4_partials<HD>(p, t, head * HD + d4 * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
-    else
-      gt[k] = u < units ? *reinterpret_cast<const float4*>(p.gate + int64_t(t) * Q + head * HD + d4 * 4)
-                        : make_float4(0.f, 0.f, 0.f, 0.f);
+    gt[k] = u < units ? *reinterpret_cast<const float4*>(p.gate + int64_t(t) * Q + head * HD + d4 * 4)
+                      : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   for (int s0 = 0; s0 < active; s0 += SB) {
     float4 v[UPT][SB];
@@ -632,7 +542,7 @@ __device__ __forceinline__ void merge_splits(const KParams& p, int tid, int nrow
 // flight together (one L2 round trip per batch; the gate rides along the first), each
 // folded in with one max, independent weights and one rescale.
 // ------------------------------------------------------------------------------------
-template <int HD, int UPT, int SB, bool SS, bool QK>
+template <int HD, int UPT, int SB, bool SS>
 __device__ __forceinline__ void merge_splits_rows(const KParams& p, int tid, int nrows, int gstart,
                                              int kvh, int G, int active, float* sv) {
   constexpr int UPR = HD / 4;  // float4 units per row
@@ -652,11 +562,8 @@ __device__ __forceinline__ void merge_splits_rows(const KParams& p, int tid, int
 #pragma unroll
   for (int k = 0; k < UPT; ++k) {
     acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    if constexpr (QK)
-      gt[k] = mine ? gate4_partials<HD>(p, t, head * HD + (d40 + k) * 4) : make_float4(0.f, 0.f, 0.f, 0.f);
-    else
-      gt[k] = mine ? *reinterpret_cast<const float4*>(p.gate + int64_t(t) * Q + head * HD + (d40 + k) * 4)
-                   : make_float4(0.f, 0.f, 0.f, 0.f);
+    gt[k] = mine ? *reinterpret_cast<const float4*>(p.gate + int64_t(t) * Q + head * HD + (d40 + k) * 4)
+                 : make_float4(0.f, 0.f, 0.f, 0.f);
   }
   for (int s0 = 0; s0 < active; s0 += SB) {
     float4 v[SB][UPT];
@@ -751,7 +658,7 @@ __device__ __forceinline__ void sumsq_tail(const KParams& p, const float* sv, in
 // ------------------------------------------------------------------------------------
 // The kernel.  grid = (splits, NKV, T); block = 160 threads (4 consumer warps + producer).
 // ------------------------------------------------------------------------------------
-template <int HD, int NT, int NS, bool SS, bool QK>
+template <int HD, int NT, int NS, bool SS>
 __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     decode_kernel(const __grid_constant__ KParams p) {
   using L = Smem<HD, NS>;
@@ -801,17 +708,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     // pulling them into L2 now, while that first load is in flight.
     const int hq = kvh * G;
     const int64_t qrow = int64_t(tok) * p.q_stride;
-    if constexpr (QK) {
-      // This token's q rows, k and v rows and gate rows in every split-K slice.
-      const int KV = p.NKV * HD;
-      for (int k = 0; k < p.split_k; ++k) {
-        const float* sl = p.pq + (int64_t(k) * p.T + tok) * p.prow;
-        prefetch_range(sl + hq * HD, G * HD * 4, lane);
-        prefetch_range(sl + Q + kvh * HD, HD * 4, lane);
-        prefetch_range(sl + Q + KV + kvh * HD, HD * 4, lane);
-        prefetch_range(sl + Q + 2 * KV + hq * HD, G * HD * 4, lane);
-      }
-    } else if (p.raw) {
+    if (p.raw) {
       const float* qf = static_cast<const float*>(p.q) + qrow;
       prefetch_range(qf + hq * HD, G * HD * 4, lane);
       prefetch_range(qf + (p.NH + kvh) * HD, HD * 4, lane);
@@ -822,7 +719,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     } else {
       prefetch_range(static_cast<const __nv_bfloat16*>(p.q) + qrow + hq * HD, G * HD * 2, lane);
     }
-    if constexpr (!QK) prefetch_range(p.gate + int64_t(tok) * Q + hq * HD, G * HD * 4, lane);
+    prefetch_range(p.gate + int64_t(tok) * Q + hq * HD, G * HD * 4, lane);
     if (p.tm_mode && lane == 0) {
       prefetch_tensormap(&p.tmk);
       if (p.tm_mode == 2) prefetch_tensormap(&p.tmv);
@@ -886,14 +783,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
         const int r = i / HD, d = i % HD;
         const int t = gstart + r / G, head = kvh * G + r % G;
         const int e = head * HD + d;
-        float gv;
-        if constexpr (QK) {
-          const float4 g4 = gate4_partials<HD>(p, t, e & ~3);
-          gv = (e & 3) == 0 ? g4.x : (e & 3) == 1 ? g4.y : (e & 3) == 2 ? g4.z : g4.w;
-        } else {
-          gv = p.gate[int64_t(t) * Q + e];
-        }
-        const float val = 0.0f * gv;
+        const float val = 0.0f * p.gate[int64_t(t) * Q + e];
         p.out[int64_t(t) * Q + (e % 8) * (Q / 8) + e / 8] = val;
         if (SS) sv0[i] = val * val;
       }
@@ -1086,7 +976,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   // Every load of this warp's rows (q, sqk) and of its first sub token (k, v) is issued
   // before any of the arithmetic: one L2 round trip, not one per dependent step.
   constexpr int RPW = ROWS / kConsumerWarps;  // query rows per consumer warp
-  if constexpr (HD == 256 || QK) {
+  if constexpr (HD == 256) {
     const bool sub0 = p.raw && warp < nsub;
     // 256-dim heads: 16-byte loads where the bases allow them (every row offset is a
     // multiple of 16 bytes), and in raw mode the FP64 sums of all of this warp's rows (its
@@ -1094,7 +984,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     // (same bits), so that their shuffle chains overlap.
     const bool vec = ((reinterpret_cast<uintptr_t>(p.q) | reinterpret_cast<uintptr_t>(p.v)) &
                       15) == 0;
-    const bool vsqk = PER_LANE % 8 == 0 && p.sqk_dtype == DORY_DTYPE_BF16 &&
+    const bool vsqk = p.sqk_dtype == DORY_DTYPE_BF16 &&
                       (reinterpret_cast<uintptr_t>(p.sqk) & 15) == 0;
     auto load_f32 = [&](const float* src, float (&x)[PER_LANE]) {
       if (vec) {
@@ -1109,22 +999,18 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
       }
     };
     auto load_bf16 = [&](const __nv_bfloat16* src, bool v16, float (&x)[PER_LANE]) {
-      if constexpr (PER_LANE % 8 == 0) {
-        if (v16) {
+      if (v16) {
 #pragma unroll
-          for (int i = 0; i < PER_LANE; i += 8) {
-            const uint4 w = *reinterpret_cast<const uint4*>(src + lane * PER_LANE + i);
-            const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+        for (int i = 0; i < PER_LANE; i += 8) {
+          const uint4 w = *reinterpret_cast<const uint4*>(src + lane * PER_LANE + i);
+          const uint32_t u[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              x[i + 2 * k] = __uint_as_float(u[k] << 16);
-              x[i + 2 * k + 1] = __uint_as_float(u[k] & 0xffff0000u);
-            }
+          for (int k = 0; k < 4; ++k) {
+            x[i + 2 * k] = __uint_as_float(u[k] << 16);
+            x[i + 2 * k + 1] = __uint_as_float(u[k] & 0xffff0000u);
           }
-          return;
         }
-      }
-      {
+      } else {
 #pragma unroll
         for (int i = 0; i < PER_LANE; ++i) x[i] = __bfloat162float(src[lane * PER_LANE + i]);
       }
@@ -1138,12 +1024,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
       if (r >= nrows) continue;
       const int t = gstart + r / G;
       const int head = kvh * G + r % G;
-      if constexpr (QK) {
-        rope_row<PER_LANE, HD>(p, t, token_position(p, t), head, lane, qv[j]);
-#pragma unroll
-        for (int i = 0; i < PER_LANE; ++i)
-          sqv[j][i] = load_sqk(p.sqk, p.sqk_dtype, head * HD + lane * PER_LANE + i);
-      } else if (p.raw) {
+      if (p.raw) {
         load_f32(static_cast<const float*>(p.q) + int64_t(t) * p.q_stride + head * HD, qv[j]);
         if (vsqk) {
           load_bf16(static_cast<const __nv_bfloat16*>(p.sqk) + head * HD, true, sqv[j]);
@@ -1163,13 +1044,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     for (int i = 0; i < PER_LANE; ++i) kv0[i] = vv0[i] = 0.0f;
     if (sub0) {
       const int t = p.shared ? warp : tok;
-      if constexpr (QK) {
-        rope_row<PER_LANE, HD>(p, t, token_position(p, t), p.NH + kvh, lane, kv0);
-        partial_rows<PER_LANE>(p, t, int64_t(p.NH + p.NKV + kvh) * HD + lane * PER_LANE, vv0);
-      } else {
-        load_f32(static_cast<const float*>(p.q) + int64_t(t) * p.q_stride + (p.NH + kvh) * HD, kv0);
-        load_f32(p.v + int64_t(t) * p.NKV * HD + kvh * HD, vv0);
-      }
+      load_f32(static_cast<const float*>(p.q) + int64_t(t) * p.q_stride + (p.NH + kvh) * HD, kv0);
+      load_f32(p.v + int64_t(t) * p.NKV * HD + kvh * HD, vv0);
     }
     if (p.raw) {
       double acc[RPW + 1];
@@ -1293,31 +1169,18 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   if (p.raw) {
     for (int s = warp + kConsumerWarps; s < nsub; s += kConsumerWarps) {
       const int t = p.shared ? s : tok;
-      if constexpr (QK) {
-        float kv[PER_LANE], vv[PER_LANE];
-        rope_row<PER_LANE, HD>(p, t, token_position(p, t), p.NH + kvh, lane, kv);
-        partial_rows<PER_LANE>(p, t, int64_t(p.NH + p.NKV + kvh) * HD + lane * PER_LANE, vv);
-        const float rn = row_inv_norm<PER_LANE>(kv, p.eps);
+      const float* ksrc =
+          static_cast<const float*>(p.q) + int64_t(t) * p.q_stride + (p.NH + kvh) * HD;
+      const float* vsrc = p.v + int64_t(t) * p.NKV * HD + kvh * HD;
+      float kv[PER_LANE];
 #pragma unroll
-        for (int i = 0; i < PER_LANE; ++i) {
-          const int d = lane * PER_LANE + i;
-          subkv[(s * 2 + 0) * HD + d] = __float2bfloat16_rn(__fmul_rn(kv[i], rn));
-          subkv[(s * 2 + 1) * HD + d] = __float2bfloat16_rn(vv[i]);
-        }
-      } else {
-        const float* ksrc =
-            static_cast<const float*>(p.q) + int64_t(t) * p.q_stride + (p.NH + kvh) * HD;
-        const float* vsrc = p.v + int64_t(t) * p.NKV * HD + kvh * HD;
-        float kv[PER_LANE];
+      for (int i = 0; i < PER_LANE; ++i) kv[i] = ksrc[lane * PER_LANE + i];
+      const float rn = row_inv_norm<PER_LANE>(kv, p.eps);
 #pragma unroll
-        for (int i = 0; i < PER_LANE; ++i) kv[i] = ksrc[lane * PER_LANE + i];
-        const float rn = row_inv_norm<PER_LANE>(kv, p.eps);
-#pragma unroll
-        for (int i = 0; i < PER_LANE; ++i) {
-          const int d = lane * PER_LANE + i;
-          subkv[(s * 2 + 0) * HD + d] = __float2bfloat16_rn(__fmul_rn(kv[i], rn));
-          subkv[(s * 2 + 1) * HD + d] = __float2bfloat16_rn(vsrc[d]);
-        }
+      for (int i = 0; i < PER_LANE; ++i) {
+        const int d = lane * PER_LANE + i;
+        subkv[(s * 2 + 0) * HD + d] = __float2bfloat16_rn(__fmul_rn(kv[i], rn));
+        subkv[(s * 2 + 1) * HD + d] = __float2bfloat16_rn(vsrc[d]);
       }
     }
   }
@@ -1557,25 +1420,14 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     if (single) {
       const float inv = 1.0f / (Lsum > 0.0f ? Lsum : 1.0f);
       const int e0 = head * HD + k8 * 8;
+      const float* gt = p.gate + int64_t(t) * Q + e0;
       float* out = p.out + int64_t(t) * Q + e0 / 8;
       float ss = 0.0f;
-      if constexpr (QK) {
-        const float4 ga = gate4_partials<HD>(p, t, e0), gb = gate4_partials<HD>(p, t, e0 + 4);
-        const float gt[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float val = acc[e] * inv * gt[e];
-          out[e * (Q / 8)] = val;
-          ss += val * val;
-        }
-      } else {
-        const float* gt = p.gate + int64_t(t) * Q + e0;
-#pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const float val = acc[e] * inv * gt[e];
-          out[e * (Q / 8)] = val;
-          ss += val * val;
-        }
+      for (int e = 0; e < 8; ++e) {
+        const float val = acc[e] * inv * gt[e];
+        out[e * (Q / 8)] = val;
+        ss += val * val;
       }
       if (SS) sv[it] = ss;  // item it = r * IPR + k8
     } else {
@@ -1613,14 +1465,14 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   constexpr int NTHR = kConsumerWarps * 32;
   constexpr int kMaxUnits = ROWS * (HD / 4);
   if (nrows * (HD / 4) <= NTHR) {
-    merge_splits<HD, 1, 16, SS, QK>(p, tid, nrows, gstart, kvh, G, sp.active, sv);
+    merge_splits<HD, 1, 16, SS>(p, tid, nrows, gstart, kvh, G, sp.active, sv);
   } else if constexpr (kMaxUnits <= 2 * NTHR) {
-    merge_splits_rows<HD, 2, 8, SS, QK>(p, tid, nrows, gstart, kvh, G, sp.active, sv);
+    merge_splits_rows<HD, 2, 8, SS>(p, tid, nrows, gstart, kvh, G, sp.active, sv);
   } else {
     if (nrows * (HD / 4) <= 2 * NTHR)
-      merge_splits_rows<HD, 2, 8, SS, QK>(p, tid, nrows, gstart, kvh, G, sp.active, sv);
+      merge_splits_rows<HD, 2, 8, SS>(p, tid, nrows, gstart, kvh, G, sp.active, sv);
     else
-      merge_splits_rows<HD, 4, 8, SS, QK>(p, tid, nrows, gstart, kvh, G, sp.active, sv);
+      merge_splits_rows<HD, 4, 8, SS>(p, tid, nrows, gstart, kvh, G, sp.active, sv);
   }
   if (SS) sumsq_tail<false>(p, sv, HD / 4, nrows, gstart, gcount, G, kvh, tid, s_rowss);
 }
@@ -1704,8 +1556,8 @@ __global__ void __launch_bounds__(128) qk_norm_kernel(const __grid_constant__ Qk
 // ------------------------------------------------------------------------------------
 // The multi-token path's q/k/v/gate epilogue as its own launch (reference
 // _qkvg_epilogue_kernel, kernels/dory_multi_token.py:53-80): grid (rows / HD, T), one thread
-// per pair of rows.  Same arithmetic as the attention kernel's QK mode (split-K sum in
-// order, unfused rotary products, the same gate expression), so both give the same bits.
+// per pair of rows.  The split-K sum in order from zero, the rotary products and sums
+// rounded one by one (no fused multiply-add), the gate as sigmoid((y * s) * s).
 // ------------------------------------------------------------------------------------
 struct QkvgArgs {
   const float* partials;
@@ -1780,9 +1632,9 @@ int32_t fail(int32_t status, const char* fmt, ...) {
   return status;
 }
 
-template <int HD, int NT, int NS, bool SS, bool QK>
+template <int HD, int NT, int NS, bool SS>
 int32_t launch(const KParams& kp, dim3 grid, int smem_bytes, cudaStream_t stream) {
-  auto fn = decode_kernel<HD, NT, NS, SS, QK>;
+  auto fn = decode_kernel<HD, NT, NS, SS>;
   static int configured[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return fail(DORY_ERR_CUDA, "cudaGetDevice failed");
@@ -1831,15 +1683,8 @@ int32_t dispatch(const KParams& kp, dim3 grid, cudaStream_t stream) {
                 "the warps' merge buffer must fit in the ring");
   // The sum-of-squares epilogue is a separate instantiation: compiled in, even unused, it
   // measured ~0.5 us slower on single-sequence calls.
-  // Reading q/k/v/gate from the GEMV partials (QK) is one more: the other instantiations
-  // keep their code.
-  const int bytes = Smem<HD, NS>::bytes(kp.nsub);
-  if (kp.qk) {
-    if (kp.sumsq) return launch<HD, NT, NS, true, true>(kp, grid, bytes, stream);
-    return launch<HD, NT, NS, false, true>(kp, grid, bytes, stream);
-  }
-  if (kp.sumsq) return launch<HD, NT, NS, true, false>(kp, grid, bytes, stream);
-  return launch<HD, NT, NS, false, false>(kp, grid, bytes, stream);
+  if (kp.sumsq) return launch<HD, NT, NS, true>(kp, grid, Smem<HD, NS>::bytes(kp.nsub), stream);
+  return launch<HD, NT, NS, false>(kp, grid, Smem<HD, NS>::bytes(kp.nsub), stream);
 }
 
 template <int HD>
@@ -2062,21 +1907,7 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
   const bool multi = a.flags & DORY_FLAG_MULTI_TOKEN;
   const bool shared = a.flags & DORY_FLAG_SHARED_CACHE;
   const bool overlap = a.flags & DORY_FLAG_OVERLAP_LAUNCH;
-  const bool qkp = a.flags & DORY_FLAG_QKVG_PARTIALS;
   if (a.num_tokens < 0) return fail(DORY_ERR_INVALID_ARGUMENT, "negative token count");
-  if (qkp) {
-    if (!raw || !multi)
-      return fail(DORY_ERR_INVALID_ARGUMENT, "q/k/v/gate partials need a raw multi-token call");
-    if (!a.qkvg_partials || !a.positions || !a.cos_sin || !a.s_gate)
-      return fail(DORY_ERR_INVALID_ARGUMENT, "partials, positions, cos_sin and s_gate are required");
-    if (a.split_k < 1 || a.max_position < 1)
-      return fail(DORY_ERR_INVALID_ARGUMENT, "split_k and max_position must be positive");
-    if (a.positions_dtype < 0 || a.positions_dtype > 1 || a.cos_sin_dtype < 0 ||
-        a.cos_sin_dtype > 2 || a.s_gate_dtype < 0 || a.s_gate_dtype > 2)
-      return fail(DORY_ERR_INVALID_ARGUMENT, "positions / cos_sin / s_gate dtype");
-    if (reinterpret_cast<uintptr_t>(a.qkvg_partials) & 15)
-      return fail(DORY_ERR_ALIGNMENT, "q/k/v/gate partials need a 16-byte aligned base");
-  }
   if (a.num_tokens > a.max_tokens)
     return fail(DORY_ERR_INVALID_ARGUMENT, "too many tokens for the scratch buffers");
   if (!multi && a.num_tokens != 1)
@@ -2085,10 +1916,10 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
     return fail(DORY_ERR_INVALID_ARGUMENT, "shared_cache needs a raw multi-token call");
   if (multi && (!a.cache_offsets || !a.block_table_offsets))
     return fail(DORY_ERR_INVALID_ARGUMENT, "multi-token calls need int64 cache/table offsets");
-  if (raw && ((!qkp && !a.v) || !a.sqk || (!multi && !a.slot_mapping)))
+  if (raw && (!a.v || !a.sqk || (!multi && !a.slot_mapping)))
     return fail(DORY_ERR_INVALID_ARGUMENT, "raw calls need v, sqk and a slot mapping");
-  if ((!qkp && (!a.q || !a.gate)) || !a.key_cache || !a.value_cache || !a.block_table ||
-      !a.seq_lens || !a.out_nibble_major || !a.scratch)
+  if (!a.q || !a.key_cache || !a.value_cache || !a.block_table || !a.seq_lens || !a.gate ||
+      !a.out_nibble_major || !a.scratch)
     return fail(DORY_ERR_INVALID_ARGUMENT, "null tensor argument");
   if (a.splits < 1 || a.blocks_per_tile < 1)
     return fail(DORY_ERR_INVALID_ARGUMENT, "splits and blocks_per_tile must be positive");
@@ -2103,7 +1934,7 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
   if (shared && a.num_tokens > kMaxSub)
     return fail(DORY_ERR_UNSUPPORTED, "shared-cache calls take at most %d tokens", kMaxSub);
   if (a.sqk_dtype < 0 || a.sqk_dtype > 2) return fail(DORY_ERR_INVALID_ARGUMENT, "sqk dtype");
-  if (!qkp && (reinterpret_cast<uintptr_t>(a.gate) & 15))
+  if (reinterpret_cast<uintptr_t>(a.gate) & 15)
     return fail(DORY_ERR_ALIGNMENT, "gate needs a 16-byte aligned base");
   if ((reinterpret_cast<uintptr_t>(a.key_cache) & 15) ||
       (reinterpret_cast<uintptr_t>(a.value_cache) & 15) || (a.stride_block & 7) ||
@@ -2179,20 +2010,6 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
   kp.overlap = overlap;
   kp.q_stride = (raw ? a.num_heads + a.num_kv_heads : a.num_heads) * HD;
   kp.nsub = raw ? (shared ? a.num_tokens : 1) : 0;
-  if (qkp) {
-    kp.qk = 1;
-    kp.pq = a.qkvg_partials;
-    kp.positions = a.positions;
-    kp.cos_sin = a.cos_sin;
-    kp.s_gate = a.s_gate;
-    kp.s_gate_factor = a.s_gate_factor;
-    kp.split_k = a.split_k;
-    kp.prow = 2 * (a.num_heads + a.num_kv_heads) * HD;
-    kp.max_position = a.max_position;
-    kp.pos_dtype = a.positions_dtype;
-    kp.cos_dtype = a.cos_sin_dtype;
-    kp.sgate_dtype = a.s_gate_dtype;
-  }
   // Tensor maps of the K and V views.  Multi-token calls may shift the cache by whole
   // blocks (per-loop caches at cache_offsets[t]); the block extent then allows up to 64
   // caches' worth of blocks past the view.  Other offsets take the copy path.

@@ -151,52 +151,6 @@ class DecodeAttention:
                      block_table_offsets=block_table_offsets, shared=shared_cache,
                      out_sumsq=out_sumsq)
 
-    def multi_from_partials(self, qkvg_partials: torch.Tensor, positions: torch.Tensor,
-                            cos_sin_cache: torch.Tensor, s_gate: torch.Tensor,
-                            s_gate_factor: float, sqk: torch.Tensor, sqk_factor: float,
-                            eps: float, cache_offsets: torch.Tensor, key_cache: torch.Tensor,
-                            value_cache: torch.Tensor, block_tables: torch.Tensor,
-                            block_table_offsets: torch.Tensor, seq_lens: torch.Tensor,
-                            window: int, softmax_scale: float, out_nibble_major: torch.Tensor,
-                            shared_cache: bool = False,
-                            out_sumsq: torch.Tensor | None = None) -> None:
-        """multi_from_raw fed by the multi-token path's q/k/v/gate GEMV directly: its
-        epilogue (the reference's _qkvg_epilogue_kernel, kernels/dory_multi_token.py:53-80,
-        which MultiTokenSublayers.attention launches before multi_from_raw, :196-205) runs
-        inside this launch, so qk, v and gate are never written out.  No counterpart in the
-        reference's DecodeAttention.
-
-        qkvg_partials: FP32 [split_k, T, 2 * (heads + kv_heads) * head_dim], the GEMV's
-        split-K partial sums (rows: q heads, k heads, v heads, output gate; rows 2i and 2i + 1
-        of a q or k head are rotary dims i and i + head_dim / 2); positions: [T] int64 or
-        int32 rotary positions; cos_sin_cache: [max_position, head_dim] (cos, then sin) of
-        float32 / bfloat16 / float16; s_gate: [heads * head_dim], gate = sigmoid(y * s * s)
-        with s = s_gate * s_gate_factor.  The rest as multi_from_raw."""
-        tokens = seq_lens.shape[0]
-        if (tokens > self.max_tokens or cache_offsets.dtype != torch.int64
-                or block_table_offsets.dtype != torch.int64):
-            raise ValueError("too many tokens for the scratch buffers, or non-int64 offsets")
-        rows = 2 * (self.num_heads + self.num_kv_heads) * self.head_dim
-        if (qkvg_partials.dtype != torch.float32 or qkvg_partials.dim() != 3
-                or qkvg_partials.shape[1] != tokens or qkvg_partials.shape[2] != rows
-                or not qkvg_partials.is_contiguous()):
-            raise ValueError("qkvg_partials must be contiguous float32 [split_k, T, "
-                             "2 * (heads + kv_heads) * head_dim]")
-        if positions.dtype not in (torch.int64, torch.int32) or positions.numel() != tokens:
-            raise ValueError("positions must be int64 or int32 with one entry per token")
-        if (cos_sin_cache.dim() != 2 or cos_sin_cache.shape[1] != self.head_dim
-                or cos_sin_cache.dtype not in _SQK_DTYPES or not cos_sin_cache.is_contiguous()):
-            raise ValueError("cos_sin_cache must be contiguous [max_position, head_dim]")
-        if (s_gate.dtype not in _SQK_DTYPES or s_gate.numel() != self.num_heads * self.head_dim
-                or not s_gate.is_contiguous()):
-            raise ValueError("s_gate must be contiguous with heads * head_dim entries")
-        self._launch(None, key_cache, value_cache, block_tables, seq_lens, window,
-                     softmax_scale, None, out_nibble_major, raw=(None, sqk, sqk_factor, eps, None),
-                     tokens=tokens, cache_offsets=cache_offsets,
-                     block_table_offsets=block_table_offsets, shared=shared_cache,
-                     out_sumsq=out_sumsq,
-                     qkvg=(qkvg_partials, positions, cos_sin_cache, s_gate, s_gate_factor))
-
     # ---- diagnostics ----
 
     def fetch_errors(self, clear: bool = True) -> int:
@@ -219,7 +173,7 @@ class DecodeAttention:
 
     def _launch(self, q, key_cache, value_cache, block_table, seq_lens, window, softmax_scale,
                 gate, out_nibble_major, raw, tokens, cache_offsets,
-                block_table_offsets=None, shared=False, out_sumsq=None, qkvg=None) -> None:
+                block_table_offsets=None, shared=False, out_sumsq=None) -> None:
         if key_cache.stride() != value_cache.stride() or key_cache.stride(-1) != 1:
             raise ValueError("key and value caches need equal strides and unit last stride")
         if key_cache.dtype != torch.bfloat16 or value_cache.dtype != torch.bfloat16:
@@ -232,22 +186,9 @@ class DecodeAttention:
             raise ValueError("block tables and seq_lens must be int32")
         p = self._params
         flags = _native.FLAG_OVERLAP_LAUNCH if self.overlap_launch else 0
-        if qkvg is not None:
-            partials, positions, cos_sin, s_gate, s_gate_factor = qkvg
-            flags |= _native.FLAG_QKVG_PARTIALS
-            p.qkvg_partials, p.positions = partials.data_ptr(), positions.data_ptr()
-            p.cos_sin, p.s_gate = cos_sin.data_ptr(), s_gate.data_ptr()
-            p.s_gate_factor, p.split_k = float(s_gate_factor), partials.shape[0]
-            p.max_position = cos_sin.shape[0]
-            p.positions_dtype = 0 if positions.dtype == torch.int64 else 1
-            p.cos_sin_dtype, p.s_gate_dtype = _SQK_DTYPES[cos_sin.dtype], _SQK_DTYPES[s_gate.dtype]
-        else:
-            p.qkvg_partials = p.positions = p.cos_sin = p.s_gate = None
-            p.s_gate_factor, p.split_k, p.max_position = 0.0, 0, 0
-            p.positions_dtype = p.cos_sin_dtype = p.s_gate_dtype = 0
         if raw is not None:
             v, sqk, sqk_factor, eps, slot_mapping = raw
-            if qkvg is None and (q.dtype != torch.float32 or v.dtype != torch.float32):
+            if q.dtype != torch.float32 or v.dtype != torch.float32:
                 raise ValueError("raw q/k and v must be float32")
             sqk_dtype = _SQK_DTYPES.get(sqk.dtype)
             if sqk_dtype is None:
@@ -255,7 +196,7 @@ class DecodeAttention:
             if slot_mapping is not None and slot_mapping.dtype != torch.int64:
                 raise ValueError("slot_mapping must be int64")
             flags |= _native.FLAG_RAW_QKV
-            p.v, p.sqk, p.slot_mapping = _ptr(v), sqk.data_ptr(), _ptr(slot_mapping)
+            p.v, p.sqk, p.slot_mapping = v.data_ptr(), sqk.data_ptr(), _ptr(slot_mapping)
             p.sqk_factor, p.eps, p.sqk_dtype = float(sqk_factor), float(eps), sqk_dtype
         else:
             if q.dtype != torch.bfloat16:
@@ -269,14 +210,14 @@ class DecodeAttention:
             p.cache_offsets, p.block_table_offsets = cache_offsets.data_ptr(), block_table_offsets.data_ptr()
         else:
             p.cache_offsets = p.block_table_offsets = None
-        if (gate is not None and gate.dtype != torch.float32) or out_nibble_major.dtype != torch.float32:
+        if gate.dtype != torch.float32 or out_nibble_major.dtype != torch.float32:
             raise ValueError("gate and out_nibble_major must be float32")
         for t in (q, gate, out_nibble_major, seq_lens):
-            if t is not None and not t.is_contiguous():
+            if not t.is_contiguous():
                 raise ValueError("q/qk, v, gate, seq_lens and out_nibble_major must be contiguous")
-        p.q, p.key_cache, p.value_cache = _ptr(q), key_cache.data_ptr(), value_cache.data_ptr()
+        p.q, p.key_cache, p.value_cache = q.data_ptr(), key_cache.data_ptr(), value_cache.data_ptr()
         p.block_table, p.seq_lens = block_table.data_ptr(), seq_lens.data_ptr()
-        p.gate, p.out_nibble_major = _ptr(gate), out_nibble_major.data_ptr()
+        p.gate, p.out_nibble_major = gate.data_ptr(), out_nibble_major.data_ptr()
         if out_sumsq is not None:
             if (out_sumsq.dtype != torch.float32 or not out_sumsq.is_contiguous()
                     or out_sumsq.numel() < tokens):

@@ -21,7 +21,7 @@ library, under the reference kernels' own names and launch forms.
   - `qkvg_epilogue(...)`: split-K sum, rotary embedding, sigmoid output gate;
   - `_qkvg_epilogue_kernel[(rows // HEAD_DIM, T)](partials, positions, cos_sin, s_gate,
     qk, v, gate, s_gate_factor, Q_ROWS=, KV_ROWS=, HEAD_DIM=, SPLIT_K=, T=, num_warps=4)`.
-  DecodeAttention.multi_from_partials does the same inside the attention launch.
+  Its outputs are the inputs of DecodeAttention.multi_from_raw.
 * `route_reference_kernels()`: points the reference modules' own kernel names
   (dory_attention._qk_norm_cache_kernel, dory_multi_token._qkvg_epilogue_kernel) at these
   steps, so the reference's sublayers (whose GEMVs are not part of this build) run them.

@@ -60,13 +60,7 @@ enum {
    * immediately before this call on the stream must not write this call's seq_lens, block
    * tables, offsets, slot_mapping or the cache rows it attends (q/k/v/gate and all outputs
    * are ordered as usual).  No counterpart in the reference (Triton launches). */
-  DORY_FLAG_OVERLAP_LAUNCH = 8u,
-  /* With RAW_QKV | MULTI_TOKEN: q, k, v and the output gate come from the multi-token
-   * path's split-K q/k/v/gate GEMV partials (qkvg_partials and the fields after it) instead
-   * of q, v and gate, which are then unused: the reference's _qkvg_epilogue_kernel
-   * (kernels/dory_multi_token.py:53-80) done inside this launch.  No counterpart in the
-   * reference (it launches the epilogue on its own before multi_from_raw). */
-  DORY_FLAG_QKVG_PARTIALS = 16u
+  DORY_FLAG_OVERLAP_LAUNCH = 8u
 };
 
 /* Device error bits, accumulated in the scratch header and read back with
@@ -76,8 +70,8 @@ enum {
   DORY_DEVERR_SLOT_OOB = 2u,      /* an append slot outside the cache                     */
   DORY_DEVERR_OFFSET_ALIGN = 4u,  /* a cache offset not a multiple of 8 elements          */
   DORY_DEVERR_WAIT_TIMEOUT = 8u,  /* a pipeline wait gave up after its iteration limit    */
-  DORY_DEVERR_POSITION_OOB = 16u  /* a rotary position outside [0, max_position): that
-                                   * token's q and k are taken as zero                     */
+  DORY_DEVERR_POSITION_OOB = 16u  /* dory_qkvg_epilogue: a rotary position outside
+                                   * [0, max_position); that token's q and k are zero      */
 };
 
 /*
@@ -127,19 +121,6 @@ typedef struct DoryDecodeParams {
   int32_t max_tokens;             /* scratch capacity in tokens                             */
   int32_t sqk_dtype;              /* DoryDType                                               */
   uint32_t flags;                 /* DORY_FLAG_*                                             */
-  /* DORY_FLAG_QKVG_PARTIALS only (NULL / 0 otherwise).  Rows of the partials: q heads, k
-   * heads, v heads, output gate (2 * (Q + NKV * HD)); rows 2i and 2i + 1 of a q or k head
-   * hold rotary dims i and i + HD / 2 (reference rotary_pair_order). */
-  const float* qkvg_partials;     /* FP32 [split_k, T, 2 * (Q + NKV * HD)], 16-byte aligned */
-  const void* positions;          /* [T] rotary positions, int64 or int32 (positions_dtype) */
-  const void* cos_sin;            /* [max_position, HD] of cos_sin_dtype: cos, then sin     */
-  const void* s_gate;             /* [Q] output-gate scales of s_gate_dtype                  */
-  float s_gate_factor;            /* gate = sigmoid(y * s * s), s = s_gate * s_gate_factor   */
-  int32_t split_k;                /* >= 1                                                    */
-  int32_t max_position;           /* cos_sin.shape[0]                                        */
-  int32_t positions_dtype;        /* 0: int64, 1: int32                                      */
-  int32_t cos_sin_dtype;          /* DoryDType                                               */
-  int32_t s_gate_dtype;           /* DoryDType                                               */
 } DoryDecodeParams;
 
 /* ABI version of the loaded library (DORY_DECODE_ABI_VERSION). */
@@ -247,8 +228,7 @@ int32_t dory_qk_norm_cache(const DoryQkNormParams* params, void* stream);
  * runs between its q/k/v/gate GEMV and multi_from_raw (:196-205).  Reads the split-K
  * partials and writes qk FP32 [T, (NH + NKV) * HD] (rotary embedding applied), v FP32
  * [T, NKV * HD] and gate FP32 [T, NH * HD] (sigmoid applied): the inputs of a raw
- * multi-token call.  dory_decode_attention with DORY_FLAG_QKVG_PARTIALS does the same
- * inside the attention launch.
+ * multi-token call (dory_decode_attention with RAW_QKV | MULTI_TOKEN).
  */
 typedef struct DoryQkvgParams {
   const float* partials;          /* FP32 [split_k, T, 2 * (Q + NKV * HD)], 16-byte aligned */

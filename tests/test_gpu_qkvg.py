@@ -1,13 +1,13 @@
-"""The multi-token path's q/k/v/gate epilogue on B200, on its own and inside the attention.
+"""The multi-token path's q/k/v/gate epilogue on B200.
 
 * `qkvg_epilogue` (the reference's `_qkvg_epilogue_kernel`, kernels/dory_multi_token.py:53-80)
   against the golden vectors the reference's own kernel produced: qk and v to the bit, the
   gate within the sigmoid's rounding; the launch-form shim gives the same bits.
-* `DecodeAttention.multi_from_partials` (the epilogue inside the attention launch) against
-  the same epilogue followed by `multi_from_raw`: outputs, out_sumsq and the cache pool to the
-  bit, for single tokens, batches with padding and shared-cache wavefronts, head dims
-  64/128/256, split_k 1-4, int64/int32 positions, FP32/BF16 cos-sin tables and gate scales;
-  and against the oracle (epilogue then attention) within the BASELINE bar, cache bit-exact.
+* The multi-token sublayer's two launches (the epilogue, then `multi_from_raw`, as
+  MultiTokenSublayers.attention runs them, :196-205) against the oracle (its epilogue, then
+  its attention) within the BASELINE bar, the cache pool bit-exact: single tokens, batches
+  with padding, shared-cache wavefronts, head dims 64/128/256, split_k 1-4, int64/int32
+  positions, FP32/BF16/FP16 cos-sin tables and gate scales, with out_sumsq.
 * Positions outside the cos/sin table are reported in the error word, not dereferenced.
 """
 
@@ -73,7 +73,7 @@ def test_launch_form_shim_gives_same_bits():
     assert torch.equal(qk2.cpu(), qk) and torch.equal(v2.cpu(), v) and torch.equal(g2.cpu(), gate)
 
 
-# ---- the epilogue inside the attention launch ----
+# ---- the epilogue, then the attention ----
 
 def with_partials(case: W.Case, seed: int, split_k: int, cos_dtype=torch.float32,
                   s_gate_dtype=torch.bfloat16):
@@ -93,37 +93,31 @@ def with_partials(case: W.Case, seed: int, split_k: int, cos_dtype=torch.float32
     return ex
 
 
-def run_both(case: W.Case, ex, splits=8, sumsq=False, int32_positions=False):
-    """(fused out, fused sumsq, fused raw cache), (unfused ...), as CPU tensors."""
+def run_sublayer(case: W.Case, ex, splits=8, sumsq=False, int32_positions=False):
+    """The epilogue then multi_from_raw on the device: (out, sumsq, raw cache) on the CPU."""
     NH, NKV, HD, T = case.num_heads, case.num_kv_heads, case.head_dim, case.tokens
-    results = []
-    for fused in (True, False):
-        d = W.to_device(case, "triton", DEV)
-        attn = DecodeAttention(NH, NKV, HD, DEV, splits=splits, max_tokens=max(T, 1))
-        ss = torch.full((T,), float("nan"), device=DEV) if sumsq else None
-        parts = ex["partials"].to(DEV)
-        pos = ex["positions"].to(torch.int32 if int32_positions else torch.int64).to(DEV)
-        cos_sin, s_gate = ex["cos_sin"].to(DEV), ex["s_gate"].to(DEV)
-        if fused:
-            attn.multi_from_partials(parts, pos, cos_sin, s_gate, ex["s_gate_factor"], d["sqk"],
-                                     case.sqk_factor, EPS, d["cache_offsets"], d["key"],
-                                     d["value"], d["tables"], d["table_offsets"], d["seq_lens"],
-                                     case.window, case.scale, d["out"],
-                                     shared_cache=case.shared, out_sumsq=ss)
-        else:
-            qk = torch.empty(T, (NH + NKV) * HD, device=DEV)
-            v = torch.empty(T, NKV * HD, device=DEV)
-            gate = torch.empty(T, NH * HD, device=DEV)
-            qkvg_epilogue(parts, pos, cos_sin, s_gate, ex["s_gate_factor"], qk, v, gate, NH,
-                          NKV, HD)
-            attn.multi_from_raw(qk, v, d["sqk"], case.sqk_factor, EPS, d["cache_offsets"],
-                                d["key"], d["value"], d["tables"], d["table_offsets"],
-                                d["seq_lens"], case.window, case.scale, gate, d["out"],
-                                shared_cache=case.shared, out_sumsq=ss)
-        torch.cuda.synchronize()
-        attn.check_errors()
-        results.append((d["out"].cpu(), None if ss is None else ss.cpu(), d["raw"].cpu()))
-    return results
+    d = W.to_device(case, "triton", DEV)
+    attn = DecodeAttention(NH, NKV, HD, DEV, splits=splits, max_tokens=max(T, 1))
+    ss = torch.full((T,), float("nan"), device=DEV) if sumsq else None
+    pos = ex["positions"].to(torch.int32 if int32_positions else torch.int64).to(DEV)
+    qk = torch.empty(T, (NH + NKV) * HD, device=DEV)
+    v = torch.empty(T, NKV * HD, device=DEV)
+    gate = torch.empty(T, NH * HD, device=DEV)
+    qkvg_epilogue(ex["partials"].to(DEV), pos, ex["cos_sin"].to(DEV), ex["s_gate"].to(DEV),
+                  ex["s_gate_factor"], qk, v, gate, NH, NKV, HD)
+    attn.multi_from_raw(qk, v, d["sqk"], case.sqk_factor, EPS, d["cache_offsets"], d["key"],
+                        d["value"], d["tables"], d["table_offsets"], d["seq_lens"], case.window,
+                        case.scale, gate, d["out"], shared_cache=case.shared, out_sumsq=ss)
+    torch.cuda.synchronize()
+    attn.check_errors()
+    return d["out"].cpu(), None if ss is None else ss.cpu(), d["raw"].cpu()
+
+
+def check_against_oracle(case, out, raw):
+    assert_close(out, oracle_out(case))
+    before = W.to_device(case, "triton", "cpu")["raw"]
+    exp = expected_raw(case, "triton", before, oracle_rows(case))
+    assert torch.equal(raw.view(torch.int16), exp.view(torch.int16))
 
 
 CASES = {
@@ -144,76 +138,56 @@ CASES = {
 
 @pytest.mark.parametrize("split_k", [1, 2, 4])
 @pytest.mark.parametrize("name", sorted(CASES))
-def test_fused_equals_epilogue_then_attention(name, split_k):
+def test_epilogue_then_attention_matches_oracle(name, split_k):
     case = CASES[name]()
     if name == "batched_padding":
         case.seq_lens[0] = 0
     ex = with_partials(case, seed=910 + split_k, split_k=split_k)
-    (fo, _, fraw), (uo, _, uraw) = run_both(case, ex)
-    assert torch.equal(fo, uo)
-    assert torch.equal(fraw.view(torch.int16), uraw.view(torch.int16))
-
-
-@pytest.mark.parametrize("name", ["single_256", "wavefront_128", "batched_padding"])
-def test_fused_matches_oracle(name):
-    case = CASES[name]()
-    if name == "batched_padding":
-        case.seq_lens[0] = 0
-    ex = with_partials(case, seed=920, split_k=2)
-    (fo, _, fraw), _ = run_both(case, ex)
-    assert_close(fo, oracle_out(case))
-    d = W.to_device(case, "triton", "cpu", copy_cache=True)
-    exp = expected_raw(case, "triton", d["raw"], oracle_rows(case))
-    assert torch.equal(fraw.view(torch.int16), exp.view(torch.int16))
+    out, _, raw = run_sublayer(case, ex)
+    check_against_oracle(case, out, raw)
 
 
 @pytest.mark.parametrize("cos_dtype,s_gate_dtype,int32_positions",
                          [(torch.bfloat16, torch.float32, True),
                           (torch.float16, torch.bfloat16, False)])
-def test_fused_dtypes_and_sumsq(cos_dtype, s_gate_dtype, int32_positions):
+def test_dtypes_and_sumsq(cos_dtype, s_gate_dtype, int32_positions):
     case = CASES["wavefront_256"]()
     ex = with_partials(case, seed=930, split_k=3, cos_dtype=cos_dtype, s_gate_dtype=s_gate_dtype)
-    (fo, fss, fraw), (uo, uss, uraw) = run_both(case, ex, sumsq=True,
-                                                int32_positions=int32_positions)
-    assert torch.equal(fo, uo) and torch.equal(fss, uss)
-    assert torch.equal(fraw.view(torch.int16), uraw.view(torch.int16))
-    assert_close(fo, oracle_out(case))
+    out, ss, raw = run_sublayer(case, ex, sumsq=True, int32_positions=int32_positions)
+    check_against_oracle(case, out, raw)
+    torch.testing.assert_close(ss.double(), out.double().reshape(case.tokens, -1).square().sum(1),
+                               rtol=1e-5, atol=1e-6)
 
 
 def test_position_outside_table_is_reported():
     case = W.single(seed=940, context=300, pool_blocks=30)
     ex = with_partials(case, seed=941, split_k=1)
-    ex["cos_sin"] = ex["cos_sin"][:100]  # position 300 is past the table
-    d = W.to_device(case, "triton", DEV)
-    attn = DecodeAttention(32, 8, 128, DEV, splits=4)
-    attn.multi_from_partials(ex["partials"].to(DEV), ex["positions"].to(DEV),
-                             ex["cos_sin"].to(DEV), ex["s_gate"].to(DEV), ex["s_gate_factor"],
-                             d["sqk"], case.sqk_factor, EPS, d["cache_offsets"], d["key"],
-                             d["value"], d["tables"], d["table_offsets"], d["seq_lens"], 0,
-                             case.scale, d["out"])
+    NH, NKV, HD = 32, 8, 128
+    err = torch.zeros(1, dtype=torch.int32, device=DEV)
+    qk = torch.full((1, (NH + NKV) * HD), float("nan"), device=DEV)
+    v = torch.empty(1, NKV * HD, device=DEV)
+    gate = torch.empty(1, NH * HD, device=DEV)
+    qkvg_epilogue(ex["partials"].to(DEV), ex["positions"].to(DEV), ex["cos_sin"][:100].to(DEV),
+                  ex["s_gate"].to(DEV), 0.9, qk, v, gate, NH, NKV, HD, error_word=err)
     torch.cuda.synchronize()
-    assert attn.fetch_errors() & 16  # DORY_DEVERR_POSITION_OOB
-    assert torch.isfinite(d["out"]).all()
+    assert int(err.item()) & 16  # DORY_DEVERR_POSITION_OOB: position 300 is past the table
+    assert torch.equal(qk.cpu(), torch.zeros_like(qk.cpu()))
 
 
 def test_argument_errors():
-    case = W.single(seed=950, context=100, pool_blocks=10)
-    ex = with_partials(case, seed=951, split_k=2)
-    d = W.to_device(case, "triton", DEV)
-    attn = DecodeAttention(32, 8, 128, DEV, splits=4)
-    args = [ex["partials"].to(DEV), ex["positions"].to(DEV), ex["cos_sin"].to(DEV),
-            ex["s_gate"].to(DEV), 0.9, d["sqk"], case.sqk_factor, EPS, d["cache_offsets"],
-            d["key"], d["value"], d["tables"], d["table_offsets"], d["seq_lens"], 0,
-            case.scale, d["out"]]
-    bad = list(args)
-    bad[0] = args[0][:, :, :-128].contiguous()  # wrong row count
-    with pytest.raises(ValueError):
-        attn.multi_from_partials(*bad)
-    bad = list(args)
-    bad[1] = args[1].to(torch.float32)  # float positions
-    with pytest.raises(ValueError):
-        attn.multi_from_partials(*bad)
-    bad = list(args)
-    bad[2] = args[2][:, :64].contiguous()  # cos/sin of the wrong head dim
-    with pytest.raises(ValueError):
-        attn.multi_from_partials(*bad)
+    NH, NKV, HD, T = 4, 2, 64, 2
+    Q, KV = NH * HD, NKV * HD
+    parts = torch.zeros(1, T, 2 * (Q + KV), device=DEV)
+    pos = torch.zeros(T, dtype=torch.int64, device=DEV)
+    cs = torch.zeros(8, HD, device=DEV)
+    sg = torch.ones(Q, device=DEV)
+    outs = (torch.empty(T, Q + KV, device=DEV), torch.empty(T, KV, device=DEV),
+            torch.empty(T, Q, device=DEV))
+    with pytest.raises(ValueError):  # wrong row count
+        qkvg_epilogue(parts[:, :, :-64].contiguous(), pos, cs, sg, 1.0, *outs, NH, NKV, HD)
+    with pytest.raises(ValueError):  # float positions
+        qkvg_epilogue(parts, pos.float(), cs, sg, 1.0, *outs, NH, NKV, HD)
+    with pytest.raises(ValueError):  # cos/sin of another head dim
+        qkvg_epilogue(parts, pos, cs[:, :32].contiguous(), sg, 1.0, *outs, NH, NKV, HD)
+    with pytest.raises(ValueError):  # output of the wrong size
+        qkvg_epilogue(parts, pos, cs, sg, 1.0, outs[0][:1], outs[1], outs[2], NH, NKV, HD)
