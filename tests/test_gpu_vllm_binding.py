@@ -22,12 +22,17 @@ from vllm_binding import VllmDecodeBinding, kv_cache_views
 
 pytestmark = pytest.mark.gpu
 
-triton_attn = pytest.importorskip("vllm.v1.attention.backends.triton_attn")
 DEV = torch.device("cuda")
+
+
+def triton_backend():
+    """vLLM's Triton attention backend module (imported only when a test runs)."""
+    return pytest.importorskip("vllm.v1.attention.backends.triton_attn")
 
 
 def vllm_batch(case: W.Case, layout: str, padded: int, extra_width: int = 3):
     """(kv_cache, metadata, slot_mapping list) of a decode batch in vLLM's structures."""
+    triton_attn = triton_backend()
     NKV, HD, B = case.num_kv_heads, case.head_dim, case.block_size
     if layout == "vllm":
         shape = triton_attn.TritonAttentionBackend.get_kv_cache_shape(case.num_blocks, B, NKV, HD)
