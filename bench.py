@@ -422,7 +422,7 @@ def layer_call(attn, wl: DeviceWorkload, app: int, layer: int, ins, out):
         from dory_sublayer_steps import qkvg_epilogue
         qk_b, v_b, gate_b = wl.qkvg_bufs
         qkvg_epilogue(ins[0], wl.positions, wl.cos_sin, wl.s_gate, 0.9, qk_b, v_b, gate_b,
-                      wl.nh, wl.nkv, wl.hd)
+                      wl.nh, wl.nkv, wl.hd, overlap_launch=attn.overlap_launch)
         attn.multi_from_raw(qk_b, v_b, wl.sqk, W.SQK_FACTOR, EPS, wl.cache_offsets, key, value,
                             wl.tables, wl.table_offsets, wl.seq_lens, window, scale, gate_b, out,
                             shared_cache=wl.shared, out_sumsq=sumsq)

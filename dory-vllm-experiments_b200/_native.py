@@ -81,6 +81,7 @@ class DoryQkvgParams(ctypes.Structure):
         ("s_gate_factor", _f32), ("num_tokens", _i32), ("num_heads", _i32),
         ("num_kv_heads", _i32), ("head_dim", _i32), ("split_k", _i32), ("max_position", _i32),
         ("positions_dtype", _i32), ("cos_sin_dtype", _i32), ("s_gate_dtype", _i32),
+        ("flags", _u32),
     ]
 
 

@@ -1575,6 +1575,11 @@ struct QkvgArgs {
 template <int HD>
 __global__ void __launch_bounds__(HD / 2) qkvg_epilogue_kernel(const __grid_constant__ QkvgArgs a) {
   constexpr int HALF = HD / 2;
+  // Programmatic dependent launch (no-ops otherwise): the partials are read after the
+  // previous grid; the next grid (an overlapped attention call, whose consumers wait for
+  // this grid to complete before reading qk / v / gate) may start at once.
+  grid_dependency_wait();
+  grid_launch_dependents();
   const int b = blockIdx.x, t = blockIdx.y, i = threadIdx.x;
   const int64_t prow = 2 * int64_t(a.NH + a.NKV) * HD;
   const int64_t row = int64_t(b) * HD + 2 * i;
@@ -1839,12 +1844,21 @@ int32_t dory_qkvg_epilogue(const DoryQkvgParams* P, void* stream) {
   k.pos_dtype = a.positions_dtype;
   k.cos_dtype = a.cos_sin_dtype;
   k.sgate_dtype = a.s_gate_dtype;
-  const dim3 grid(2 * (a.num_heads + a.num_kv_heads), a.num_tokens);
-  cudaStream_t s = (cudaStream_t)stream;
-  if (a.head_dim == 64) qkvg_epilogue_kernel<64><<<grid, 32, 0, s>>>(k);
-  else if (a.head_dim == 128) qkvg_epilogue_kernel<128><<<grid, 64, 0, s>>>(k);
-  else qkvg_epilogue_kernel<256><<<grid, 128, 0, s>>>(k);
-  const cudaError_t e = cudaGetLastError();
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(2 * (a.num_heads + a.num_kv_heads), a.num_tokens);
+  cfg.blockDim = dim3(a.head_dim / 2);
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (a.flags & DORY_FLAG_OVERLAP_LAUNCH) ? 1 : 0;
+  cudaError_t e;
+  if (a.head_dim == 64) e = cudaLaunchKernelEx(&cfg, qkvg_epilogue_kernel<64>, k);
+  else if (a.head_dim == 128) e = cudaLaunchKernelEx(&cfg, qkvg_epilogue_kernel<128>, k);
+  else e = cudaLaunchKernelEx(&cfg, qkvg_epilogue_kernel<256>, k);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return fail(DORY_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
   return DORY_OK;
 }

@@ -142,13 +142,17 @@ _qk_norm_cache_kernel = _QkNormCacheLaunch()
 def qkvg_epilogue(partials: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor,
                   s_gate: torch.Tensor, s_gate_factor: float, qk: torch.Tensor,
                   v: torch.Tensor, gate: torch.Tensor, num_heads: int, num_kv_heads: int,
-                  head_dim: int, error_word: torch.Tensor | None = None) -> None:
+                  head_dim: int, error_word: torch.Tensor | None = None,
+                  overlap_launch: bool = False) -> None:
     """The multi-token path's q/k/v/gate epilogue: partials FP32 [split_k, T, 2 * (Q + KV)]
     (rows: q heads, k heads, v heads, output gate; rows 2i and 2i + 1 of a q or k head are
     rotary dims i and i + head_dim / 2) -> qk FP32 [T, Q + KV] (rotary embedding at
     positions[t] from cos_sin [max_position, head_dim]), v FP32 [T, KV] and gate FP32
     [T, Q] = sigmoid(y * s * s), s = s_gate * s_gate_factor.  error_word: optional int32
-    device tensor that collects DORY_DEVERR_POSITION_OOB.  Enqueued on the current
+    device tensor that collects DORY_DEVERR_POSITION_OOB.  overlap_launch: launch as a
+    programmatic dependent of the previous kernel (its partials are read after it
+    completes); either way an attention call made with overlap_launch may start while this
+    kernel runs, its reads of qk / v / gate waiting for it.  Enqueued on the current
     stream."""
     Q, KV = num_heads * head_dim, num_kv_heads * head_dim
     if (partials.dtype != torch.float32 or partials.dim() != 3 or partials.shape[2] != 2 * (Q + KV)
@@ -177,6 +181,7 @@ def qkvg_epilogue(partials: torch.Tensor, positions: torch.Tensor, cos_sin: torc
     p.split_k, p.max_position = partials.shape[0], cos_sin.shape[0]
     p.positions_dtype = 0 if positions.dtype == torch.int64 else 1
     p.cos_sin_dtype, p.s_gate_dtype = _SQK_DTYPES[cos_sin.dtype], _SQK_DTYPES[s_gate.dtype]
+    p.flags = _native.FLAG_OVERLAP_LAUNCH if overlap_launch else 0
     stream = torch.cuda.current_stream(partials.device).cuda_stream
     _native.check(_native.load().dory_qkvg_epilogue(ctypes.byref(p), ctypes.c_void_p(stream)))
 

@@ -249,6 +249,11 @@ typedef struct DoryQkvgParams {
   int32_t positions_dtype;        /* 0: int64, 1: int32 */
   int32_t cos_sin_dtype;          /* DoryDType */
   int32_t s_gate_dtype;           /* DoryDType */
+  uint32_t flags;                 /* DORY_FLAG_OVERLAP_LAUNCH: launch as a programmatic
+                                   * dependent of the previous kernel on the stream (the
+                                   * partials are read after it completes); the kernel lets
+                                   * its own dependent (an overlapped attention call) start
+                                   * at once, whose reads of qk / v / gate wait for it */
 } DoryQkvgParams;
 
 /* sizeof(DoryQkvgParams) as compiled into the library. */

@@ -191,3 +191,51 @@ def test_argument_errors():
         qkvg_epilogue(parts, pos, cs[:, :32].contiguous(), sg, 1.0, *outs, NH, NKV, HD)
     with pytest.raises(ValueError):  # output of the wrong size
         qkvg_epilogue(parts, pos, cs, sg, 1.0, outs[0][:1], outs[1], outs[2], NH, NKV, HD)
+
+
+def test_overlapped_chain_reusing_buffers_in_a_graph():
+    """Epilogue and attention of several layers, every launch a programmatic dependent of
+    the one before, all layers sharing one set of qk / v / gate buffers (each epilogue
+    rewrites them while the previous layer's attention may still be reading its gate):
+    the same bits as plain launches."""
+    cases = [CASES["wavefront_128"]() for _ in range(3)]
+    exs = [with_partials(c, seed=970 + i, split_k=2) for i, c in enumerate(cases)]
+    NH, NKV, HD, T = 32, 8, 128, cases[0].tokens
+    devs = [W.to_device(c, "triton", DEV) for c in cases]
+    bufs = (torch.empty(T, (NH + NKV) * HD, device=DEV), torch.empty(T, NKV * HD, device=DEV),
+            torch.empty(T, NH * HD, device=DEV))
+    parts = [e["partials"].to(DEV) for e in exs]
+    pos = exs[0]["positions"].to(DEV)
+    cos_sin, s_gate = exs[0]["cos_sin"].to(DEV), exs[0]["s_gate"].to(DEV)
+
+    def step(attn, overlap):
+        for d, part in zip(devs, parts):
+            qkvg_epilogue(part, pos, cos_sin, s_gate, 0.9, *bufs, NH, NKV, HD,
+                          overlap_launch=overlap)
+            attn.multi_from_raw(bufs[0], bufs[1], d["sqk"], cases[0].sqk_factor, EPS,
+                                d["cache_offsets"], d["key"], d["value"], d["tables"],
+                                d["table_offsets"], d["seq_lens"], 0, cases[0].scale, bufs[2],
+                                d["out"], shared_cache=True)
+
+    plain = DecodeAttention(NH, NKV, HD, DEV, splits=8, max_tokens=T)
+    step(plain, False)
+    torch.cuda.synchronize()
+    want = [d["out"].clone() for d in devs]
+    over = DecodeAttention(NH, NKV, HD, DEV, splits=8, max_tokens=T, overlap_launch=True)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        step(over, True)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step(over, True)
+    for _ in range(3):
+        for d in devs:
+            d["out"].fill_(float("nan"))
+        graph.replay()
+        torch.cuda.synchronize()
+        for d, w in zip(devs, want):
+            assert torch.equal(d["out"], w)
+    over.check_errors()
