@@ -13,7 +13,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 LIBRARY = HERE / "libdory_decode.so"
 
-ABI_VERSION = 4
+ABI_VERSION = 5
 
 # DoryStatus
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_ALIGNMENT, ERR_CUDA = range(5)
@@ -36,7 +36,7 @@ EXPORTS = ("dory_decode_abi_version", "dory_decode_params_bytes", "dory_decode_s
            "dory_decode_scratch_init", "dory_decode_attention", "dory_decode_fetch_errors",
            "dory_decode_last_error", "dory_decode_attention_static_scratch",
            "dory_qk_norm_params_bytes", "dory_qk_norm_cache", "dory_qkvg_params_bytes",
-           "dory_qkvg_epilogue")
+           "dory_qkvg_epilogue", "dory_residual_params_bytes", "dory_residual_update")
 
 # Size of the library's static scratch array (DORY_DECODE_STATIC_SCRATCH_BYTES).
 STATIC_SCRATCH_BYTES = 4 << 20
@@ -85,6 +85,16 @@ class DoryQkvgParams(ctypes.Structure):
     ]
 
 
+class DoryResidualParams(ctypes.Structure):
+    """Mirror of DoryResidualParams (include/dory_decode.h); field order is the ABI."""
+    _fields_ = [
+        ("partials", _vp), ("x", _vp), ("x_sumsq", _vp), ("a", _vp), ("alpha", _vp),
+        ("h_out", _vp), ("h_out_nibble_major", _vp), ("alpha_scale", _f32), ("eps", _f32),
+        ("num_tokens", _i32), ("hidden", _i32), ("x_dim", _i32), ("split_k", _i32),
+        ("a_dtype", _i32), ("alpha_dtype", _i32), ("flags", _u32),
+    ]
+
+
 _lib = None
 
 
@@ -123,6 +133,10 @@ def load(path: os.PathLike | None = None) -> ctypes.CDLL:
     lib.dory_qkvg_params_bytes.argtypes = []
     lib.dory_qkvg_epilogue.restype = _i32
     lib.dory_qkvg_epilogue.argtypes = [ctypes.POINTER(DoryQkvgParams), _vp]
+    lib.dory_residual_params_bytes.restype = _i64
+    lib.dory_residual_params_bytes.argtypes = []
+    lib.dory_residual_update.restype = _i32
+    lib.dory_residual_update.argtypes = [ctypes.POINTER(DoryResidualParams), _vp]
     if lib.dory_decode_abi_version() != ABI_VERSION:
         raise RuntimeError(f"{path}: ABI version {lib.dory_decode_abi_version()} != {ABI_VERSION}")
     if lib.dory_decode_params_bytes() != ctypes.sizeof(DoryDecodeParams):
@@ -134,6 +148,9 @@ def load(path: os.PathLike | None = None) -> ctypes.CDLL:
     if lib.dory_qkvg_params_bytes() != ctypes.sizeof(DoryQkvgParams):
         raise RuntimeError(f"{path}: DoryQkvgParams is {lib.dory_qkvg_params_bytes()} "
                            f"bytes, the binding's is {ctypes.sizeof(DoryQkvgParams)}")
+    if lib.dory_residual_params_bytes() != ctypes.sizeof(DoryResidualParams):
+        raise RuntimeError(f"{path}: DoryResidualParams is {lib.dory_residual_params_bytes()} "
+                           f"bytes, the binding's is {ctypes.sizeof(DoryResidualParams)}")
     _lib = lib
     return lib
 

@@ -1625,6 +1625,175 @@ __global__ void __launch_bounds__(HD / 2) qkvg_epilogue_kernel(const __grid_cons
 }
 
 // ------------------------------------------------------------------------------------
+// The residual update after a sublayer's output GEMV (reference _residual_tokens_kernel,
+// kernels/dory_multi_token.py:109-131, and residual_update, kernels/dory_common.py:55-81):
+// one CTA per token; thread w owns hidden elements 8w .. 8w + 7 (G = 4 groups of them, 512
+// threads at most, when the hidden size exceeds 8192), which gives one 16-byte natural-order BF16 store and eight
+// coalesced nibble-major stores per group.
+//   b = (0 + p_0 + ... + p_{k-1}) * r_x, r_x = 1 / sqrt(sum x^2 + eps)  (1 without x)
+//   h = n(n(a) + |alpha * alpha_scale| * (n(b) - n(a)))
+// Every sum of squares is taken in FP64 and rounded once (inv_norm_from_sum); products and
+// sums are rounded one by one.  All global loads are issued before the first barrier.
+// ------------------------------------------------------------------------------------
+struct ResidualArgs {
+  const float* partials;
+  const float* x;
+  const float* x_sumsq;
+  const void* a;
+  const void* alpha;
+  __nv_bfloat16* h;
+  float* h_nm;
+  float alpha_scale, eps;
+  int T, H, K_IN, split_k, a_dtype, alpha_dtype;
+};
+
+// Eight consecutive elements [i, i + 8) of an FP32 / BF16 / FP16 array (16-byte aligned).
+__device__ __forceinline__ void load8(const void* p, int dtype, int64_t i, float (&out)[8]) {
+  if (dtype == DORY_DTYPE_F32) {
+    const float4* q = reinterpret_cast<const float4*>(static_cast<const float*>(p) + i);
+    const float4 u0 = __ldg(q), u1 = __ldg(q + 1);
+    out[0] = u0.x; out[1] = u0.y; out[2] = u0.z; out[3] = u0.w;
+    out[4] = u1.x; out[5] = u1.y; out[6] = u1.z; out[7] = u1.w;
+    return;
+  }
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(p) + i));
+  const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    if (dtype == DORY_DTYPE_BF16) {
+      out[2 * j] = __uint_as_float(w[j] << 16);
+      out[2 * j + 1] = __uint_as_float(w[j] & 0xffff0000u);
+    } else {
+      out[2 * j] = __half2float(__ushort_as_half(uint16_t(w[j] & 0xffffu)));
+      out[2 * j + 1] = __half2float(__ushort_as_half(uint16_t(w[j] >> 16)));
+    }
+  }
+}
+
+// Sum over the CTA of N doubles; every thread gets the same totals (warps added in order).
+template <int N>
+__device__ __forceinline__ void block_sum(double (&v)[N], double* s_red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
+#pragma unroll
+  for (int n = 0; n < N; ++n)
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v[n] += __shfl_xor_sync(0xffffffffu, v[n], off);
+  __syncthreads();  // the previous sum's readers are done with s_red
+  if (lane == 0)
+#pragma unroll
+    for (int n = 0; n < N; ++n) s_red[warp * N + n] = v[n];
+  __syncthreads();
+#pragma unroll
+  for (int n = 0; n < N; ++n) {
+    double s = 0.0;
+    for (int w = 0; w < nwarps; ++w) s += s_red[w * N + n];
+    v[n] = s;
+  }
+}
+
+template <int G>
+__global__ void __launch_bounds__(G == 1 ? 1024 : 512) residual_kernel(const __grid_constant__ ResidualArgs a) {
+  __shared__ double s_red[32 * 2];
+  // Programmatic dependent launch (no-ops otherwise): inputs are read after the previous
+  // grid; a dependent grid may start at once (it waits for this grid before reading h).
+  grid_dependency_wait();
+  grid_launch_dependents();
+  const int t = blockIdx.x, tid = threadIdx.x, nthr = blockDim.x, W = a.H >> 3;
+  float b[G][8], av[G][8];
+  double sx = 0.0;
+  // this thread's groups: split-K sum in order from zero, the sublayer input
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const int w = tid + g * nthr;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) b[g][j] = av[g][j] = 0.0f;
+    if (w < W) {
+      const int64_t e = int64_t(t) * a.H + 8 * w;
+      for (int k = 0; k < a.split_k; ++k) {
+        const float4* p = reinterpret_cast<const float4*>(a.partials + int64_t(k) * a.T * a.H + e);
+        const float4 u0 = __ldg(p), u1 = __ldg(p + 1);
+        const float u[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) b[g][j] = __fadd_rn(b[g][j], u[j]);
+      }
+      load8(a.a, a.a_dtype, e, av[g]);
+    }
+  }
+  // the GEMV input's sum of squares
+  if (a.x) {
+    const float* x = a.x + int64_t(t) * a.K_IN;
+    if ((a.K_IN & 3) == 0 && (reinterpret_cast<uintptr_t>(a.x) & 15) == 0) {
+      const float4* x4 = reinterpret_cast<const float4*>(x);
+      for (int i = tid; i < (a.K_IN >> 2); i += nthr) {
+        const float4 u = __ldg(x4 + i);
+        sx += double(u.x) * u.x + double(u.y) * u.y + double(u.z) * u.z + double(u.w) * u.w;
+      }
+    } else {
+      for (int i = tid; i < a.K_IN; i += nthr) {
+        const float u = __ldg(x + i);
+        sx += double(u) * u;
+      }
+    }
+  }
+  float r_x = 1.0f;
+  if (a.x) {
+    double v[1] = {sx};
+    block_sum<1>(v, s_red);
+    r_x = inv_norm_from_sum(v[0], a.eps);
+  } else if (a.x_sumsq) {
+    r_x = inv_norm_from_sum(double(__ldg(a.x_sumsq + t)), a.eps);
+  }
+  double s2[2] = {0.0, 0.0};
+#pragma unroll
+  for (int g = 0; g < G; ++g)
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      b[g][j] = __fmul_rn(b[g][j], r_x);
+      s2[0] += double(av[g][j]) * av[g][j];
+      s2[1] += double(b[g][j]) * b[g][j];
+    }
+  block_sum<2>(s2, s_red);
+  const float ra = inv_norm_from_sum(s2[0], a.eps), rb = inv_norm_from_sum(s2[1], a.eps);
+  double sz[1] = {0.0};
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const int w = tid + g * nthr;
+    float al[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) al[j] = 0.0f;
+    if (w < W) load8(a.alpha, a.alpha_dtype, 8 * int64_t(w), al);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float lr = fabsf(__fmul_rn(al[j], a.alpha_scale));
+      const float ya = __fmul_rn(av[g][j], ra), yb = __fmul_rn(b[g][j], rb);
+      const float z = __fadd_rn(ya, __fmul_rn(lr, __fsub_rn(yb, ya)));
+      b[g][j] = z;
+      sz[0] += double(z) * z;
+    }
+  }
+  block_sum<1>(sz, s_red);
+  const float rz = inv_norm_from_sum(sz[0], a.eps);
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const int w = tid + g * nthr;
+    if (w >= W) continue;
+    float hv[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) hv[j] = __fmul_rn(b[g][j], rz);
+    const int64_t e = int64_t(t) * a.H + 8 * w;
+    uint4 packed;
+    packed.x = pack_bf16x2(hv[0], hv[1]);
+    packed.y = pack_bf16x2(hv[2], hv[3]);
+    packed.z = pack_bf16x2(hv[4], hv[5]);
+    packed.w = pack_bf16x2(hv[6], hv[7]);
+    *reinterpret_cast<uint4*>(a.h + e) = packed;
+    float* nm = a.h_nm + int64_t(t) * a.H + w;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) nm[int64_t(j) * W] = hv[j];
+  }
+}
+
+// ------------------------------------------------------------------------------------
 // Host side
 // ------------------------------------------------------------------------------------
 thread_local char g_last_error[512] = "";
@@ -1858,6 +2027,77 @@ int32_t dory_qkvg_epilogue(const DoryQkvgParams* P, void* stream) {
   if (a.head_dim == 64) e = cudaLaunchKernelEx(&cfg, qkvg_epilogue_kernel<64>, k);
   else if (a.head_dim == 128) e = cudaLaunchKernelEx(&cfg, qkvg_epilogue_kernel<128>, k);
   else e = cudaLaunchKernelEx(&cfg, qkvg_epilogue_kernel<256>, k);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(DORY_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
+  return DORY_OK;
+}
+
+int64_t dory_residual_params_bytes(void) { return int64_t(sizeof(DoryResidualParams)); }
+
+int32_t dory_residual_update(const DoryResidualParams* P, void* stream) {
+  if (!P) return fail(DORY_ERR_INVALID_ARGUMENT, "null params");
+  const DoryResidualParams& a = *P;
+  if (a.num_tokens < 0 || a.split_k < 1)
+    return fail(DORY_ERR_INVALID_ARGUMENT, "num_tokens must be >= 0 and split_k >= 1");
+  if (a.hidden < 8 || a.hidden % 8)
+    return fail(DORY_ERR_INVALID_ARGUMENT, "hidden %d is not a positive multiple of 8", a.hidden);
+  if (a.hidden > 16384)
+    return fail(DORY_ERR_UNSUPPORTED, "hidden %d (supported: up to 16384)", a.hidden);
+  if (a.a_dtype < 0 || a.a_dtype > 2 || a.alpha_dtype < 0 || a.alpha_dtype > 2)
+    return fail(DORY_ERR_INVALID_ARGUMENT, "a / alpha dtype");
+  if (a.x && a.x_sumsq) return fail(DORY_ERR_INVALID_ARGUMENT, "give x or x_sumsq, not both");
+  if (a.x && a.x_dim < 1) return fail(DORY_ERR_INVALID_ARGUMENT, "x_dim must be positive");
+  if (a.num_tokens == 0) return DORY_OK;  // nothing is read: empty tensors may be NULL
+  if (!a.partials || !a.a || !a.alpha || !a.h_out || !a.h_out_nibble_major)
+    return fail(DORY_ERR_INVALID_ARGUMENT, "null tensor argument");
+  const void* aligned[] = {a.partials, a.a, a.alpha, a.h_out, a.h_out_nibble_major};
+  for (const void* q : aligned)
+    if (reinterpret_cast<uintptr_t>(q) & 15)
+      return fail(DORY_ERR_ALIGNMENT, "partials, a, alpha and the outputs need 16-byte aligned bases");
+  // The outputs must not overlap the inputs the CTAs of other tokens still read (the
+  // reference's residual_update refuses an h_out aliasing a, dory_common.py:74-75).
+  const int64_t n = int64_t(a.num_tokens) * a.hidden;
+  const int64_t a_bytes = n * (a.a_dtype == DORY_DTYPE_F32 ? 4 : 2);
+  auto overlap = [](const void* p, int64_t pn, const void* q, int64_t qn) {
+    const uintptr_t p0 = reinterpret_cast<uintptr_t>(p), q0 = reinterpret_cast<uintptr_t>(q);
+    return pn > 0 && qn > 0 && p0 < q0 + uint64_t(qn) && q0 < p0 + uint64_t(pn);
+  };
+  if (overlap(a.h_out, n * 2, a.a, a_bytes) || overlap(a.h_out_nibble_major, n * 4, a.a, a_bytes) ||
+      overlap(a.h_out, n * 2, a.partials, n * 4 * a.split_k) ||
+      overlap(a.h_out_nibble_major, n * 4, a.partials, n * 4 * a.split_k))
+    return fail(DORY_ERR_INVALID_ARGUMENT, "the outputs must not alias the sublayer input or the partials");
+  ResidualArgs k;
+  memset(&k, 0, sizeof(k));
+  k.partials = a.partials;
+  k.x = a.x;
+  k.x_sumsq = a.x_sumsq;
+  k.a = a.a;
+  k.alpha = a.alpha;
+  k.h = static_cast<__nv_bfloat16*>(a.h_out);
+  k.h_nm = a.h_out_nibble_major;
+  k.alpha_scale = a.alpha_scale;
+  k.eps = a.eps;
+  k.T = a.num_tokens;
+  k.H = a.hidden;
+  k.K_IN = a.x ? a.x_dim : 0;
+  k.split_k = a.split_k;
+  k.a_dtype = a.a_dtype;
+  k.alpha_dtype = a.alpha_dtype;
+  const int groups = a.hidden / 8;
+  const int G = groups > 1024 ? 4 : 1;
+  const int threads = ((groups + G - 1) / G + 31) / 32 * 32;
+  cudaLaunchConfig_t cfg;
+  memset(&cfg, 0, sizeof(cfg));
+  cfg.gridDim = dim3(a.num_tokens);
+  cfg.blockDim = dim3(threads);
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = (a.flags & DORY_FLAG_OVERLAP_LAUNCH) ? 1 : 0;
+  cudaError_t e = G == 1 ? cudaLaunchKernelEx(&cfg, residual_kernel<1>, k)
+                         : cudaLaunchKernelEx(&cfg, residual_kernel<4>, k);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return fail(DORY_ERR_CUDA, "kernel launch: %s", cudaGetErrorString(e));
   return DORY_OK;

@@ -22,9 +22,22 @@ library, under the reference kernels' own names and launch forms.
   - `_qkvg_epilogue_kernel[(rows // HEAD_DIM, T)](partials, positions, cos_sin, s_gate,
     qk, v, gate, s_gate_factor, Q_ROWS=, KV_ROWS=, HEAD_DIM=, SPLIT_K=, T=, num_warps=4)`.
   Its outputs are the inputs of DecodeAttention.multi_from_raw.
+* The residual update after a sublayer's output GEMV, the consumer of the attention output
+  (kernels/dory_multi_token.py:109-131, `_residual_tokens_kernel`, launched by
+  MultiTokenSublayers._residual after the attention output GEMV and the MLP down GEMV,
+  :173-181; kernels/dory_common.py:55-81, `residual_update`, the single-token form):
+  - `residual_tokens(...)`: b = (sum of the split-K partials) / |x|, h = n(n(a) +
+    |alpha * alpha_scale| * (n(b) - n(a))), stored as BF16 and nibble-major FP32; |x| from
+    x itself or from x_sumsq, the out_sumsq of the attention call, so the attention output
+    is not read again;
+  - `_residual_tokens_kernel[(T,)](partials, x, a, alpha, h_out, h_out_nm, alpha_scale, eps,
+    H=, K_IN=, SPLIT_K=, T=, W_BLOCK=, X_BLOCK=, num_warps=8)`;
+  - `residual_update(a, b, alpha, alpha_scale, h_out, h_out_nibble_major, num_warps=4)`.
 * `route_reference_kernels()`: points the reference modules' own kernel names
-  (dory_attention._qk_norm_cache_kernel, dory_multi_token._qkvg_epilogue_kernel) at these
-  steps, so the reference's sublayers (whose GEMVs are not part of this build) run them.
+  (dory_attention._qk_norm_cache_kernel, dory_multi_token._qkvg_epilogue_kernel,
+  dory_multi_token._residual_tokens_kernel, and residual_update in dory_common,
+  dory_attention and dory_mlp) at these steps, so the reference's sublayers (whose GEMVs
+  are not part of this build) run them.
 
 This module has its own name: putting this directory ahead of the reference's kernels/ on
 sys.path replaces dory_decode_attention only, and the reference's dory_attention and
@@ -38,7 +51,7 @@ import ctypes
 import torch
 
 import _native
-from dory_decode_attention import _SQK_DTYPES
+from dory_decode_attention import _SQK_DTYPES, EPS
 
 
 def _ptr(t) -> int | None:
@@ -209,16 +222,105 @@ class _QkvgEpilogueLaunch:
 _qkvg_epilogue_kernel = _QkvgEpilogueLaunch()
 
 
+def residual_tokens(partials: torch.Tensor, x: torch.Tensor | None, a: torch.Tensor,
+                    alpha: torch.Tensor, alpha_scale: float, eps: float, h_out: torch.Tensor,
+                    h_out_nm: torch.Tensor, x_sumsq: torch.Tensor | None = None,
+                    overlap_launch: bool = False) -> None:
+    """The residual update of T tokens after an output GEMV.  partials FP32 [split_k, T, H]
+    (the GEMV of the unnormalised input), x FP32 [T, K] (the GEMV input, any layout per
+    token) or x_sumsq FP32 [T] (its sum of squares, e.g. DecodeAttention's out_sumsq) or
+    neither (the partials are b already), a [T, H] the sublayer input (BF16 / FP16 / FP32),
+    alpha [H] -> h_out BF16 [T, H] and h_out_nm FP32 [T, 8, H / 8] (nibble-major).
+    h_out / h_out_nm must not alias a or the partials (ValueError).  overlap_launch: launch
+    as a programmatic dependent of the previous kernel.  Enqueued on the current stream."""
+    if partials.dtype != torch.float32 or partials.dim() != 3 or not partials.is_contiguous():
+        raise ValueError("partials must be contiguous float32 [split_k, T, H]")
+    if not partials.is_cuda:
+        raise RuntimeError("residual_tokens runs on CUDA tensors only (no CPU path)")
+    split_k, tokens, hidden = partials.shape
+    if x is not None and x_sumsq is not None:
+        raise ValueError("give x or x_sumsq, not both")
+    if x is not None and (x.dtype != torch.float32 or not x.is_contiguous()
+                          or x.numel() % max(tokens, 1) or x.numel() == 0):
+        raise ValueError("x must be contiguous float32 with the same length for every token")
+    if x_sumsq is not None and (x_sumsq.dtype != torch.float32 or not x_sumsq.is_contiguous()
+                                or x_sumsq.numel() < tokens):
+        raise ValueError("x_sumsq must be contiguous float32 with one entry per token")
+    if a.dtype not in _SQK_DTYPES or not a.is_contiguous() or a.numel() != tokens * hidden:
+        raise ValueError("a must be contiguous [T, H] float32, bfloat16 or float16")
+    if alpha.dtype not in _SQK_DTYPES or not alpha.is_contiguous() or alpha.numel() != hidden:
+        raise ValueError("alpha must be contiguous [H]")
+    if (h_out.dtype != torch.bfloat16 or not h_out.is_contiguous()
+            or h_out.numel() != tokens * hidden):
+        raise ValueError("h_out must be contiguous bfloat16 [T, H]")
+    if (h_out_nm.dtype != torch.float32 or not h_out_nm.is_contiguous()
+            or h_out_nm.numel() != tokens * hidden):
+        raise ValueError("h_out_nm must be contiguous float32 [T, 8, H / 8]")
+    p = _native.DoryResidualParams()
+    p.partials, p.x, p.x_sumsq = partials.data_ptr(), _ptr(x), _ptr(x_sumsq)
+    p.a, p.alpha = a.data_ptr(), alpha.data_ptr()
+    p.h_out, p.h_out_nibble_major = h_out.data_ptr(), h_out_nm.data_ptr()
+    p.alpha_scale, p.eps = float(alpha_scale), float(eps)
+    p.num_tokens, p.hidden, p.split_k = tokens, hidden, split_k
+    p.x_dim = x.numel() // tokens if x is not None and tokens else 0
+    p.a_dtype, p.alpha_dtype = _SQK_DTYPES[a.dtype], _SQK_DTYPES[alpha.dtype]
+    p.flags = _native.FLAG_OVERLAP_LAUNCH if overlap_launch else 0
+    stream = torch.cuda.current_stream(partials.device).cuda_stream
+    _native.check(_native.load().dory_residual_update(ctypes.byref(p), ctypes.c_void_p(stream)))
+
+
+class _ResidualTokensLaunch:
+    """`_residual_tokens_kernel[grid](...)`: the reference Triton kernel's launch form
+    (kernels/dory_multi_token.py:109-113, launched at :177-181).  grid = (T,); partials is
+    viewed as [SPLIT_K, T, H] and x as [T, K_IN]."""
+
+    def __getitem__(self, grid):
+        def launch(partials_ptr, x_ptr, a_ptr, alpha_ptr, h_ptr, h_nibble_major_ptr,
+                   alpha_scale, eps, *, H, K_IN, SPLIT_K, T, W_BLOCK=None, X_BLOCK=None,
+                   num_warps=None, num_stages=None):
+            tokens = grid[0] if isinstance(grid, (tuple, list)) else int(grid)
+            if tokens != T:
+                raise ValueError("grid must be (T,)")
+            residual_tokens(partials_ptr.view(SPLIT_K, T, H), x_ptr.reshape(T, K_IN),
+                            a_ptr.reshape(T, H), alpha_ptr, alpha_scale, eps,
+                            h_ptr.reshape(T, H), h_nibble_major_ptr.reshape(T, 8, H // 8))
+
+        return launch
+
+
+_residual_tokens_kernel = _ResidualTokensLaunch()
+
+
+def residual_update(a: torch.Tensor, b: torch.Tensor, alpha: torch.Tensor, alpha_scale: float,
+                    h_out: torch.Tensor, h_out_nibble_major: torch.Tensor,
+                    num_warps: int = 4) -> None:
+    """a: BF16 [H] sublayer input; b: FP32 [H] sublayer output; alpha: [H] -> h_out BF16
+    [H] and h_out_nibble_major FP32 [8, H / 8] (kernels/dory_common.py:71-81; num_warps is
+    the Triton knob, accepted and unused).  ValueError if h_out aliases a, as there."""
+    if h_out.data_ptr() == a.data_ptr():
+        raise ValueError("output must not alias the sublayer input")
+    hidden = a.numel()
+    residual_tokens(b.reshape(1, 1, hidden), None, a.reshape(1, hidden), alpha, alpha_scale,
+                    EPS, h_out.reshape(1, hidden), h_out_nibble_major.reshape(1, 8, hidden // 8))
+
+
 def route_reference_kernels() -> list[str]:
     """Points the reference's module-level kernels at this build's steps: the reference's
     dory_attention._qk_norm_cache_kernel (launched by FusedAttentionSublayer.pre_attention
-    and pre_attention_qkv) and dory_multi_token._qkvg_epilogue_kernel (launched by
-    MultiTokenSublayers.attention).  The reference's kernels/ must be importable (after this
+    and pre_attention_qkv), dory_multi_token._qkvg_epilogue_kernel and
+    _residual_tokens_kernel (launched by MultiTokenSublayers.attention / _residual), and
+    residual_update where dory_common defines it and dory_attention / dory_mlp import it
+    (the unfused residual of FusedAttentionSublayer / FusedMlpSublayer).  The reference's kernels/ must be importable (after this
     directory on sys.path).  Returns the names it replaced."""
     import importlib
     routed = []
     for module, name, step in (("dory_attention", "_qk_norm_cache_kernel", _qk_norm_cache_kernel),
-                               ("dory_multi_token", "_qkvg_epilogue_kernel", _qkvg_epilogue_kernel)):
+                               ("dory_multi_token", "_qkvg_epilogue_kernel", _qkvg_epilogue_kernel),
+                               ("dory_multi_token", "_residual_tokens_kernel",
+                                _residual_tokens_kernel),
+                               ("dory_common", "residual_update", residual_update),
+                               ("dory_attention", "residual_update", residual_update),
+                               ("dory_mlp", "residual_update", residual_update)):
         mod = importlib.import_module(module)
         if not hasattr(mod, name):
             raise ImportError(f"{module} has no {name}: is it the reference's module?")
@@ -228,4 +330,5 @@ def route_reference_kernels() -> list[str]:
 
 
 __all__ = ["qk_norm_cache", "_qk_norm_cache_kernel", "qkvg_epilogue", "_qkvg_epilogue_kernel",
+           "residual_tokens", "_residual_tokens_kernel", "residual_update",
            "route_reference_kernels"]

@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define DORY_DECODE_ABI_VERSION 4
+#define DORY_DECODE_ABI_VERSION 5
 
 /* Status codes returned by every entry point. */
 typedef enum DoryStatus {
@@ -261,6 +261,49 @@ int64_t dory_qkvg_params_bytes(void);
 
 /* One launch of the epilogue on `stream`. */
 int32_t dory_qkvg_epilogue(const DoryQkvgParams* params, void* stream);
+
+/*
+ * The residual update after a sublayer's output GEMV, the consumer of the attention output:
+ * the reference's _residual_tokens_kernel (kernels/dory_multi_token.py:109-131), which
+ * MultiTokenSublayers._residual launches after the attention output GEMV and after the MLP
+ * down GEMV (:173-181, :210, :225), and residual_update (kernels/dory_common.py:55-81), the
+ * single-token form with b given.  For each of T tokens:
+ *
+ *   b = (0 + partials[0] + ... + partials[split_k - 1]) * r_x
+ *   r_x = 1 / sqrt(sum x^2 + eps)   from x, from x_sumsq, or 1 when both are NULL
+ *   h = n(n(a) + |alpha * alpha_scale| * (n(b) - n(a))),   n(y) = y / sqrt(sum y^2 + eps)
+ *
+ * and h is stored as BF16 in natural order and as FP32 nibble-major (h_nm[t][j][w] =
+ * h[t][8w + j]), the next sublayer's GEMV input.  x_sumsq is the out_sumsq an attention
+ * call (dory_decode_attention) produced, so the attention output is not read a second time.
+ * The outputs must not overlap a or the partials.
+ */
+typedef struct DoryResidualParams {
+  const float* partials;          /* FP32 [split_k, T, H], 16-byte aligned                   */
+  const float* x;                 /* optional FP32 [T, x_dim]: the GEMV's input              */
+  const float* x_sumsq;           /* optional FP32 [T]: sum of x^2 given directly            */
+  const void* a;                  /* [T, H] of a_dtype: the sublayer input, 16-byte aligned  */
+  const void* alpha;              /* [H] of alpha_dtype, 16-byte aligned                     */
+  void* h_out;                    /* BF16 [T, H], 16-byte aligned                            */
+  float* h_out_nibble_major;      /* FP32 [T, 8, H / 8], 16-byte aligned                     */
+  float alpha_scale;
+  float eps;
+  int32_t num_tokens;
+  int32_t hidden;                 /* H: a multiple of 8, at most 16384                       */
+  int32_t x_dim;                  /* K: elements of x per token                              */
+  int32_t split_k;
+  int32_t a_dtype;                /* DoryDType */
+  int32_t alpha_dtype;            /* DoryDType */
+  uint32_t flags;                 /* DORY_FLAG_OVERLAP_LAUNCH: launch as a programmatic
+                                   * dependent of the previous kernel on the stream (inputs
+                                   * are read after it completes) */
+} DoryResidualParams;
+
+/* sizeof(DoryResidualParams) as compiled into the library. */
+int64_t dory_residual_params_bytes(void);
+
+/* One launch of the residual update on `stream` (one CTA per token). */
+int32_t dory_residual_update(const DoryResidualParams* params, void* stream);
 
 /* Copies the device error word (DORY_DEVERR_* bits) to *flags_out, synchronising `stream`;
  * clears it when `clear` is non-zero.  The only entry point that waits on the device. */

@@ -21,6 +21,9 @@ chrisbennight/dory-vllm-experiments:
   kernels/w4a16_gemv.py:91-93);
 * the multi-token path's q/k/v/gate epilogue (kernels/dory_multi_token.py:53-80): split-K
   sum, rotary embedding on adjacent row pairs, the scaled sigmoid output gate;
+* the residual update after the output GEMV (kernels/dory_multi_token.py:109-131,
+  kernels/dory_common.py:55-81): the split-K sum over the input's norm (or over a given
+  sum of squares), h = n(n(a) + |alpha * alpha_scale| * (n(b) - n(a)));
 * multi-token calls (:270-305): token t uses cache_offsets[t] and block_table_offsets[t];
   shared_cache=True caches every token's k/v before any attention (:294-301), which the
   reference's own test checks against single-token calls in position order
@@ -301,6 +304,58 @@ def qkvg_epilogue(partials: torch.Tensor, positions, cos_sin: torch.Tensor,
     z = ((y[:, Q + 2 * KV:] * s).astype(np.float32) * s).astype(np.float32)
     gate = torch.sigmoid(torch.from_numpy(z)).numpy()
     return torch.from_numpy(qk.copy()), torch.from_numpy(v.copy()), torch.from_numpy(gate)
+
+
+# ---------------------------------------------------------------------------------------
+# the residual update after a sublayer's output GEMV (dory_multi_token.py:109-131,
+# _residual_tokens_kernel; dory_common.py:55-81, residual_update): the consumer of the
+# attention output and of its squared norm
+# ---------------------------------------------------------------------------------------
+
+def _inv_norm_of_sum(s32: np.ndarray, eps: float) -> np.ndarray:
+    """Correctly rounded FP32 1/sqrt(s + eps) of FP32 sums s (eps added in FP32)."""
+    t = (np.asarray(s32, dtype=np.float32) + np.float32(eps)).astype(np.float32)
+    return (1.0 / np.sqrt(t.astype(np.float64))).astype(np.float32)
+
+
+def residual_tokens(partials, x, x_sumsq, a, alpha, alpha_scale: float, eps: float = EPS):
+    """Split-K partials FP32 [split_k, T, H] of the output GEMV W x (x unnormalised), the
+    GEMV input x FP32 [T, K] or its sum of squares x_sumsq FP32 [T] (or neither: the
+    partials are already b, as residual_update's b), the sublayer input a [T, H] and the
+    per-dimension alpha [H] -> (h FP32 [T, H], h BF16 [T, H], h nibble-major FP32 [T, 8, H / 8]).
+
+    b = (0 + p_0 + ... + p_{k-1}) * r_x in split order (:121-124), r_x = 1/sqrt(sum x^2 + eps)
+    (:118-119); lr = |alpha * alpha_scale| (:126); h = n(n(a) + lr * (n(b) - n(a))) (:127-130)
+    with n(y) = y * 1/sqrt(sum y^2 + eps).  Sums of squares in FP64, rounded once to FP32,
+    inverse square roots correctly rounded, every product and sum rounded on its own (no
+    fused multiply-add); h is stored as BF16 (round to nearest even) and as FP32 in the
+    nibble-major order out[j][w] = h[8w + j] (dory_common.py:46-52)."""
+    p = np.asarray(partials, dtype=np.float32)
+    split_k, T, H = p.shape
+    if H % 8:
+        raise ValueError("hidden size must be a multiple of 8")
+    if x is not None and x_sumsq is not None:
+        raise ValueError("give x or x_sumsq, not both")
+    y = np.zeros((T, H), dtype=np.float32)
+    for k in range(split_k):
+        y = (y + p[k]).astype(np.float32)
+    if x is not None:
+        xs = np.asarray(x, dtype=np.float32).reshape(T, -1)
+        r_x = inv_norm(xs, eps)
+    elif x_sumsq is not None:
+        r_x = _inv_norm_of_sum(np.asarray(x_sumsq, dtype=np.float32).reshape(T), eps)
+    else:
+        r_x = np.ones(T, dtype=np.float32)
+    b = (y * r_x[:, None]).astype(np.float32)
+    av = np.asarray(a.float() if isinstance(a, torch.Tensor) else a, dtype=np.float32).reshape(T, H)
+    al = np.asarray(alpha.float() if isinstance(alpha, torch.Tensor) else alpha,
+                    dtype=np.float32).reshape(H)
+    lr = np.abs((al * np.float32(alpha_scale)).astype(np.float32))
+    ya, yb = normalize(av, eps), normalize(b, eps)
+    z = (ya + (lr * (yb - ya).astype(np.float32)).astype(np.float32)).astype(np.float32)
+    h = normalize(z, eps)
+    h_t = torch.from_numpy(h.copy())
+    return h_t, h_t.to(torch.bfloat16), h_t.reshape(T, H // 8, 8).transpose(1, 2).contiguous()
 
 
 def relative_error(x: torch.Tensor, reference: torch.Tensor) -> float:

@@ -7,6 +7,8 @@
  *   - a known answer: a non-raw call (DecodeAttention.__call__) over a paged BF16 cache whose
  *     value rows are all 1.0 returns the gate itself (the softmax weights sum to one), for any
  *     keys, block table and split count; a padding request (seq_len 0) returns 0;
+ *   - a known answer of the residual update: a sublayer input and a GEMV output that are both
+ *     constant vectors give h = 1 / sqrt(H) everywhere (2^-4 for H = 256, exact in BF16);
  *   - the device error word stays clear.
  *
  * Build and run (tests/test_c_abi.py does this):
@@ -69,6 +71,8 @@ int main(void) {
   CHECK(dory_decode_params_bytes() == (int64_t)sizeof(DoryDecodeParams), "DoryDecodeParams size");
   CHECK(dory_qk_norm_params_bytes() == (int64_t)sizeof(DoryQkNormParams), "DoryQkNormParams size");
   CHECK(dory_qkvg_params_bytes() == (int64_t)sizeof(DoryQkvgParams), "DoryQkvgParams size");
+  CHECK(dory_residual_params_bytes() == (int64_t)sizeof(DoryResidualParams),
+        "DoryResidualParams size");
 
   /* ---- argument errors: statuses and reasons, nothing launched ---- */
   CHECK(dory_decode_attention(NULL, NULL) == DORY_ERR_INVALID_ARGUMENT, "null params");
@@ -80,6 +84,12 @@ int main(void) {
   CHECK(dory_decode_attention(&bad, NULL) == DORY_ERR_INVALID_ARGUMENT,
         "heads not a multiple of kv_heads");
   CHECK(dory_decode_scratch_bytes(1, SPLITS, NH, NKV, HD) > 0, "scratch size");
+  DoryResidualParams rbad;
+  memset(&rbad, 0, sizeof(rbad));
+  rbad.num_tokens = 1;
+  rbad.hidden = 12; /* not a multiple of 8 */
+  rbad.split_k = 1;
+  CHECK(dory_residual_update(&rbad, NULL) == DORY_ERR_INVALID_ARGUMENT, "hidden 12");
 
   cudaStream_t s;
   CUDA(cudaStreamCreate(&s));
@@ -181,6 +191,61 @@ int main(void) {
   uint32_t flags = 1;
   CHECK(dory_decode_fetch_errors(d_scratch, &flags, 1, (void*)s) == DORY_OK, "fetch errors");
   CHECK(flags == 0, "device error word %u", flags);
+
+  /* ---- residual update: constant a (2^-4 in BF16, unit norm at H = 256) and constant
+   *      GEMV partials 1.5 + 0.5 over x = sixteen ones give h = 2^-4 ---- */
+  enum { RH = 256, RT = 2, RK = 16 };
+  float parts[2 * RT * RH], xs[RT * RK], alpha[RH], h_nm[RT * RH];
+  uint16_t a_rows[RT * RH], h_rows[RT * RH];
+  for (int i = 0; i < RT * RH; ++i) {
+    parts[i] = 1.5f;
+    parts[RT * RH + i] = 0.5f;
+    a_rows[i] = bf16(0.0625f);
+  }
+  for (int i = 0; i < RT * RK; ++i) xs[i] = 1.0f;
+  for (int i = 0; i < RH; ++i) alpha[i] = 0.01f * (float)(i % 7);
+  void *d_parts, *d_x, *d_a, *d_alpha, *d_h, *d_hnm;
+  CUDA(cudaMalloc(&d_parts, sizeof(parts)));
+  CUDA(cudaMalloc(&d_x, sizeof(xs)));
+  CUDA(cudaMalloc(&d_a, sizeof(a_rows)));
+  CUDA(cudaMalloc(&d_alpha, sizeof(alpha)));
+  CUDA(cudaMalloc(&d_h, sizeof(h_rows)));
+  CUDA(cudaMalloc(&d_hnm, sizeof(h_nm)));
+  CUDA(cudaMemcpy(d_parts, parts, sizeof(parts), cudaMemcpyHostToDevice));
+  CUDA(cudaMemcpy(d_x, xs, sizeof(xs), cudaMemcpyHostToDevice));
+  CUDA(cudaMemcpy(d_a, a_rows, sizeof(a_rows), cudaMemcpyHostToDevice));
+  CUDA(cudaMemcpy(d_alpha, alpha, sizeof(alpha), cudaMemcpyHostToDevice));
+  DoryResidualParams r;
+  memset(&r, 0, sizeof(r));
+  r.partials = (const float*)d_parts;
+  r.x = (const float*)d_x;
+  r.a = d_a;
+  r.alpha = d_alpha;
+  r.h_out = d_h;
+  r.h_out_nibble_major = (float*)d_hnm;
+  r.alpha_scale = 2.5f;
+  r.eps = 1e-6f;
+  r.num_tokens = RT;
+  r.hidden = RH;
+  r.x_dim = RK;
+  r.split_k = 2;
+  r.a_dtype = DORY_DTYPE_BF16;
+  r.alpha_dtype = DORY_DTYPE_F32;
+  const int32_t rs = dory_residual_update(&r, (void*)s);
+  CHECK(rs == DORY_OK, "dory_residual_update: %d (%s)", rs, dory_decode_last_error());
+  CUDA(cudaStreamSynchronize(s));
+  CUDA(cudaMemcpy(h_rows, d_h, sizeof(h_rows), cudaMemcpyDeviceToHost));
+  CUDA(cudaMemcpy(h_nm, d_hnm, sizeof(h_nm), cudaMemcpyDeviceToHost));
+  for (int i = 0; i < RT * RH; ++i) {
+    CHECK(h_rows[i] == bf16(0.0625f), "residual h[%d] bits %04x", i, (unsigned)h_rows[i]);
+    CHECK(fabs((double)h_nm[i] - 0.0625) < 1e-7, "residual h_nm[%d] = %.9g", i, h_nm[i]);
+  }
+  cudaFree(d_parts);
+  cudaFree(d_x);
+  cudaFree(d_a);
+  cudaFree(d_alpha);
+  cudaFree(d_h);
+  cudaFree(d_hnm);
 
   free(key);
   free(value);

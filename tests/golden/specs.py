@@ -95,3 +95,54 @@ def qkvg_digest(case: QkvgCase) -> str:
     for t in (case.partials, case.positions, case.cos_sin.float(), case.s_gate.float()):
         h.update(t.contiguous().numpy().tobytes())
     return h.hexdigest()
+
+
+class ResidualCase:
+    """Seeded inputs of the residual update: split-K partials FP32 [split_k, T, H] of the
+    output GEMV, its input x FP32 [T, K] (None: the partials are b itself, residual_update),
+    the sublayer input a [T, H] (unit rows, as the hidden state is) and alpha [H]."""
+
+    def __init__(self, seed: int, tokens: int, hidden: int, x_dim: int | None, split_k: int,
+                 dtype=torch.bfloat16, alpha_scale: float = 2.5):
+        g = torch.Generator().manual_seed(seed)
+        self.partials = torch.randn(split_k, tokens, hidden, generator=g) * 3.0
+        self.x = None if x_dim is None else torch.randn(tokens, x_dim, generator=g)
+        a = torch.randn(tokens, hidden, generator=g)
+        self.a = (a / a.norm(dim=1, keepdim=True)).to(dtype)
+        self.alpha = (torch.randn(hidden, generator=g) * 0.02).to(dtype)
+        self.alpha_scale = alpha_scale
+
+    @property
+    def tokens(self) -> int:
+        return self.partials.shape[1]
+
+    @property
+    def hidden(self) -> int:
+        return self.partials.shape[2]
+
+
+def residual_specs() -> dict:
+    """name -> zero-argument builder of a ResidualCase.  The Dory shapes: hidden 2560, the
+    attention output GEMV over 4096 inputs and the MLP down GEMV over 7168, both split-K 4
+    (kernels/dory_multi_token.py:43-45), four wavefront rows."""
+    return {
+        "residual_attn_dory": lambda: ResidualCase(51, 4, 2560, 4096, 4),
+        "residual_mlp_dory": lambda: ResidualCase(52, 2, 2560, 7168, 4),
+        # 37 groups of 8 (not a warp multiple), an input length not a multiple of 4, FP32 a
+        "residual_ragged_f32": lambda: ResidualCase(53, 3, 296, 101, 3, dtype=torch.float32),
+        # hidden 12288: two groups of 8 per thread
+        "residual_wide": lambda: ResidualCase(54, 1, 12288, 4096, 2),
+        # residual_update (kernels/dory_common.py:55-81): one token, b given
+        "residual_update_dory": lambda: ResidualCase(55, 1, 2560, None, 1),
+    }
+
+
+def residual_digest(case: ResidualCase) -> str:
+    h = hashlib.sha256()
+    parts = [case.partials, case.a.float(), case.alpha.float()]
+    if case.x is not None:
+        parts.append(case.x)
+    for t in parts:
+        h.update(t.contiguous().numpy().tobytes())
+    h.update(repr(case.alpha_scale).encode())
+    return h.hexdigest()
