@@ -168,14 +168,32 @@ WORKLOADS = ("config5", "config1", "config2", "config3", "config4",
 
 def tuned_splits(workload: str, world: int):
     """(splits, min_blocks_per_split) measured fastest on B200 for each workload; config 5
-    uses 4 splits once its 512 sequences are partitioned over 2+ GPUs, and 8 splits of at
-    least 96 blocks at 8+ GPUs (fewer, longer sequences per GPU: finer splits of the long
-    ones even out the last wave; measured on one GPU's share of each partition)."""
+    uses 4 splits once its 512 sequences are partitioned over 2+ GPUs, and 3 splits at 8+
+    GPUs, where each GPU's sequences run longest-first (`longest_first`; measured on one
+    GPU's share of each partition)."""
     if workload == "config5":
-        return (2, 64) if world == 1 else (4, 64) if world < 8 else (8, 96)
+        return (2, 64) if world == 1 else (4, 64) if world < 8 else (3, 64)
     return {"config1": (16, 1), "config2": (16, 1), "config3": (2, 32),
             "config4": (32, 1), "dory640": (16, 1), "dory2048": (32, 1),
             "dory8192": (32, 1)}.get(workload, (2, 64))
+
+
+def longest_first(workload: str, world: int) -> bool:
+    """Whether a GPU's share of the request partition is launched longest sequence first.
+    With 64 config-5 sequences per GPU (8 GPUs) the longest ones' splits then start in the
+    first wave and the short ones fill the tail: 85.1 us per layer with 3 splits against
+    90.9 us for the best setting in request order (8 splits of at least 96 blocks), one GPU
+    running rank 0's share.  With 128 or more sequences per GPU it measured slower (2 GPUs:
+    340 against 324 us; 4 GPUs: 172 against 168 us; 1 GPU: 5%), so request order stays."""
+    return workload == "config5" and world >= 8
+
+
+def rank_sequences(workload: str, lens_all: list, world: int, rank: int) -> list:
+    """This rank's sequence indices of the request partition, in launch order."""
+    mine = W.partition(lens_all, world)[rank]
+    if longest_first(workload, world):
+        mine = sorted(mine, key=lambda i: (-lens_all[i], i))
+    return mine
 
 
 @dataclass
@@ -489,7 +507,7 @@ def bench_ours(args, world, rank, local):
         mine = list(range(len(lens_all)))  # a single sequence does not shard: replicas
         scaling = "replicas"
     else:
-        mine = W.partition(lens_all, world)[rank]
+        mine = rank_sequences(args.workload, lens_all, world, rank)
         scaling = "strong"
     lens = [lens_all[i] for i in mine]
     wl = DeviceWorkload(spec, lens, dev, spec.seed + 1000 * rank)

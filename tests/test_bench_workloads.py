@@ -89,3 +89,23 @@ def test_cpu_sample_weights_windows():
     for c, _, _, _ in sample.cases:
         assert (c.num_heads, c.num_kv_heads, c.head_dim) == (16, 4, 256)
     assert sample.once() > 0
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_rank_sequences_cover_the_partition(world):
+    """Each rank launches exactly its partition share; at 8+ GPUs config 5's shares run
+    longest first, below that in request order."""
+    lens = bench.workload_spec("config5").lens
+    seen = []
+    for rank in range(world):
+        mine = bench.rank_sequences("config5", lens, world, rank)
+        assert sorted(mine) == W.partition(lens, world)[rank]
+        ctx = [lens[i] for i in mine]
+        if world >= 8:
+            assert ctx == sorted(ctx, reverse=True)
+        else:
+            assert mine == sorted(mine)
+        seen += mine
+    assert sorted(seen) == list(range(len(lens)))
+    assert bench.tuned_splits("config5", world) == {1: (2, 64), 2: (4, 64), 4: (4, 64),
+                                                     8: (3, 64)}[world]
