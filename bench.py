@@ -255,12 +255,13 @@ def workload_spec(name: str) -> Spec:
 
 
 def algorithmic_bytes(seq_lens, shared: bool, window: int, nh: int, nkv: int, hd: int,
-                      split_k: int = 0) -> int:
+                      split_k: int = 0, residual_hidden: int = 0) -> int:
     """Bytes one launch must move: unique attended positions x the K/V row bytes (the new
     rows written, the rest read) + per-token q/k/v/gate reads and out writes (FP32) + sqk
     + the block-table entries of the attended range + seq_lens.  With a sliding window w a
     token attends [max(seq_len - w, 0), seq_len); a shared-cache group reads the union of
-    its tokens' ranges once."""
+    its tokens' ranges once.  split_k: the q/k/v/gate epilogue's I/O replaces the q/k/v/gate
+    reads; residual_hidden: the residual update's I/O is added (the sublayer chain)."""
     kv_row = nkv * hd * 2 * 2
     token_io = ((nh + nkv) * hd + nkv * hd + 2 * nh * hd) * 4
     extra = 0
@@ -269,6 +270,12 @@ def algorithmic_bytes(seq_lens, shared: bool, window: int, nh: int, nkv: int, hd
         # position and bf16 cos/sin row; the bf16 gate scales once per launch
         token_io = (split_k * 2 * (nh + nkv) * hd + nh * hd) * 4 + 8 + hd * 2
         extra = nh * hd * 2
+    if residual_hidden:
+        # the output GEMV's split-K partials, the sublayer input (bf16), h as bf16 and as
+        # nibble-major FP32, the output statistic written and read; alpha (bf16) once
+        H = residual_hidden
+        token_io += RESIDUAL_SPLIT_K * H * 4 + H * 2 + H * 2 + H * 4 + 8
+        extra += H * 2
 
     def span(n):
         return (max(n - window, 0) if window > 0 else 0), n
@@ -365,7 +372,8 @@ class DeviceWorkload:
     def algorithmic_bytes_per_application(self, layer: int = 0) -> int:
         return algorithmic_bytes(self.seq_lens_list, self.shared, self.window(layer),
                                  self.nh, self.nkv, self.hd,
-                                 QKVG_SPLIT_K if self.path == "qkvg" else 0)
+                                 QKVG_SPLIT_K if self.path in ("qkvg", "sublayer") else 0,
+                                 self.hidden if self.path == "sublayer" else 0)
 
     def algorithmic_bytes_per_step(self) -> int:
         return sum(self.algorithmic_bytes_per_application(layer) for layer in self.layers)
@@ -394,7 +402,8 @@ def prepare_call_path(wl: DeviceWorkload):
     wl.path = "call"
 
 
-QKVG_SPLIT_K = 2  # the reference's q/k/v/gate GEMV configuration (dory_multi_token.py:44)
+QKVG_SPLIT_K = 2  # the reference's q/k/v/gate GEMV configuration (dory_multi_token.py:41)
+RESIDUAL_SPLIT_K = 4  # its attention output GEMV configuration (dory_multi_token.py:42)
 
 
 def prepare_qkvg_path(wl: DeviceWorkload):
@@ -416,11 +425,36 @@ def prepare_qkvg_path(wl: DeviceWorkload):
     wl.path = "qkvg"
 
 
+def prepare_sublayer_path(wl: DeviceWorkload):
+    """`--path sublayer`: the non-GEMM steps of the multi-token attention sublayer
+    (MultiTokenSublayers.attention, dory_multi_token.py:183-210): the q/k/v/gate epilogue,
+    multi_from_raw with the output statistic, then the residual update after the output
+    GEMV (`_residual_tokens_kernel`, :109-131) fed that statistic instead of the output.
+    Each layer's inputs are both GEMVs' split-K partials (the GEMVs themselves, NVFP4, are
+    not part of this build).  Hidden size 2560 (the Dory model) for 256-dim heads, else
+    heads x head_dim."""
+    prepare_qkvg_path(wl)
+    T, L = wl.tokens, wl.num_layers
+    wl.hidden = H = 2560 if wl.hd == 256 else wl.nh * wl.hd
+    gd = torch.Generator(device=wl.dev).manual_seed(78)
+    wl.o_partials = torch.randn(L, RESIDUAL_SPLIT_K, T, H, device=wl.dev, generator=gd)
+    a = torch.randn(T, H, device=wl.dev, generator=gd)
+    wl.h_in = (a / a.norm(dim=1, keepdim=True)).to(torch.bfloat16)
+    wl.alpha = (torch.randn(H, device=wl.dev, generator=gd) * 0.02).to(torch.bfloat16)
+    wl.h_out = torch.empty(T, H, dtype=torch.bfloat16, device=wl.dev)
+    wl.h_out_nm = torch.empty(T, 8, H // 8, device=wl.dev)
+    if wl.sumsq is None:
+        wl.sumsq = torch.zeros(L, T, device=wl.dev)
+    wl.path = "sublayer"
+
+
 def step_inputs(wl: DeviceWorkload):
     """The per-layer input tensors ([layers, T, ...]) the workload's path reads."""
     if wl.path == "call":
         return (wl.q_call, wl.gate)
-    if wl.path.startswith("qkvg"):
+    if wl.path == "sublayer":
+        return (wl.partials, wl.o_partials)
+    if wl.path == "qkvg":
         return (wl.partials,)
     return (wl.qk, wl.v, wl.gate)
 
@@ -436,14 +470,17 @@ def layer_call(attn, wl: DeviceWorkload, app: int, layer: int, ins, out):
         attn(q[0], key, value, wl.tables[0], wl.seq_lens[0:1], window, scale, gate[0], out[0],
              out_sumsq=sumsq)
         return
-    if wl.path == "qkvg":
-        from dory_sublayer_steps import qkvg_epilogue
+    if wl.path in ("qkvg", "sublayer"):
+        from dory_sublayer_steps import qkvg_epilogue, residual_tokens
         qk_b, v_b, gate_b = wl.qkvg_bufs
         qkvg_epilogue(ins[0], wl.positions, wl.cos_sin, wl.s_gate, 0.9, qk_b, v_b, gate_b,
                       wl.nh, wl.nkv, wl.hd, overlap_launch=attn.overlap_launch)
         attn.multi_from_raw(qk_b, v_b, wl.sqk, W.SQK_FACTOR, EPS, wl.cache_offsets, key, value,
                             wl.tables, wl.table_offsets, wl.seq_lens, window, scale, gate_b, out,
                             shared_cache=wl.shared, out_sumsq=sumsq)
+        if wl.path == "sublayer":
+            residual_tokens(ins[1], None, wl.h_in, wl.alpha, 2.5, EPS, wl.h_out, wl.h_out_nm,
+                            x_sumsq=sumsq, overlap_launch=attn.overlap_launch)
         return
     qk, v, gate = ins
     if wl.path == "separate":
@@ -522,6 +559,8 @@ def bench_ours(args, world, rank, local):
         prepare_call_path(wl)
     elif args.path == "qkvg":
         prepare_qkvg_path(wl)
+    elif args.path == "sublayer":
+        prepare_sublayer_path(wl)
     attn = make_attention(wl, args)
     apps = len(layers)
 
@@ -602,7 +641,7 @@ def bench_ours(args, world, rank, local):
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": args.steps * apps * (2 if wl.path in ("separate", "qkvg") else 1),
+        "gpu_launches": args.steps * apps * {"separate": 2, "qkvg": 2, "sublayer": 3}.get(wl.path, 1),
         "clocks": clocks.summary(),
     }
     if rank == 0:
@@ -864,10 +903,12 @@ def main() -> int:
     ap.add_argument("--min-blocks-per-split", type=int, default=None)
     ap.add_argument("--overlap-launch", action="store_true",
                     help="launch each layer call as a programmatic dependent of the previous one")
-    ap.add_argument("--path", choices=("fused", "separate", "call", "qkvg"),
+    ap.add_argument("--path", choices=("fused", "separate", "call", "qkvg", "sublayer"),
                     default="fused",
                     help="qkvg: the multi-token q/k/v/gate epilogue kernel on the GEMV's "
-                         "split-K partials, then multi_from_raw; "
+                         "split-K partials, then multi_from_raw; sublayer: qkvg, then the "
+                         "residual update on the output GEMV's partials, fed the attention "
+                         "output's sum of squares; "
                          "call: the non-raw __call__ alone (q normalised and its k/v cached "
                          "beforehand); separate: the q/k normalisation kernel then the "
                          "non-raw call "

@@ -124,7 +124,7 @@ class ResidualCase:
 def residual_specs() -> dict:
     """name -> zero-argument builder of a ResidualCase.  The Dory shapes: hidden 2560, the
     attention output GEMV over 4096 inputs and the MLP down GEMV over 7168, both split-K 4
-    (kernels/dory_multi_token.py:43-45), four wavefront rows."""
+    (kernels/dory_multi_token.py:42, 44), four wavefront rows."""
     return {
         "residual_attn_dory": lambda: ResidualCase(51, 4, 2560, 4096, 4),
         "residual_mlp_dory": lambda: ResidualCase(52, 2, 2560, 7168, 4),

@@ -109,3 +109,13 @@ def test_rank_sequences_cover_the_partition(world):
     assert sorted(seen) == list(range(len(lens)))
     assert bench.tuned_splits("config5", world) == {1: (2, 64), 2: (4, 64), 4: (4, 64),
                                                      8: (3, 64)}[world]
+
+
+def test_sublayer_bytes_add_the_residual_io():
+    """--path sublayer adds, per token, the output GEMV's partials, the sublayer input, h in
+    both layouts and the output statistic written and read; alpha once per launch."""
+    H, lens = 2560, [100, 2000, 7]
+    base = bench.algorithmic_bytes(lens, False, 1024, 16, 4, 256, bench.QKVG_SPLIT_K)
+    sub = bench.algorithmic_bytes(lens, False, 1024, 16, 4, 256, bench.QKVG_SPLIT_K, H)
+    per_token = bench.RESIDUAL_SPLIT_K * H * 4 + H * 2 + H * 2 + H * 4 + 8
+    assert sub - base == len(lens) * per_token + H * 2
