@@ -241,7 +241,7 @@ def residual_tokens(partials: torch.Tensor, x: torch.Tensor | None, a: torch.Ten
     if x is not None and x_sumsq is not None:
         raise ValueError("give x or x_sumsq, not both")
     if x is not None and (x.dtype != torch.float32 or not x.is_contiguous()
-                          or x.numel() % max(tokens, 1) or x.numel() == 0):
+                          or (tokens and (x.numel() % tokens or x.numel() == 0))):
         raise ValueError("x must be contiguous float32 with the same length for every token")
     if x_sumsq is not None and (x_sumsq.dtype != torch.float32 or not x_sumsq.is_contiguous()
                                 or x_sumsq.numel() < tokens):
