@@ -78,3 +78,30 @@ def test_rejects_bad_arguments():
     with pytest.raises(ValueError):
         O.residual_tokens(torch.zeros(1, 1, 12), None, None, torch.zeros(1, 12), torch.zeros(12),
                           1.0)
+
+
+@pytest.mark.parametrize("seed,hidden", [(60, 64), (61, 2560), (62, 16384)])
+def test_properties(seed, hidden):
+    """Size-independent properties of h = n(n(a) + lr (n(b) - n(a))): unit rows; the
+    partials and x enter only through b / |b|, so scaling the partials or x by a positive
+    factor leaves h unchanged up to rounding while sum b^2 stays far above eps; lr = 0
+    gives h = n(n(a)) and b parallel to a gives h = n(a)."""
+    g = torch.Generator().manual_seed(seed)
+    T = 3
+    parts = torch.randn(2, T, hidden, generator=g)
+    x = torch.randn(T, 300, generator=g)
+    a = torch.randn(T, hidden, generator=g)
+    a = (a / a.norm(dim=1, keepdim=True)).to(torch.bfloat16)
+    alpha = (torch.randn(hidden, generator=g) * 0.05).to(torch.bfloat16)
+    h, _, _ = O.residual_tokens(parts, x, None, a, alpha, 2.5)
+    np.testing.assert_allclose(h.double().norm(dim=1).numpy(), 1.0, atol=1e-6)
+    # scalings that keep sum b^2 far above eps (below it, eps breaks the invariance)
+    for scaled in ((parts * 3.7, x), (parts, x * 0.01), (parts * 2.0, x * 0.5)):
+        h2, _, _ = O.residual_tokens(scaled[0], scaled[1], None, a, alpha, 2.5)
+        np.testing.assert_allclose(h2.numpy(), h.numpy(), atol=2e-7, rtol=0)
+    h0, _, _ = O.residual_tokens(parts, x, None, a, torch.zeros(hidden), 2.5)
+    na = O.normalize(O.normalize(a.float().numpy()))
+    np.testing.assert_allclose(h0.numpy(), na, atol=1e-7, rtol=0)
+    par = a.float()[None] * 0.5  # b = 0.5 a (one split), no x: n(b) = n(a)
+    hp, _, _ = O.residual_tokens(par, None, None, a, alpha, 2.5)
+    np.testing.assert_allclose(hp.numpy(), O.normalize(a.float().numpy()), atol=1e-7, rtol=0)
