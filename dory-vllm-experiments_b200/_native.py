@@ -155,6 +155,15 @@ def load(path: os.PathLike | None = None) -> ctypes.CDLL:
     return lib
 
 
+def check_devices(device, *tensors) -> None:
+    """ValueError unless every given tensor (None skipped) is on `device`, a CUDA device:
+    the kernels dereference the raw pointers, so a host tensor or one on another GPU must
+    be refused before the launch."""
+    for t in tensors:
+        if t is not None and t.device != device:
+            raise ValueError(f"a tensor argument is on {t.device}; this call runs on {device}")
+
+
 def check(status: int) -> None:
     """Maps a DoryStatus to the reference's exception types (ValueError for bad arguments)."""
     if status == OK:

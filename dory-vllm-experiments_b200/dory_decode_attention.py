@@ -180,6 +180,12 @@ class DecodeAttention:
             raise ValueError("key and value caches must be bfloat16")
         if not key_cache.is_cuda:
             raise RuntimeError("DecodeAttention runs on CUDA tensors only (no CPU path)")
+        if key_cache.device != self.scratch.device:
+            raise ValueError(f"caches on {key_cache.device}, this instance's scratch on "
+                             f"{self.scratch.device}")
+        _native.check_devices(key_cache.device, q, value_cache, block_table, seq_lens, gate,
+                              out_nibble_major, out_sumsq, cache_offsets, block_table_offsets,
+                              *(raw[:2] + raw[4:] if raw is not None else ()))
         if key_cache.shape[-1] != self.head_dim or key_cache.shape[-2] != self.num_kv_heads:
             raise ValueError("cache view must be [blocks, block_size, kv_heads, head_dim]")
         if block_table.dtype != torch.int32 or seq_lens.dtype != torch.int32:

@@ -78,6 +78,8 @@ def qk_norm_cache(qk: torch.Tensor, v: torch.Tensor, sqk: torch.Tensor, sqk_fact
         raise ValueError("q_out must be contiguous bfloat16")
     if not qk.is_cuda:
         raise RuntimeError("qk_norm_cache runs on CUDA tensors only (no CPU path)")
+    _native.check_devices(qk.device, v, sqk, q_out, key_cache, value_cache, slot_mapping,
+                          k_out, v_out, error_word)
     num_tokens = qk.shape[0] if qk.dim() == 2 else 1
     num_kv_heads = v.shape[-1] // head_dim
     if qk.shape[-1] != (num_heads + num_kv_heads) * head_dim:
@@ -173,6 +175,7 @@ def qkvg_epilogue(partials: torch.Tensor, positions: torch.Tensor, cos_sin: torc
         raise ValueError("partials must be contiguous float32 [split_k, T, 2 * (Q + KV)]")
     if not partials.is_cuda:
         raise RuntimeError("qkvg_epilogue runs on CUDA tensors only (no CPU path)")
+    _native.check_devices(partials.device, positions, cos_sin, s_gate, qk, v, gate, error_word)
     tokens = partials.shape[1]
     if positions.dtype not in (torch.int64, torch.int32) or positions.numel() != tokens:
         raise ValueError("positions must be int64 or int32 with one entry per token")
@@ -237,6 +240,7 @@ def residual_tokens(partials: torch.Tensor, x: torch.Tensor | None, a: torch.Ten
         raise ValueError("partials must be contiguous float32 [split_k, T, H]")
     if not partials.is_cuda:
         raise RuntimeError("residual_tokens runs on CUDA tensors only (no CPU path)")
+    _native.check_devices(partials.device, x, a, alpha, h_out, h_out_nm, x_sumsq)
     split_k, tokens, hidden = partials.shape
     if x is not None and x_sumsq is not None:
         raise ValueError("give x or x_sumsq, not both")
