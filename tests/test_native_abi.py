@@ -130,3 +130,72 @@ def test_qk_norm_host_validation(lib, kw, status, message):
     p = _qk_params(**kw)
     assert lib.dory_qk_norm_cache(ctypes.byref(p), None) == status
     assert message in lib.dory_decode_last_error().decode()
+
+
+def _qkvg_params(**kw):
+    p = _native.DoryQkvgParams()
+    for f in ("partials", "positions", "cos_sin", "s_gate", "qk_out", "v_out", "gate_out"):
+        setattr(p, f, 0x1000)  # never dereferenced: every case fails before any CUDA call
+    p.num_tokens, p.num_heads, p.num_kv_heads, p.head_dim = 1, 4, 2, 64
+    p.split_k, p.max_position, p.s_gate_factor = 2, 16, 0.9
+    for k, val in kw.items():
+        setattr(p, k, val)
+    return p
+
+
+@pytest.mark.parametrize("kw,status,message", [
+    (dict(head_dim=96), _native.ERR_UNSUPPORTED, "head_dim"),
+    (dict(num_heads=0), _native.ERR_INVALID_ARGUMENT, "positive"),
+    (dict(split_k=0), _native.ERR_INVALID_ARGUMENT, "positive"),
+    (dict(max_position=0), _native.ERR_INVALID_ARGUMENT, "positive"),
+    (dict(positions_dtype=2), _native.ERR_INVALID_ARGUMENT, "dtype"),
+    (dict(cos_sin_dtype=3), _native.ERR_INVALID_ARGUMENT, "dtype"),
+    (dict(gate_out=None), _native.ERR_INVALID_ARGUMENT, "null tensor"),
+    (dict(partials=0x1008), _native.ERR_ALIGNMENT, "16-byte"),
+])
+def test_qkvg_host_validation(lib, kw, status, message):
+    assert lib.dory_qkvg_params_bytes() == ctypes.sizeof(_native.DoryQkvgParams)
+    p = _qkvg_params(**kw)
+    assert lib.dory_qkvg_epilogue(ctypes.byref(p), None) == status
+    assert message in lib.dory_decode_last_error().decode()
+
+
+def _residual_params(**kw):
+    p = _native.DoryResidualParams()
+    # distinct, 16-byte aligned, non-overlapping fake addresses (never dereferenced)
+    p.partials, p.a, p.alpha, p.h_out, p.h_out_nibble_major = (
+        0x10000, 0x20000, 0x30000, 0x40000, 0x50000)
+    p.num_tokens, p.hidden, p.split_k = 1, 64, 1
+    p.a_dtype, p.alpha_dtype = _native.DTYPE_BF16, _native.DTYPE_BF16
+    p.alpha_scale, p.eps = 2.5, 1e-6
+    for k, val in kw.items():
+        setattr(p, k, val)
+    return p
+
+
+@pytest.mark.parametrize("kw,status,message", [
+    (dict(hidden=12), _native.ERR_INVALID_ARGUMENT, "multiple of 8"),
+    (dict(hidden=0), _native.ERR_INVALID_ARGUMENT, "multiple of 8"),
+    (dict(hidden=16392), _native.ERR_UNSUPPORTED, "16384"),
+    (dict(split_k=0), _native.ERR_INVALID_ARGUMENT, "split_k"),
+    (dict(num_tokens=-1), _native.ERR_INVALID_ARGUMENT, "num_tokens"),
+    (dict(a_dtype=5), _native.ERR_INVALID_ARGUMENT, "dtype"),
+    (dict(x=0x60000, x_sumsq=0x70000, x_dim=16), _native.ERR_INVALID_ARGUMENT, "not both"),
+    (dict(x=0x60000, x_dim=0), _native.ERR_INVALID_ARGUMENT, "x_dim"),
+    (dict(alpha=None), _native.ERR_INVALID_ARGUMENT, "null tensor"),
+    (dict(a=0x20002), _native.ERR_ALIGNMENT, "16-byte"),
+    (dict(h_out=0x20000), _native.ERR_INVALID_ARGUMENT, "alias"),           # h_out == a
+    (dict(h_out_nibble_major=0x10040), _native.ERR_INVALID_ARGUMENT, "alias"),  # inside partials
+])
+def test_residual_host_validation(lib, kw, status, message):
+    assert lib.dory_residual_params_bytes() == ctypes.sizeof(_native.DoryResidualParams)
+    p = _residual_params(**kw)
+    assert lib.dory_residual_update(ctypes.byref(p), None) == status
+    assert message in lib.dory_decode_last_error().decode()
+
+
+def test_zero_token_calls_need_no_tensors(lib):
+    """T = 0 returns OK before any pointer is looked at or any CUDA call is made."""
+    p = _native.DoryResidualParams()
+    p.num_tokens, p.hidden, p.split_k = 0, 64, 1
+    assert lib.dory_residual_update(ctypes.byref(p), None) == _native.OK
