@@ -15,6 +15,8 @@ from pathlib import Path
 import numpy as np
 import pytest
 import torch
+from hypothesis import given, settings
+from hypothesis import strategies as st
 
 import dory_oracle as O
 import specs
@@ -130,3 +132,28 @@ def test_nibble_major_layout():
     assert nm.shape == (8, 8)
     for e in range(64):
         assert nm[e % 8, e // 8] == x[e]
+
+
+@given(seq_len=st.integers(0, 20000), window=st.sampled_from([0, 1, 15, 16, 17, 1024, 4096]),
+       block=st.sampled_from([16, 32, 64]), splits=st.integers(1, 148),
+       bpt=st.integers(1, 8))
+@settings(max_examples=400, deadline=None)
+def test_split_layout_partitions_the_attended_blocks(seq_len, window, block, splits, bpt):
+    """For any sequence length, window, block size, split count and tile size, the splits'
+    tile ranges [s * tps, min((s + 1) * tps, tiles)) are contiguous, disjoint and cover every
+    tile exactly once; the tiles cover the attended blocks; at most `splits` are active."""
+    n, first, first_block, tiles, tps = O.split_layout(seq_len, window, block, splits, bpt)
+    assert n == seq_len and tps >= 1
+    assert first == (max(seq_len - window, 0) if window > 0 else 0)
+    assert first_block == first // block
+    num_blocks = -(-seq_len // block) - first_block
+    assert tiles == -(-num_blocks // bpt)
+    covered = []
+    for s in range(splits):
+        lo, hi = s * tps, min((s + 1) * tps, tiles)
+        covered.extend(range(lo, hi))
+    assert covered == list(range(tiles))
+    active = -(-tiles // tps)
+    assert active <= splits
+    # blocks of the range: tiles * bpt reaches the last attended block, no tile is empty
+    assert tiles * bpt >= num_blocks > (tiles - 1) * bpt or tiles == 0
