@@ -56,3 +56,25 @@ def test_rotary_pairs_are_adjacent_rows():
     assert torch.equal(head0[HD // 2:], torch.arange(1, HD, 2, dtype=torch.float32))
     assert torch.equal(v[0], torch.arange((NH + NKV) * HD, (NH + 2 * NKV) * HD,
                                           dtype=torch.float32))
+
+
+@pytest.mark.parametrize("head_dim,split_k", [(64, 1), (128, 2), (256, 3)])
+def test_rotation_preserves_head_norms(head_dim, split_k):
+    """With a true rotation table (cos = cos(theta), sin = sin(theta)), the rotary step keeps
+    every q and k head's norm (each (i, i + half) pair is rotated by theta), and v and the
+    gate do not depend on the table."""
+    NH, NKV, T = 4, 2, 3
+    Q, KV = NH * head_dim, NKV * head_dim
+    g = torch.Generator().manual_seed(head_dim + split_k)
+    parts = torch.randn(split_k, T, 2 * (Q + KV), generator=g)
+    theta = torch.rand(50, head_dim // 2, generator=g, dtype=torch.float64) * 6.283
+    cos_sin = torch.cat([theta.cos(), theta.sin()], dim=1).float()
+    pos = torch.randint(0, 50, (T,), generator=g)
+    s_gate = torch.rand(Q, generator=g) + 0.5
+    qk, v, gate = O.qkvg_epilogue(parts, pos, cos_sin, s_gate, 0.9, NH, NKV, head_dim)
+    y = parts.double().sum(0)[:, :Q + KV].reshape(T, NH + NKV, head_dim)
+    got = qk.double().reshape(T, NH + NKV, head_dim)
+    torch.testing.assert_close(got.norm(dim=-1), y.norm(dim=-1), rtol=1e-5, atol=1e-6)
+    ident = torch.cat([torch.ones(50, head_dim // 2), torch.zeros(50, head_dim // 2)], dim=1)
+    _, v2, gate2 = O.qkvg_epilogue(parts, pos, ident, s_gate, 0.9, NH, NKV, head_dim)
+    assert torch.equal(v, v2) and torch.equal(gate, gate2)
