@@ -9,7 +9,7 @@ import dory_oracle as O
 import workloads as W
 from dory_decode_attention import EPS, DecodeAttention
 
-# BASELINE parity bar for the bf16 path: 2e-2 absolute / 1e-2 relative.
+# Parity bar for the bf16 path: 2e-2 absolute / 1e-2 relative.
 ATOL, RTOL = 2e-2, 1e-2
 
 

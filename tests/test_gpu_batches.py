@@ -1,7 +1,7 @@
 """Parity of large batched calls (64 sequences, thousands of (token, KV head, split) CTAs)
 with the oracle, through DecodeAttention and the C ABI.
 
-Outputs within the BASELINE bar (2e-2 abs / 1e-2 rel) and a relative-L2 bound; the whole
+Outputs within the bf16 bar (2e-2 abs / 1e-2 rel) and a relative-L2 bound; the whole
 cache pool bit for bit after the append.  Covers the three cache layouts, split counts and
 minimum split sizes (many empty splits), windows, padding requests, edge lengths (1, 15-17,
 block boundaries), cache offsets that are not whole blocks (copy path) mixed with whole-block

@@ -1,7 +1,7 @@
 """Parity of the sm_100a kernel (through DecodeAttention and the C ABI) with the reference.
 
 * Outputs against the golden vectors from the reference's own eager code, within the
-  BASELINE bar (2e-2 abs / 1e-2 rel) and a relative-L2 bound.
+  bf16 bar (2e-2 abs / 1e-2 rel) and a relative-L2 bound.
 * The whole cache pool after the call, bit for bit: only the appended slots change and they
   hold the oracle's rows (the reference's appended rows agree with those to the bit on
   all but ~1e-5 of elements, within one bf16 ulp there).

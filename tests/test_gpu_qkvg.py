@@ -5,7 +5,7 @@
   gate within the sigmoid's rounding; the launch-form shim gives the same bits.
 * The multi-token sublayer's two launches (the epilogue, then `multi_from_raw`, as
   MultiTokenSublayers.attention runs them, :196-205) against the oracle (its epilogue, then
-  its attention) within the BASELINE bar, the cache pool bit-exact: single tokens, batches
+  its attention) within the bf16 bar (2e-2 abs / 1e-2 rel), the cache pool bit-exact: single tokens, batches
   with padding, shared-cache wavefronts, head dims 64/128/256, split_k 1-4, int64/int32
   positions, FP32/BF16/FP16 cos-sin tables and gate scales, with out_sumsq.
 * Positions outside the cos/sin table are reported in the error word, not dereferenced.

@@ -3,7 +3,7 @@ consumer's output GEMV normalises by, dory_attention.py:114-117), computed in th
 epilogue.
 
 * against the kernel's own output summed in FP64 (only the summation order differs) and
-  against the oracle's output (the BASELINE bar, relative);
+  against the oracle's output (1e-2 relative, the bf16 bar);
 * every epilogue path: one split (direct store), split merge by the last CTA, padding
   requests (0), shared-cache token groups, 8-row and 16-row tiles, head dims 64/128/256;
 * bit-identical on repeated calls and graph replays (fixed summation order, self-resetting

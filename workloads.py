@@ -25,7 +25,7 @@ from dataclasses import dataclass, field
 import torch
 
 LAYOUTS = ("triton", "unbind", "bench")
-NH, NKV, HD, BLOCK = 32, 8, 128, 16  # the BASELINE configurations' attention shape
+NH, NKV, HD, BLOCK = 32, 8, 128, 16  # 32 query heads, 8 KV heads, head_dim 128, block size 16
 SQK_FACTOR = 0.7
 
 
