@@ -13,7 +13,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 LIBRARY = HERE / "libdory_decode.so"
 
-ABI_VERSION = 5
+ABI_VERSION = 6
 
 # DoryStatus
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_ALIGNMENT, ERR_CUDA = range(5)
@@ -35,6 +35,7 @@ DEVERR_NAMES = {DEVERR_BLOCK_OOB: "block id out of range", DEVERR_SLOT_OOB: "slo
 EXPORTS = ("dory_decode_abi_version", "dory_decode_params_bytes", "dory_decode_scratch_bytes",
            "dory_decode_scratch_init", "dory_decode_attention", "dory_decode_fetch_errors",
            "dory_decode_last_error", "dory_decode_attention_static_scratch",
+           "dory_decode_static_scratch_fetch_errors",
            "dory_qk_norm_params_bytes", "dory_qk_norm_cache", "dory_qkvg_params_bytes",
            "dory_qkvg_epilogue", "dory_residual_params_bytes", "dory_residual_update")
 
@@ -125,6 +126,8 @@ def load(path: os.PathLike | None = None) -> ctypes.CDLL:
     lib.dory_decode_last_error.argtypes = []
     lib.dory_decode_attention_static_scratch.restype = _i32
     lib.dory_decode_attention_static_scratch.argtypes = [ctypes.POINTER(DoryDecodeParams), _vp]
+    lib.dory_decode_static_scratch_fetch_errors.restype = _i32
+    lib.dory_decode_static_scratch_fetch_errors.argtypes = [ctypes.POINTER(_u32), _i32, _vp]
     lib.dory_qk_norm_params_bytes.restype = _i64
     lib.dory_qk_norm_params_bytes.argtypes = []
     lib.dory_qk_norm_cache.restype = _i32

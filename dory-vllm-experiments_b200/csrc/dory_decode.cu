@@ -126,6 +126,25 @@ __host__ __device__ inline ScratchLayout scratch_layout(int max_tokens, int S, i
   L.total = align256(L.po + int64_t(max_tokens) * S * NH * HD * 4);
   return L;
 }
+// Host side: the same layout with every product and sum checked for int64 overflow (the
+// counts come from the caller); false if any step overflows or a count is not positive.
+inline bool scratch_layout_checked(int max_tokens, int S, int NH, int NKV, int HD,
+                                   ScratchLayout* out) {
+  if (max_tokens < 1 || S < 1 || NH < 1 || NKV < 1 || HD < 1) return false;
+  // The largest term is the partials, max_tokens * S * NH * HD * 4 bytes; the others are
+  // smaller products of the same counts.  With every term at most 2^60 the layout's sum of
+  // five terms and its alignment padding stays far below 2^63.
+  const int64_t kLimit = int64_t(1) << 60;
+  int64_t rows, po_bytes, ctr_bytes;
+  if (__builtin_mul_overflow(int64_t(max_tokens), int64_t(S), &rows) ||
+      __builtin_mul_overflow(rows, int64_t(NH), &rows) ||
+      __builtin_mul_overflow(rows, int64_t(HD) * 4, &po_bytes) ||
+      __builtin_mul_overflow(int64_t(max_tokens), int64_t(NKV) * 4, &ctr_bytes) ||
+      po_bytes > kLimit || rows * 8 > kLimit || ctr_bytes > kLimit)
+    return false;
+  *out = scratch_layout(max_tokens, S, NH, NKV, HD);
+  return true;
+}
 
 // Dynamic shared memory layout for one instantiation.  Each ring stage holds the K tile
 // and then the V tile of one 16-row chunk, each as HD / 64 boxes of [16 rows][64 dims] bf16
@@ -1950,8 +1969,9 @@ int64_t dory_decode_params_bytes(void) { return int64_t(sizeof(DoryDecodeParams)
 
 int64_t dory_decode_scratch_bytes(int32_t max_tokens, int32_t splits, int32_t num_heads,
                                   int32_t num_kv_heads, int32_t head_dim) {
-  if (max_tokens < 1 || splits < 1 || num_heads < 1 || num_kv_heads < 1 || head_dim < 1) return 0;
-  return scratch_layout(max_tokens, splits, num_heads, num_kv_heads, head_dim).total;
+  ScratchLayout SL;
+  if (!scratch_layout_checked(max_tokens, splits, num_heads, num_kv_heads, head_dim, &SL)) return 0;
+  return SL.total;
 }
 
 int32_t dory_decode_scratch_init(void* scratch, int64_t scratch_bytes, void* stream) {
@@ -2195,8 +2215,9 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
       (a.stride_offset & 7) || (a.stride_head & 7))
     return fail(DORY_ERR_ALIGNMENT,
                 "key/value caches need 16-byte aligned bases and strides (multiples of 8)");
-  const ScratchLayout SL =
-      scratch_layout(a.max_tokens, a.splits, a.num_heads, a.num_kv_heads, HD);
+  ScratchLayout SL;
+  if (!scratch_layout_checked(a.max_tokens, a.splits, a.num_heads, a.num_kv_heads, HD, &SL))
+    return fail(DORY_ERR_INVALID_ARGUMENT, "max_tokens x splits x heads x head_dim overflows");
   if (a.scratch_bytes < SL.total)
     return fail(DORY_ERR_INVALID_ARGUMENT, "scratch too small (%lld < %lld bytes)",
                 (long long)a.scratch_bytes, (long long)SL.total);
@@ -2307,29 +2328,64 @@ namespace {
 // Split partials, merge counters and error word for callers that cannot allocate device
 // memory.  Device code could name it directly; host code only through the address
 // cudaGetSymbolAddress returns (the host-side symbol is a stand-in, not a device pointer).
+// Device globals start zeroed, so the error word and the counters start at zero.
 __device__ __align__(256) uint8_t g_static_scratch[DORY_DECODE_STATIC_SCRATCH_BYTES];
 
-constexpr int kMaxDevices = 64;
+// The array's device address belongs to a CUDA context (each context that loads this
+// library has its own copy), so it is cached per context: the runtime's primary context
+// of a device, or a context a driver-API host made current itself.
+constexpr int kMaxContexts = 64;
 std::mutex g_static_mutex;
-void* g_static_ptr[kMaxDevices] = {nullptr};
+struct StaticEntry {
+  CUcontext ctx;
+  void* ptr;
+};
+StaticEntry g_static_entries[kMaxContexts];
+int g_static_used = 0;
 
-// Device address of g_static_scratch on the current device, looked up once per device.
-int32_t static_scratch_address(void** out) {
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess) return fail(DORY_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
-  if (dev < 0 || dev >= kMaxDevices)
-    return fail(DORY_ERR_UNSUPPORTED, "device ordinal %d beyond %d", dev, kMaxDevices);
-  std::lock_guard<std::mutex> lock(g_static_mutex);
-  if (!g_static_ptr[dev]) {
+PFN_cuCtxGetCurrent_v4000 ctx_get_current() {
+  static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
     void* ptr = nullptr;
-    e = cudaGetSymbolAddress(&ptr, g_static_scratch);
-    if (e != cudaSuccess || ptr == nullptr)
-      return fail(DORY_ERR_CUDA, "cudaGetSymbolAddress(static scratch): %s",
-                  cudaGetErrorString(e));
-    g_static_ptr[dev] = ptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(ptr);
+  });
+  return fn;
+}
+
+CUcontext current_context() {
+  CUcontext ctx = nullptr;
+  auto get = ctx_get_current();
+  if (!get || get(&ctx) != CUDA_SUCCESS) return nullptr;
+  return ctx;
+}
+
+// Device address of g_static_scratch in the calling thread's current context (the current
+// device's primary context when none is bound), looked up once per context.
+int32_t static_scratch_address(void** out) {
+  CUcontext ctx = current_context();
+  std::lock_guard<std::mutex> lock(g_static_mutex);
+  if (ctx)
+    for (int i = 0; i < g_static_used; ++i)
+      if (g_static_entries[i].ctx == ctx) {
+        *out = g_static_entries[i].ptr;
+        return DORY_OK;
+      }
+  void* ptr = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
+  if (e != cudaSuccess || ptr == nullptr)
+    return fail(DORY_ERR_CUDA, "cudaGetSymbolAddress(static scratch): %s", cudaGetErrorString(e));
+  if (!ctx) ctx = current_context();  // the runtime has now bound the primary context
+  if (ctx) {
+    if (g_static_used == kMaxContexts)
+      return fail(DORY_ERR_UNSUPPORTED, "static scratch used from more than %d contexts",
+                  kMaxContexts);
+    g_static_entries[g_static_used++] = StaticEntry{ctx, ptr};
   }
-  *out = g_static_ptr[dev];
+  *out = ptr;
   return DORY_OK;
 }
 
@@ -2337,11 +2393,10 @@ int32_t static_scratch_address(void** out) {
 
 extern "C" int32_t dory_decode_attention_static_scratch(const DoryDecodeParams* P, void* stream) {
   if (!P) return fail(DORY_ERR_INVALID_ARGUMENT, "null params");
-  if (P->max_tokens < 1 || P->splits < 1 || P->num_heads < 1 || P->num_kv_heads < 1 ||
-      P->head_dim < 1)
-    return fail(DORY_ERR_INVALID_ARGUMENT, "invalid scratch shape");
-  const ScratchLayout SL =
-      scratch_layout(P->max_tokens, P->splits, P->num_heads, P->num_kv_heads, P->head_dim);
+  ScratchLayout SL;
+  if (!scratch_layout_checked(P->max_tokens, P->splits, P->num_heads, P->num_kv_heads,
+                              P->head_dim, &SL))
+    return fail(DORY_ERR_INVALID_ARGUMENT, "invalid or overflowing scratch shape");
   if (SL.total > DORY_DECODE_STATIC_SCRATCH_BYTES)
     return fail(DORY_ERR_INVALID_ARGUMENT,
                 "this call needs %lld bytes of scratch; the static scratch holds %lld "
@@ -2350,11 +2405,24 @@ extern "C" int32_t dory_decode_attention_static_scratch(const DoryDecodeParams* 
   void* scratch = nullptr;
   const int32_t st = static_scratch_address(&scratch);
   if (st != DORY_OK) return st;
-  // The previous call's counters and error word must not leak into this one.
-  cudaError_t e = cudaMemsetAsync(scratch, 0, size_t(SL.pml), (cudaStream_t)stream);
+  // The counters (merge and sum-of-squares) sit at different offsets for different call
+  // shapes, so the previous call's must not leak into this one: clear them.  The error word
+  // in front of them is kept; it gathers the device errors of every call until
+  // dory_decode_static_scratch_fetch_errors reads (and optionally clears) it.
+  cudaError_t e = cudaMemsetAsync(static_cast<uint8_t*>(scratch) + SL.counters, 0,
+                                  size_t(SL.pml - SL.counters), (cudaStream_t)stream);
   if (e != cudaSuccess) return fail(DORY_ERR_CUDA, "cudaMemsetAsync: %s", cudaGetErrorString(e));
   DoryDecodeParams a = *P;
   a.scratch = scratch;
   a.scratch_bytes = DORY_DECODE_STATIC_SCRATCH_BYTES;
   return dory_decode_attention(&a, stream);
+}
+
+extern "C" int32_t dory_decode_static_scratch_fetch_errors(uint32_t* flags_out, int32_t clear,
+                                                           void* stream) {
+  if (!flags_out) return fail(DORY_ERR_INVALID_ARGUMENT, "null argument");
+  void* scratch = nullptr;
+  const int32_t st = static_scratch_address(&scratch);
+  if (st != DORY_OK) return st;
+  return dory_decode_fetch_errors(scratch, flags_out, clear, stream);
 }

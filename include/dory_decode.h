@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define DORY_DECODE_ABI_VERSION 5
+#define DORY_DECODE_ABI_VERSION 6
 
 /* Status codes returned by every entry point. */
 typedef enum DoryStatus {
@@ -152,27 +152,36 @@ int32_t dory_decode_attention(const DoryDecodeParams* params, void* stream);
 
 /*
  * dory_decode_attention without caller-owned scratch, for callers that cannot allocate
- * device memory: code that enqueues work while a CUDA graph is being captured in the
- * global capture mode (where cudaMalloc is an error), engines that have already reserved
- * the whole device for their own KV-cache allocator, and foreign-function hosts with no
- * device allocator of their own.  No counterpart in the reference (its DecodeAttention
- * always allocates its scratch, dory_decode_attention.py:242-246).
+ * device memory: serving engines that hand the whole device to their own KV-cache
+ * allocator up front (nothing is left for a second allocator, and freeing would fragment
+ * theirs), foreign-function hosts (C, Go, Java) that have no device allocator of their own,
+ * and programs whose policy forbids device allocation after start-up.  No counterpart in
+ * the reference.
  *
  * Takes the same parameters; `scratch` and `scratch_bytes` are ignored.  The split partials,
  * merge counters and error word live instead in one statically sized device array inside
  * this library (DORY_DECODE_STATIC_SCRATCH_BYTES = 4 MiB), which every GPU that loads the
  * library holds until the process exits.  A call whose layout needs more scratch than that
  * (max_tokens * splits * num_heads * head_dim * 4 bytes of partials, plus counters) fails
- * with DORY_ERR_INVALID_ARGUMENT.  Allocates nothing: no cudaMalloc, no cudaFree.
+ * with DORY_ERR_INVALID_ARGUMENT, as does one whose layout arithmetic overflows.  Allocates
+ * nothing: no cudaMalloc, no cudaFree.
  *
- * The first call on a device looks up the array's device address (cudaGetSymbolAddress,
- * with that device current) and must therefore happen before any stream capture on that
- * device.  Every call clears the merge counters and the error word on `stream` before its
- * kernel.  All calls share the one array and it keeps the last call's contents, so calls
- * that can overlap on the GPU (different streams, without ordering between them) race.
+ * The array's device address is looked up (cudaGetSymbolAddress) by the first call in each
+ * CUDA context: the device's primary context (the runtime's), or a context a driver-API
+ * host made current itself.  That first call should come before any stream capture in that
+ * context.  Every call clears the merge counters on `stream` before its kernel; the device
+ * error word is kept and gathers the DORY_DEVERR_* bits of every call until
+ * dory_decode_static_scratch_fetch_errors reads it.  All calls share the one array and it
+ * keeps the last call's contents, so calls that can overlap on the GPU (different streams,
+ * without ordering between them) race.
  */
 #define DORY_DECODE_STATIC_SCRATCH_BYTES (4ll << 20)
 int32_t dory_decode_attention_static_scratch(const DoryDecodeParams* params, void* stream);
+
+/* The device error word of dory_decode_attention_static_scratch (DORY_DEVERR_* bits of every
+ * call in the current context since the last clear) into *flags_out, synchronising `stream`;
+ * clears it when `clear` is non-zero.  No counterpart in the reference. */
+int32_t dory_decode_static_scratch_fetch_errors(uint32_t* flags_out, int32_t clear, void* stream);
 
 /*
  * The separate q/k normalisation step of the reference's attention sublayer:

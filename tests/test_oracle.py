@@ -4,8 +4,10 @@ Pins oracle/dory_oracle.py before any kernel is compared with it:
 * inputs regenerated from the seeds hash to the digests stored by make_golden.py;
 * with the reference's single q rounding the oracle reproduces `reference_attention` to
   FP32 accuracy; with the kernel's second rounding it stays inside the bf16 tolerance;
-* appended k / v / q match the reference's `normalize_rows` bit patterns (all but a
-  fraction of rows to the bit, the rest within one bf16 ulp — FP32 summation order).
+* the appended k / v rows match the reference's `normalize_rows` bit patterns on every
+  element of every golden case, and the bf16 query on all but one element, where the
+  reference's FP32 `torch.rsqrt` (1 / sqrt, rounded twice) is one FP32 ulp above the
+  correctly rounded inverse square root and the oracle's value is the correctly rounded one.
 """
 
 from __future__ import annotations
@@ -72,26 +74,76 @@ def _ulps(a: np.ndarray, b: np.ndarray) -> np.ndarray:
     return np.abs(a.astype(np.int32) - b.astype(np.int32))
 
 
+# The one element of all golden cases where the oracle's bf16 query differs from the
+# reference's normalize_rows result: (case, token, q head, dim, oracle bits, reference bits).
+QUERY_DIFFERENCES = [("wavefront_window", 2, 17, 78, 15464, 15465)]
+
+
 def test_normalisation_vs_reference_bits():
-    """The canonical normalisation against the reference's normalize_rows bit patterns,
-    over every golden case: exact on >= 99% of elements, never more than 1 ulp away."""
-    total = exact = 0
-    worst = 0
+    """The canonical normalisation against the reference's normalize_rows bit patterns over
+    every golden case: the appended k and v rows (the cache contents) match on every
+    element; the bf16 query matches on every element but the one listed in
+    QUERY_DIFFERENCES, one bf16 ulp away."""
+    k_total = q_total = 0
+    q_diffs = []
     for name, build in CASES.items():
         g = load(name)
         case = build()
         for t in range(case.tokens):
             q, k, v = O.raw_qkv(case.qk[t], case.v[t], case.sqk, case.sqk_factor, O.EPS,
                                 case.num_heads, case.num_kv_heads, case.head_dim)
-            for mine, ref in ((k, g["k_new"][t]), (q, g["q_bf16"][t].reshape(q.shape))):
-                m = mine.view(torch.int16).numpy().reshape(ref.shape)
-                d = _ulps(m, ref)
-                total += d.size
-                exact += int((d == 0).sum())
-                worst = max(worst, int(d.max()))
-            assert np.array_equal(v.view(torch.int16).numpy(), g["v_new"][t])
-    assert worst <= 1
-    assert exact / total >= 0.99, exact / total
+            km = k.view(torch.int16).numpy().reshape(g["k_new"][t].shape)
+            assert np.array_equal(km, g["k_new"][t]), (name, t)
+            assert np.array_equal(v.view(torch.int16).numpy(), g["v_new"][t]), (name, t)
+            k_total += km.size
+            ref = g["q_bf16"][t].reshape(q.shape)
+            mine = q.view(torch.int16).numpy().reshape(ref.shape)
+            q_total += mine.size
+            for h, dim in np.argwhere(mine != ref):
+                q_diffs.append((name, t, int(h), int(dim), int(mine[h, dim]), int(ref[h, dim])))
+    assert q_diffs == QUERY_DIFFERENCES, q_diffs
+    assert k_total == 22_272 and q_total == 91_136  # elements compared (113,408 in all)
+
+
+def test_the_query_difference_is_the_reference_fp32_rsqrt():
+    """The one query element the oracle rounds differently from the reference's eager code:
+    the exact value (rational arithmetic on the same FP32 inputs) lies below the midpoint
+    of its two bf16 neighbours, so round-to-nearest gives the oracle's bits.  The reference
+    computes torch.rsqrt in FP32, which PyTorch evaluates as 1 / sqrt with two roundings:
+    one FP32 ulp above the correctly rounded inverse square root, enough to push the product
+    over the midpoint.  The same eager expression in FP64 gives the oracle's bits, so
+    PyTorch eager itself gives two different bits for this element."""
+    from fractions import Fraction
+    name, t, h, dim, mine, ref_bits = QUERY_DIFFERENCES[0]
+    case = CASES[name]()
+    NH, HD = case.num_heads, case.head_dim
+    x = case.qk[t][: NH * HD].view(NH, HD)[h]
+    s2 = (case.sqk.float()[h * HD + dim] * case.sqk_factor).square()  # FP32, as the reference
+    sum32 = x.square().sum() + O.EPS  # FP32 sum (equal to the FP64 sum rounded, here)
+    assert float(sum32) == float(np.float32(np.float32((x.double() ** 2).sum().item()) +
+                                            np.float32(O.EPS)))
+
+    def bits(v: torch.Tensor) -> int:
+        return int(v.to(torch.bfloat16).view(torch.int16))
+
+    def bf16_value(b: int) -> Fraction:
+        return Fraction(float(torch.tensor([b], dtype=torch.int16).view(torch.bfloat16)))
+
+    # exact value of s2 * x[dim] / sqrt(sum32), compared with the bf16 midpoint by squaring
+    # (all quantities positive): value < mid  <=>  (s2 * x)^2 < mid^2 * sum32
+    mid = (bf16_value(mine) + bf16_value(ref_bits)) / 2
+    num = (Fraction(float(s2)) * Fraction(float(x[dim]))) ** 2
+    assert num < mid * mid * Fraction(float(sum32)), "the exact value is below the midpoint"
+    assert bf16_value(mine) < mid < bf16_value(ref_bits)
+
+    r32 = torch.rsqrt(sum32)  # the reference's FP32 inverse square root
+    r64 = torch.rsqrt(sum32.double()).float()  # the correctly rounded FP32 value
+    assert r32.item() == np.nextafter(np.float32(r64.item()), np.float32(1.0))  # one ulp above
+    assert bits(s2 * (x[dim] * r32)) == ref_bits  # the reference's eager expression, FP32
+    assert bits(s2 * (x[dim] * r64)) == mine      # the same in FP64 precision: the oracle
+    q, _, _ = O.raw_qkv(case.qk[t], case.v[t], case.sqk, case.sqk_factor, O.EPS, NH,
+                        case.num_kv_heads, HD)
+    assert int(q.view(torch.int16).reshape(NH, HD)[h, dim]) == mine
 
 
 def test_cache_after_append_is_reference_layout():

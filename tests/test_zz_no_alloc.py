@@ -1,23 +1,29 @@
 """dory_decode_attention_static_scratch: decode attention for callers that cannot allocate.
 
-Some callers of this library cannot call cudaMalloc: code that enqueues work while a CUDA
-graph is being captured in the global capture mode (allocation is an error there), serving
-engines that reserved the whole device for their KV-cache allocator up front, and C or
-other foreign-function hosts that have no device allocator of their own.  For them the
+Some callers of this library cannot call cudaMalloc: serving engines that hand the whole
+device to their own KV-cache allocator up front, so nothing is left for a second one, and C
+or other foreign-function hosts that have no device allocator of their own.  For them the
 library keeps its split partials and merge counters in a 4 MiB device array of its own
-instead of a caller-owned scratch buffer.
+instead of a caller-owned scratch buffer, and keeps the device error word there too
+(read back with dory_decode_static_scratch_fetch_errors).
 
-This test calls that entry point through the C ABI (ctypes, as a foreign host would) twice
-in a row — a single-token call and a four-token shared-cache wavefront call — and checks
-each output against the existing entry point's (DecodeAttention with its own scratch)
-within the parity tolerance of the other tests, and the appended cache rows bit for bit.
-The file sorts last so a failure here stops a `-x` run only after every other test ran.
+The first test calls that entry point through the C ABI (ctypes, as a foreign host would)
+twice in a row — a single-token call and a four-token shared-cache wavefront call — and
+checks each output against the existing entry point's (DecodeAttention with its own scratch)
+and against the golden outputs of the reference's own eager code for the same two inputs,
+within the parity tolerance of the other tests (2e-2 abs / 1e-2 rel), and the appended cache
+rows bit for bit.  The second test makes the kernel's bounds check record an error (an
+append slot outside the cache, made on the host) and reads it back through the new export.
+The file sorts last so a failure here stops a `-x` run only after every other test ran; each
+test also passes on its own in a fresh process.
 """
 
 from __future__ import annotations
 
 import ctypes
+from pathlib import Path
 
+import numpy as np
 import pytest
 import torch
 
@@ -27,6 +33,8 @@ from dory_decode_attention import EPS, DecodeAttention
 from gpu_helpers import ATOL, RTOL
 
 pytestmark = pytest.mark.gpu
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
 
 
 def _params(case: W.Case, d: dict, splits: int) -> _native.DoryDecodeParams:
@@ -79,23 +87,65 @@ def _with_caller_scratch(case: W.Case, splits: int):
     return d["out"].cpu(), d["raw"].cpu()
 
 
-def test_static_scratch_matches_caller_scratch_two_calls_in_a_row():
+def _static_errors(lib, clear: bool) -> int:
+    flags = ctypes.c_uint32(0xFFFFFFFF)
+    stream = torch.cuda.current_stream().cuda_stream
+    _native.check(lib.dory_decode_static_scratch_fetch_errors(ctypes.byref(flags), int(clear),
+                                                              stream))
+    return flags.value
+
+
+def test_static_scratch_matches_caller_scratch_and_goldens_two_calls_in_a_row():
     lib = _native.load()
     splits = 32
+    # the inputs of the golden cases "config1" and "wavefront" (tests/golden/specs.py)
     cases = [W.single(seed=0, context=640, pool_blocks=64),
              W.wavefront(seed=1, prompt=700, generated=37, tokens=4)]
+    goldens = [torch.from_numpy(np.load(GOLDEN / f"{n}.npz")["out"])
+               for n in ("config1", "wavefront")]
     expected = [_with_caller_scratch(c, splits) for c in cases]
 
     devs = [W.to_device(c, "triton", "cuda") for c in cases]
     params = [_params(c, d, splits) for c, d in zip(cases, devs)]
     stream = torch.cuda.current_stream().cuda_stream
+    _static_errors(lib, clear=True)  # start from a clean error word
     for p in params:  # two calls back to back, sharing the library's one scratch array
         _native.check(lib.dory_decode_attention_static_scratch(ctypes.byref(p), stream))
     torch.cuda.synchronize()
 
-    for (out_ref, raw_ref), d in zip(expected, devs):
-        torch.testing.assert_close(d["out"].cpu(), out_ref, atol=ATOL, rtol=RTOL)
+    for (out_ref, raw_ref), golden, d in zip(expected, goldens, devs):
+        out = d["out"].cpu()
+        torch.testing.assert_close(out, out_ref, atol=ATOL, rtol=RTOL)
+        torch.testing.assert_close(out, golden, atol=ATOL, rtol=RTOL)
         assert torch.equal(d["raw"].cpu().view(torch.int16), raw_ref.view(torch.int16))
+    assert _static_errors(lib, clear=False) == 0
+
+
+def test_static_scratch_error_word_survives_calls_until_fetched():
+    lib = _native.load()
+    case = W.single(seed=71, context=300, pool_blocks=30)
+    d = W.to_device(case, "triton", "cuda")
+    before = d["raw"].clone()
+    stream = torch.cuda.current_stream().cuda_stream
+    _static_errors(lib, clear=True)
+    p = _params(case, d, splits=16)
+    # an append slot in block 30 of a 30-block cache: the kernel's bounds check records
+    # DORY_DEVERR_SLOT_OOB and skips the write
+    bad = torch.tensor([30 * 16 + 5], dtype=torch.int64, device="cuda")
+    p.slot_mapping = bad.data_ptr()
+    _native.check(lib.dory_decode_attention_static_scratch(ctypes.byref(p), stream))
+    # a second, valid call must not wipe the first call's error
+    good = _params(case, d, splits=16)
+    _native.check(lib.dory_decode_attention_static_scratch(ctypes.byref(good), stream))
+    torch.cuda.synchronize()
+    assert _static_errors(lib, clear=True) & _native.DEVERR_SLOT_OOB
+    assert _static_errors(lib, clear=False) == 0  # cleared
+    # the bad call wrote nothing; the good call appended its row at the case's own slot
+    slot, B = case.slot(0), case.block_size
+    after = d["raw"].cpu()
+    changed = (after.view(torch.int16) != before.cpu().view(torch.int16))
+    rows = changed.transpose(1, 2).any(dim=-1)  # [blocks, 16, kv_heads]
+    assert rows.nonzero()[:, :2].unique(dim=0).tolist() == [[slot // B, slot % B]]
 
 
 def test_static_scratch_rejects_calls_beyond_its_size():
@@ -107,3 +157,7 @@ def test_static_scratch_rejects_calls_beyond_its_size():
     status = lib.dory_decode_attention_static_scratch(ctypes.byref(p), None)
     assert status == _native.ERR_INVALID_ARGUMENT
     assert "static scratch" in lib.dory_decode_last_error().decode()
+    p.max_tokens, p.splits, p.num_heads = 1 << 30, 1 << 30, 1 << 14  # the product overflows
+    status = lib.dory_decode_attention_static_scratch(ctypes.byref(p), None)
+    assert status == _native.ERR_INVALID_ARGUMENT
+    assert "overflow" in lib.dory_decode_last_error().decode()
