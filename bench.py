@@ -294,8 +294,19 @@ def algorithmic_bytes(seq_lens, shared: bool, window: int, nh: int, nkv: int, hd
             + extra)
 
 
+# Each graph replay must touch more than this many bytes of distinct cache pools, so that
+# no step finds its K/V left in the 126 MB L2 by the step before: small workloads capture
+# several steps per graph, each over its own pools.
+L2_BYTES = 126e6
+MIN_REPLAY_BYTES = 3 * L2_BYTES
+
+
 class DeviceWorkload:
-    """Per-rank device tensors: block pools, tables, per-layer inputs and outputs."""
+    """Per-rank device tensors: block pools, tables, per-layer inputs and outputs.
+
+    One graph replay runs `reps` steps; step r's layer l reads pool (r * layers + l) modulo
+    the pool count, and `reps` is the smallest count whose distinct pools exceed
+    MIN_REPLAY_BYTES (1 for every workload whose layers alone exceed it)."""
 
     def __init__(self, spec: Spec, lens, dev, seed, mem_fraction=0.5):
         tokens_per_seq, shared, layers = spec.tokens_per_seq, spec.shared, spec.layers
@@ -345,7 +356,11 @@ class DeviceWorkload:
         self.pool_blocks = blocks
         self.pool_bytes = pool_bytes = blocks * BLOCK * self.kv_row_bytes
         free, _ = torch.cuda.mem_get_info(dev)
-        self.num_pools = max(1, min(self.num_layers, int(mem_fraction * free // pool_bytes)))
+        fit = max(1, int(mem_fraction * free // pool_bytes))
+        self.reps = max(1, math.ceil(MIN_REPLAY_BYTES / (pool_bytes * self.num_layers)))
+        if self.reps * self.num_layers > fit:
+            self.reps = 1
+        self.num_pools = max(1, min(self.num_layers * self.reps, fit))
         gd = torch.Generator(device=dev).manual_seed(seed)
         self.raws, self.keys, self.values = [], [], []
         for _ in range(self.num_pools):
@@ -363,8 +378,9 @@ class DeviceWorkload:
         self.q_out = torch.empty(T, NH_ * HD_, dtype=torch.bfloat16, device=dev)
         self.sumsq = None  # --sumsq: [layers, T] FP32 sum of squared outputs per token
 
-    def pool(self, layer: int):
-        return self.keys[layer % self.num_pools], self.values[layer % self.num_pools]
+    def pool(self, layer: int, rep: int = 0):
+        i = (rep * self.num_layers + layer) % self.num_pools
+        return self.keys[i], self.values[i]
 
     def window(self, layer: int) -> int:
         return self.spec.window(layer)
@@ -394,11 +410,12 @@ def prepare_call_path(wl: DeviceWorkload):
     from dory_sublayer_steps import qk_norm_cache
     from dory_decode_attention import EPS
     wl.q_call = torch.empty(wl.num_layers, 1, wl.nh * wl.hd, dtype=torch.bfloat16, device=wl.dev)
-    for layer in range(wl.num_layers):
-        key, value = wl.pool(layer)
-        qk_norm_cache(wl.qk[layer][0], wl.v[layer][0], wl.sqk, W.SQK_FACTOR, EPS,
-                      wl.q_call[layer][0], wl.nh, wl.hd, key_cache=key, value_cache=value,
-                      slot_mapping=wl.slots[0:1])
+    for rep in range(wl.reps):
+        for layer in range(wl.num_layers):
+            key, value = wl.pool(layer, rep)
+            qk_norm_cache(wl.qk[layer][0], wl.v[layer][0], wl.sqk, W.SQK_FACTOR, EPS,
+                          wl.q_call[layer][0], wl.nh, wl.hd, key_cache=key, value_cache=value,
+                          slot_mapping=wl.slots[0:1])
     wl.path = "call"
 
 
@@ -459,10 +476,11 @@ def step_inputs(wl: DeviceWorkload):
     return (wl.qk, wl.v, wl.gate)
 
 
-def layer_call(attn, wl: DeviceWorkload, app: int, layer: int, ins, out):
-    """One application: `ins` are this application's slices of step_inputs()."""
+def layer_call(attn, wl: DeviceWorkload, app: int, layer: int, ins, out, rep: int = 0):
+    """One application: `ins` are this application's slices of step_inputs(); `rep` picks
+    the step's pools within a multi-step replay."""
     from dory_decode_attention import EPS
-    key, value = wl.pool(layer)
+    key, value = wl.pool(layer, rep)
     window, scale = wl.window(layer), wl.hd ** -0.5
     sumsq = None if wl.sumsq is None else wl.sumsq[layer]
     if wl.path == "call":
@@ -497,9 +515,16 @@ def layer_call(attn, wl: DeviceWorkload, app: int, layer: int, ins, out):
                         shared_cache=wl.shared, out_sumsq=sumsq)
 
 
-def run_step(attn, wl: DeviceWorkload):
+def run_step(attn, wl: DeviceWorkload, rep: int = 0):
     for app, layer in enumerate(wl.layers):
-        layer_call(attn, wl, app, layer, [t[layer] for t in step_inputs(wl)], wl.out[layer])
+        layer_call(attn, wl, app, layer, [t[layer] for t in step_inputs(wl)], wl.out[layer],
+                   rep)
+
+
+def run_replay(attn, wl: DeviceWorkload):
+    """What one graph replay runs: wl.reps steps, each over its own pools."""
+    for rep in range(wl.reps):
+        run_step(attn, wl, rep)
 
 
 # ---------------------------------------------------------------------------------------
@@ -533,6 +558,51 @@ def bench_profile(args):
           flush=True)
 
 
+def time_graph(attn, wl: DeviceWorkload, steps: int, warmup: int, dist, dev):
+    """Eager warm-up and error check, then one graph replay (wl.reps steps) captured,
+    `warmup` untimed replays, and `steps` workload steps timed with CUDA events between
+    barriers while nvidia-smi samples the clocks.  `steps` must be a multiple of wl.reps.
+    Returns (ms per step on this rank, clock summary)."""
+    assert steps % wl.reps == 0
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(s):
+        run_replay(attn, wl)
+    torch.cuda.current_stream(dev).wait_stream(s)
+    torch.cuda.synchronize(dev)
+    attn.check_errors()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        run_replay(attn, wl)
+    for _ in range(warmup):
+        graph.replay()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(dist, dev)
+    with ClockSampler(dev) as clocks:
+        start.record()
+        for _ in range(steps // wl.reps):
+            graph.replay()
+        end.record()
+        torch.cuda.synchronize(dev)
+    barrier(dist, dev)
+    attn.check_errors()
+    del graph
+    return start.elapsed_time(end) / steps, clocks.summary()
+
+
+def roofline_of(wl: DeviceWorkload, workload: str, us_per_launch: float) -> dict:
+    """Roofline of the kernel: algorithmic bytes per launch / average launch time against
+    the measured copy bandwidth; traffic from the committed ncu summary when there is one."""
+    peaks = load_peaks()
+    per_launch = wl.algorithmic_bytes_per_step() / len(wl.layers)
+    achieved = per_launch / (us_per_launch * 1e-6) / 1e9
+    ratio = read_traffic_ratio(workload)
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks[0], "unit": "GB/s",
+            "frac": round(achieved / peaks[0], 4),
+            "traffic": int(ratio * per_launch) if ratio else None, "peak_source": peaks[1],
+            "algorithmic_bytes_per_launch": round(per_launch), "launch_us": round(us_per_launch, 3)}
+
+
 def bench_ours(args, world, rank, local):
     dist = init_dist(world, local)
     dev = torch.device("cuda", local if world > 1 else 0)
@@ -553,110 +623,133 @@ def bench_ours(args, world, rank, local):
     if args.path in ("separate", "call") and wl.tokens != 1:
         raise SystemExit(f"--path {args.path} takes single-sequence workloads "
                          "(config1, config4, dory*)")
-    if args.path == "separate":
-        wl.path = "separate"
-    elif args.path == "call":
-        prepare_call_path(wl)
-    elif args.path == "qkvg":
-        prepare_qkvg_path(wl)
-    elif args.path == "sublayer":
-        prepare_sublayer_path(wl)
+    prepare_path(wl, args.path)
     attn = make_attention(wl, args)
     apps = len(layers)
 
-    # capture the step in a CUDA graph (the reference's time_graph idiom)
-    s = torch.cuda.Stream(dev)
-    s.wait_stream(torch.cuda.current_stream(dev))
-    with torch.cuda.stream(s):
-        run_step(attn, wl)
-    torch.cuda.current_stream(dev).wait_stream(s)
-    torch.cuda.synchronize(dev)
-    attn.check_errors()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
-        run_step(attn, wl)
-    for _ in range(args.warmup):
-        graph.replay()
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    barrier(dist, dev)
-    with ClockSampler(dev) as clocks:
-        start.record()
-        for _ in range(args.steps):
-            graph.replay()
-        end.record()
-        torch.cuda.synchronize(dev)
-    barrier(dist, dev)
-    ms_local = start.elapsed_time(end)
+    steps = -(-args.steps // wl.reps) * wl.reps
+    ms_local, clocks = time_graph(attn, wl, steps, args.warmup, dist, dev)
     ms = max_over_ranks(dist, ms_local, dev)
-    attn.check_errors()
 
     total_seqs = len(lens_all) * (tps if shared else 1)
     bytes_rank = wl.algorithmic_bytes_per_step()
     bytes_all = sum_over_ranks(dist, float(bytes_rank), dev)
-    ms_per_step = ms / args.steps
+    ms_per_step = ms
     seqs_per_s = (total_seqs * (world if scaling == "replicas" else 1)) / (ms_per_step / 1e3)
     us_per_layer = ms_per_step * 1e3 / apps
     hbm_gbs = bytes_all / (ms_per_step / 1e3) / 1e9
-
     # roofline of the one kernel: this rank's bytes per launch / its average launch time
-    peaks = load_peaks()
-    per_launch_bytes = bytes_rank / apps  # this rank's average launch
-    launch_us = ms_local * 1e3 / (args.steps * apps)
-    achieved = per_launch_bytes / (launch_us * 1e-6) / 1e9
-    ratio = read_traffic_ratio(args.workload)
-    traffic = int(ratio * per_launch_bytes) if ratio else None
-    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks[0],
-                "unit": "GB/s", "frac": round(achieved / peaks[0], 4),
-                "traffic": traffic, "peak_source": peaks[1],
-                "algorithmic_bytes_per_launch": round(per_launch_bytes),
-                "launch_us": round(launch_us, 3)}
+    roofline = roofline_of(wl, args.workload, ms_local * 1e3 / apps)
 
     e2e = bench_e2e(attn, wl, args, dist, dev, total_seqs, world, scaling)
-    del graph
+    launches_per_step = apps * {"separate": 2, "qkvg": 2, "sublayer": 3}.get(wl.path, 1)
+    config = {"workload": f"{args.workload}: {notes}", "global_batch": total_seqs,
+              "layers_per_step": apps, "num_heads": wl.nh, "num_kv_heads": wl.nkv,
+              "head_dim": wl.hd, "block_size": BLOCK,
+              "windows": sorted({wl.window(layer) for layer in layers}),
+              "cache_layout": "vLLM Triton [blocks, kv_heads, 16, 2*head_dim] viewed "
+              "via transpose(1,2).split",
+              "parallelism": f"request partition over {world} GPU(s), no collectives",
+              "distinct_pools_per_rank": wl.num_pools, "steps_per_replay": wl.reps,
+              "l2": l2_note(wl),
+              "splits": args.splits, "min_blocks_per_split": args.min_blocks_per_split,
+              "overlap_launch": args.overlap_launch, "path": args.path,
+              "out_sumsq": bool(args.sumsq)}
+    del attn, wl
     torch.cuda.synchronize(dev)
+    torch.cuda.empty_cache()
 
-    cpu = None
+    cpu, extra = None, None
     if rank == 0 and world == 1:
         cpu = cpu_baseline(args.workload, args.cpu_seconds)
+        if args.all_configs and args.workload == "config5" and args.path == "fused":
+            extra = measure_other_configs(args, dev)
 
     line = {
         "metric": METRIC, "value": round(seqs_per_s, 2), "unit": "seqs/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+        "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
         "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded N(0,1) K/V, q/k/v, gate; random block-table permutations)",
-        "config": {"workload": f"{args.workload}: {notes}", "global_batch": total_seqs,
-                   "layers_per_step": apps, "num_heads": wl.nh, "num_kv_heads": wl.nkv,
-                   "head_dim": wl.hd, "block_size": BLOCK,
-                   "windows": sorted({wl.window(layer) for layer in layers}),
-                   "cache_layout": "vLLM Triton [blocks, kv_heads, 16, 2*head_dim] viewed "
-                   "via transpose(1,2).split",
-                   "parallelism": f"request partition over {world} GPU(s), no collectives",
-                   "distinct_pools_per_rank": wl.num_pools,
-                   "l2": l2_note(wl),
-                   "splits": args.splits, "min_blocks_per_split": args.min_blocks_per_split,
-                   "overlap_launch": args.overlap_launch, "path": args.path,
-                   "out_sumsq": bool(args.sumsq)},
+        "config": config,
         "us_per_layer_step": round(us_per_layer, 3),
         "hbm_gbs": round(hbm_gbs, 1),
         "roofline": roofline,
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": args.steps * apps * {"separate": 2, "qkvg": 2, "sublayer": 3}.get(wl.path, 1),
-        "clocks": clocks.summary(),
+        "gpu_launches": steps * launches_per_step,
+        "clocks": clocks,
     }
+    if extra is not None:
+        line["configs"] = extra
     if rank == 0:
         print(json.dumps(line), flush=True)
     if dist is not None:
         dist.destroy_process_group()
 
 
+def prepare_path(wl: DeviceWorkload, path: str):
+    if path == "separate":
+        wl.path = "separate"
+    elif path == "call":
+        prepare_call_path(wl)
+    elif path == "qkvg":
+        prepare_qkvg_path(wl)
+    elif path == "sublayer":
+        prepare_sublayer_path(wl)
+
+
+# The other configurations of the metric, reported beside the config-5 headline at N = 1:
+# the single-sequence and small-batch shapes (configs 1-4) and the reference benchmark's own
+# 16q/4kv x 256 shape (dory640/2048/8192).
+OTHER_CONFIGS = ("config1", "config2", "config3", "config4", "dory640", "dory2048", "dory8192")
+OTHER_STEPS = 400  # timed steps per mode: 0.1-0.6 s of GPU time, several clock samples
+
+
+def measure_other_configs(args, dev) -> dict:
+    """Each other configuration on this GPU: µs per layer-step with plain launches and with
+    programmatic dependent launches (`overlap_launch`), the roofline of the plain launches,
+    the clocks during both and the CPU baseline of the same workload."""
+    out = {}
+    budget = max(1.0, min(3.0, args.cpu_seconds / 5))
+    for name in OTHER_CONFIGS:
+        spec = workload_spec(name)
+        splits, mbps = tuned_splits(name, 1)
+        entry = {"workload": f"{name}: {spec.notes}", "splits": splits,
+                 "min_blocks_per_split": mbps, "layers_per_step": len(spec.layers)}
+        wl = DeviceWorkload(spec, list(spec.lens), dev, spec.seed)
+        steps = -(-OTHER_STEPS // wl.reps) * wl.reps
+        entry.update({"steps": steps, "warmup": args.warmup, "steps_per_replay": wl.reps,
+                      "distinct_pools": wl.num_pools, "l2": l2_note(wl)})
+        seqs = len(spec.lens) * spec.tokens_per_seq
+        for overlap in (False, True):
+            a = argparse.Namespace(splits=splits, min_blocks_per_split=mbps, overlap_launch=overlap)
+            attn = make_attention(wl, a)
+            ms, clocks = time_graph(attn, wl, steps, args.warmup, None, dev)
+            us = ms * 1e3 / len(spec.layers)
+            res = {"us_per_layer_step": round(us, 3), "seqs_per_s": round(seqs / (ms / 1e3), 1),
+                   "hbm_gbs": round(wl.algorithmic_bytes_per_step() / (ms / 1e3) / 1e9, 1),
+                   "roofline": roofline_of(wl, name, us), "clocks": clocks,
+                   "gpu_launches": steps * len(spec.layers)}
+            if overlap:
+                entry["overlap_launch"] = res
+            else:
+                entry.update(res)
+            del attn
+        del wl
+        torch.cuda.empty_cache()
+        entry["cpu_baseline"] = cpu_baseline(name, budget)
+        out[name] = entry
+    return out
+
+
 def l2_note(wl: DeviceWorkload) -> str:
     """How the step's inputs relate to the 126 MB L2 (nothing is flushed between steps)."""
-    touched = wl.pool_bytes * wl.num_pools
-    if wl.pool_bytes > 126e6:
+    if wl.pool_bytes > L2_BYTES:
         return "inputs larger than L2 (each pool > 126 MB; pools cycled per layer)"
-    return (f"inputs larger than L2 in total: {wl.num_pools} distinct pools of "
-            f"{wl.pool_bytes / 1e6:.1f} MB cycled per step ({touched / 1e6:.0f} MB > 126 MB)")
+    per_replay = wl.pool_bytes * min(wl.num_pools, wl.num_layers * wl.reps)
+    return (f"inputs larger than L2: each graph replay ({wl.reps} step(s)) reads "
+            f"{min(wl.num_pools, wl.num_layers * wl.reps)} distinct pools of "
+            f"{wl.pool_bytes / 1e6:.1f} MB ({per_replay / 1e6:.0f} MB > 126 MB)")
 
 
 E2E_CHUNK_BYTES = 1 << 20  # smallest host->device copy of the end-to-end leg
@@ -768,34 +861,24 @@ def read_traffic_ratio(workload: str):
 # CPU baseline / reference arm: the reference semantics in PyTorch eager FP32 on the host
 # ---------------------------------------------------------------------------------------
 
-def cpu_sample(workload: str, lens_all, budget_s: float):
-    """A bounded sample of the workload for the CPU: a spread of sequences of one layer."""
-    lens_sorted = sorted(range(len(lens_all)), key=lambda i: lens_all[i])
-    if workload == "config2":
-        return [lens_all[0]], True
-    if len(lens_all) == 1:
-        return [lens_all[0]], False
-    # evenly spaced by length so the sample's mean matches the workload's
-    k = max(2, min(len(lens_all), 64, int(budget_s * 4)))
-    pick = [lens_sorted[int((i + 0.5) * len(lens_sorted) / k)] for i in range(k)]
-    return [lens_all[i] for i in pick], False
-
-
 class CpuSample:
-    """A bounded sample of the workload on the host CPU: the reference semantics in PyTorch
-    eager FP32 (oracle/dory_oracle.py) over a spread of the workload's sequences.  One pass
-    times one application per distinct sliding window of the step and weights it by the
-    number of applications with that window."""
+    """The workload's CPU pass: the reference semantics in PyTorch eager FP32
+    (oracle/dory_oracle.py) for one attention layer over ALL of the workload's sequences
+    (the wavefront's four tokens for config 2).  One pass times one application per
+    distinct sliding window of the step; the step's time is each application's time
+    weighted by the number of applications with that window (36 full-context layers for
+    configs 3 and 5).  Passes reuse the cache: the append writes the same rows at the same
+    slots every time, so a pass after the first reads exactly what the first read."""
 
-    def __init__(self, workload: str, budget_s: float):
+    def __init__(self, workload: str):
         sys.path.insert(0, str(ROOT / "oracle"))
         import dory_oracle as O
         self.O = O
         self.threads = os.cpu_count() or 1
         torch.set_num_threads(self.threads)
         spec = self.spec = workload_spec(workload)
-        self.lens, shared = cpu_sample(workload, spec.lens, budget_s)
-        self.shared = shared
+        self.lens = list(spec.lens)
+        self.shared = spec.shared
         self.layers = len(spec.layers)
         counts: dict[int, int] = {}
         for layer in spec.layers:
@@ -804,83 +887,102 @@ class CpuSample:
         shape = dict(num_heads=spec.nh, num_kv_heads=spec.nkv, head_dim=spec.hd)
         self.cases = []  # (case, bf16 key, bf16 value, applications per step)
         for w, n in sorted(counts.items()):
-            if shared:
-                case = W.wavefront(seed=1, prompt=self.lens[0], generated=0, tokens=4,
-                                   window=w, **shape)
+            if spec.shared:
+                case = W.wavefront(seed=spec.seed, prompt=self.lens[0], generated=0,
+                                   tokens=spec.tokens_per_seq, window=w, **shape)
+                key, value = case.key.to(torch.bfloat16), case.value.to(torch.bfloat16)
             else:
-                case = W.batched(seed=4, lens=self.lens, window=w, **shape)
-            self.cases.append((case, case.key.to(torch.bfloat16), case.value.to(torch.bfloat16),
-                               n))
+                # caches of several GB (config 5): filled by parallel seeded generators
+                case = W.batched(seed=spec.seed, lens=self.lens, window=w, draw_cache=False,
+                                 **shape)
+                cshape = (case.num_blocks, case.block_size, case.num_kv_heads, case.head_dim)
+                key = W.normal_bf16(cshape, 2 * spec.seed)
+                value = W.normal_bf16(cshape, 2 * spec.seed + 1)
+            self.cases.append((case, key, value, n))
+        self.tokens = self.cases[0][0].tokens
 
-    def once(self) -> float:
-        """Seconds of one whole step, estimated from one timed application per distinct
-        window (the caches restored before each)."""
-        O, total = self.O, 0.0
+    def once(self) -> tuple[float, float]:
+        """(seconds measured for this pass, seconds of the whole step it stands for)."""
+        O, measured, step = self.O, 0.0, 0.0
         for c, key, value, n in self.cases:
-            k, v = key.clone(), value.clone()
             width = c.tables.shape[1]
             t0 = time.perf_counter()
             O.multi_from_raw(c.qk, c.v, c.sqk, c.sqk_factor, O.EPS,
-                             torch.zeros(c.tokens, dtype=torch.int64), k.view(-1), v.view(-1),
-                             tuple(k.shape), k.stride(), c.tables.reshape(-1),
+                             torch.zeros(c.tokens, dtype=torch.int64), key.view(-1),
+                             value.view(-1), tuple(key.shape), key.stride(),
+                             c.tables.reshape(-1),
                              torch.tensor([r * width for r in c.table_rows]), c.seq_lens,
                              c.window, c.scale, c.gate, c.num_heads, c.num_kv_heads,
                              shared_cache=c.shared)
-            total += n * (time.perf_counter() - t0)
-        return total
+            dt = time.perf_counter() - t0
+            measured += dt
+            step += n * dt
+        return measured, step
 
     def seqs_per_s(self, step_seconds: float) -> float:
         """Query tokens served per second (a shared-cache group counts each of its tokens,
         as the GPU arm does)."""
-        return self.cases[0][0].tokens / step_seconds
+        return self.tokens / step_seconds
 
-    def describe(self, step_seconds: float, reps: int) -> str:
+    def describe(self, measured: float, step_seconds: float, reps: int) -> str:
         windows = ", ".join(f"{n} x window {c.window}" if c.window else f"{n} x full context"
                             for c, _, _, n in self.cases)
-        return (f"{len(self.lens)} sequence(s) (ctx {min(self.lens)}..{max(self.lens)}, mean "
-                f"{sum(self.lens) / len(self.lens):.0f}), one application per distinct window "
-                f"scaled to the step's {self.layers} ({windows}), {step_seconds:.3f} s per "
-                f"step, {reps} repetition(s); PyTorch eager FP32 restatement of the reference "
-                "semantics (oracle/dory_oracle.py)")
+        what = (f"{self.tokens} wavefront tokens at {self.lens[0] + 1}.."
+                f"{self.lens[0] + self.tokens}" if self.shared else
+                f"all {len(self.lens)} sequence(s) (ctx {min(self.lens)}..{max(self.lens)}, "
+                f"mean {sum(self.lens) / len(self.lens):.0f})")
+        return (f"{what}: one application per distinct window, {measured:.3f} s per pass, "
+                f"scaled to the step's {self.layers} layer applications ({windows}) = "
+                f"{step_seconds:.3f} s per step, {reps} pass(es); PyTorch eager FP32 "
+                "restatement of the reference semantics (oracle/dory_oracle.py)")
 
 
 def cpu_baseline(workload: str, budget_s: float):
-    """Times the CPU sample, repeating it until `budget_s` seconds have passed."""
-    sample = CpuSample(workload, budget_s)
+    """Times CPU passes of the workload (after one warm-up pass) until `budget_s` seconds
+    have passed (at least one)."""
+    sample = CpuSample(workload)
     sample.once()  # warm-up
-    total, reps = 0.0, 0
-    while total < budget_s or reps == 0:
-        total += sample.once()
+    measured = step = 0.0
+    reps = 0
+    while measured < budget_s or reps == 0:
+        m, st = sample.once()
+        measured += m
+        step += st
         reps += 1
-    dt = total / reps
-    return {"value": round(sample.seqs_per_s(dt), 4), "unit": "seqs/s", "cores": sample.threads,
-            "kind": "port", "sample": sample.describe(dt, reps)}
+    return {"value": round(sample.seqs_per_s(step / reps), 4), "unit": "seqs/s",
+            "cores": sample.threads, "kind": "port",
+            "sample": sample.describe(measured / reps, step / reps, reps)}
 
 
 def bench_reference(args, world, rank, local):
+    """The reference arm: the reference's CPU implementation of the path (its eager PyTorch
+    semantics; the reference's own kernel is Triton GPU code) on the host cores, rank 0
+    only.  A step is one CPU pass (one attention layer over all of the workload's
+    sequences; `ms_per_step` is that measured pass), and the value scales it to the
+    metric's whole step of `layers_per_step` applications."""
     if rank != 0:
         return
     spec = workload_spec(args.workload)
-    lens_all, tps, shared, layers, notes = (spec.lens, spec.tokens_per_seq, spec.shared,
-                                            spec.layers, spec.notes)
-    # each step is one pass of a bounded sample, sized so the whole run takes minutes
-    budget = max(0.05, min(args.cpu_seconds, 120.0 / max(1, args.steps + args.warmup)))
-    sample = CpuSample(args.workload, budget)
+    sample = CpuSample(args.workload)
     for _ in range(args.warmup):
         sample.once()
-    times = [sample.once() for _ in range(args.steps)]
-    dt = statistics.mean(times)
-    value = sample.seqs_per_s(dt)
+    runs = [sample.once() for _ in range(args.steps)]
+    measured = statistics.mean(m for m, _ in runs)
+    step = statistics.mean(st for _, st in runs)
+    value = sample.seqs_per_s(step)
     cpu = {"value": round(value, 4), "unit": "seqs/s", "cores": sample.threads, "kind": "port",
-           "sample": sample.describe(dt, len(times))}
-    total_seqs = len(lens_all) * (tps if shared else 1)
+           "sample": sample.describe(measured, step, len(runs))}
+    total_seqs = sample.tokens
     line = {"impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "seqs/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(total_seqs / value * 1e3, 3) if value else None,
+            "ms_per_step": round(measured * 1e3, 3),
+            "step": "one CPU pass: one attention layer application per distinct window over "
+                    "every sequence of the workload; value = sequences per second of the "
+                    f"whole {len(spec.layers)}-application step ({step:.3f} s)",
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-            "dtype": "f32", "data": "synthetic (seeded), bounded CPU sample",
-            "config": {"workload": f"{args.workload}: {notes}", "global_batch": total_seqs,
-                       "layers_per_step": len(layers)},
+            "dtype": "f32", "data": "synthetic (seeded); the full workload's sequences",
+            "config": {"workload": f"{args.workload}: {spec.notes}", "global_batch": total_seqs,
+                       "layers_per_step": len(spec.layers)},
             "cpu_baseline": cpu,
             "e2e": {"value": round(value, 4), "unit": "seqs/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0},
@@ -915,6 +1017,9 @@ def main() -> int:
                          "(single-sequence workloads; the reference's two-kernel path)")
     ap.add_argument("--sumsq", action="store_true",
                     help="also produce each token's sum of squared outputs (out_sumsq)")
+    ap.add_argument("--all-configs", action=argparse.BooleanOptionalAction, default=True,
+                    help="with the default config5 workload on one GPU, also time configs "
+                         "1-4 and dory640/2048/8192 and report them under \"configs\"")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=15.0)
     ap.add_argument("--profile-steps", type=int, default=0,

@@ -11,6 +11,7 @@ import sys
 from pathlib import Path
 
 import pytest
+import torch
 
 ROOT = Path(__file__).resolve().parent.parent
 sys.path.insert(0, str(ROOT))
@@ -83,12 +84,33 @@ def test_bytes_match_independent_count(window, shared):
 
 
 def test_cpu_sample_weights_windows():
-    sample = bench.CpuSample("dory640", 0.1)
+    sample = bench.CpuSample("dory640")
     weights = {c.window: n for c, _, _, n in sample.cases}
     assert weights == {0: 14, 1024: 42}
     for c, _, _, _ in sample.cases:
         assert (c.num_heads, c.num_kv_heads, c.head_dim) == (16, 4, 256)
-    assert sample.once() > 0
+    measured, step = sample.once()
+    assert 0 < measured < step  # two applications timed, the step's 56 estimated
+
+
+def test_cpu_sample_covers_every_sequence():
+    """The CPU pass runs one layer over ALL of a batched workload's sequences (config 3's
+    64 here; config 5's 512 the same way), and a wavefront's four tokens for config 2."""
+    sample = bench.CpuSample("config3")
+    (case, key, value, n), = sample.cases
+    assert n == 36 and case.tokens == 64 and sample.lens == W.config3_lens()
+    assert key.dtype == torch.bfloat16 and key.shape[0] == case.num_blocks
+    wave = bench.CpuSample("config2")
+    assert wave.tokens == 4 and wave.cases[0][0].shared and wave.cases[0][3] == 20
+
+
+def test_small_workloads_replay_several_steps_over_distinct_pools():
+    """Config 1's 36 caches hold 97 MB, less than L2: a replay then covers enough steps,
+    each over its own pools, to read more than 3 x 126 MB."""
+    spec = bench.workload_spec("config1")
+    pool = -(-(spec.lens[0] + 1) // 16) * 16 * 8 * 128 * 2 * 2
+    reps = -(-int(bench.MIN_REPLAY_BYTES) // (pool * 36))
+    assert reps == 4 and pool * 36 * reps > 3 * 126e6
 
 
 @pytest.mark.parametrize("world", [1, 2, 4, 8])

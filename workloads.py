@@ -20,6 +20,7 @@ Cache layouts (all viewed as [blocks, block_size, kv_heads, head_dim] key/value 
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass, field
 
 import torch
@@ -115,6 +116,30 @@ def _draw_sqk(g: torch.Generator, nh: int, hd: int) -> torch.Tensor:
 def _draw_cache(g: torch.Generator, num_blocks: int, block_size: int, nkv: int, hd: int):
     return (torch.randn(num_blocks, block_size, nkv, hd, generator=g),
             torch.randn(num_blocks, block_size, nkv, hd, generator=g))
+
+
+def normal_bf16(shape, seed: int, threads: int = 0) -> torch.Tensor:
+    """A bf16 tensor of N(0, 1) draws, filled in parallel chunks by NumPy generators spawned
+    from `seed` (reproducible for a given seed and shape, whatever the thread count).  For
+    caches of several GB, where torch.randn's single-threaded CPU generator takes a minute."""
+    import concurrent.futures
+    import numpy as np
+    out = torch.empty(shape, dtype=torch.bfloat16)
+    flat = out.view(-1)
+    n = flat.numel()
+    chunk = 1 << 24
+    pieces = [(i, min(i + chunk, n)) for i in range(0, n, chunk)]
+    seeds = np.random.SeedSequence(seed).spawn(len(pieces))
+
+    def fill(job):
+        (a, b), ss = job
+        x = np.random.default_rng(ss).standard_normal(b - a, dtype=np.float32)
+        flat[a:b].copy_(torch.from_numpy(x))
+
+    workers = threads or (os.cpu_count() or 1)
+    with concurrent.futures.ThreadPoolExecutor(max_workers=workers) as ex:
+        list(ex.map(fill, zip(pieces, seeds)))
+    return out
 
 
 def single(seed: int = 0, context: int = 640, pool_blocks: int = 64, window: int = 0,
