@@ -400,7 +400,8 @@ def make_attention(wl: DeviceWorkload, args):
     return DecodeAttention(wl.nh, wl.nkv, wl.hd, wl.dev, splits=args.splits,
                            max_tokens=max(wl.tokens, 1),
                            min_blocks_per_split=args.min_blocks_per_split,
-                           overlap_launch=getattr(args, "overlap_launch", False))
+                           overlap_launch=getattr(args, "overlap_launch", False),
+                           prefetch_chunks=getattr(args, "prefetch_chunks", 0))
 
 
 def prepare_call_path(wl: DeviceWorkload):
@@ -1015,6 +1016,9 @@ def main() -> int:
                          "beforehand); separate: the q/k normalisation kernel then the "
                          "non-raw call "
                          "(single-sequence workloads; the reference's two-kernel path)")
+    ap.add_argument("--prefetch-chunks", type=int, default=0,
+                    help="L2 prefetch distance ahead of each CTA's ring, in 16-row chunks "
+                         "(0: automatic, < 0: none)")
     ap.add_argument("--sumsq", action="store_true",
                     help="also produce each token's sum of squared outputs (out_sumsq)")
     ap.add_argument("--all-configs", action=argparse.BooleanOptionalAction, default=True,

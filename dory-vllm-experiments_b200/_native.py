@@ -58,7 +58,7 @@ class DoryDecodeParams(ctypes.Structure):
         ("num_tokens", _i32), ("num_heads", _i32), ("num_kv_heads", _i32), ("head_dim", _i32),
         ("block_size", _i32), ("window", _i32), ("splits", _i32), ("blocks_per_tile", _i32),
         ("min_blocks_per_split", _i32), ("max_tokens", _i32), ("sqk_dtype", _i32),
-        ("flags", _u32),
+        ("flags", _u32), ("prefetch_chunks", _i32),
     ]
 
 

@@ -103,6 +103,7 @@ struct alignas(64) KParams {
   int64_t tm_blocks;  // extent of the block dimension of the tensor maps
   float scale, sqk_factor, eps;
   int min_bps, sqk_dtype, overlap;
+  int pf;        // L2 prefetch distance in chunks beyond the ring (0: none)
   int tm_mode;   // 0: no tensor maps; 1: tmk covers K and V (V right after K); 2: tmk, tmv
   CUtensorMap tmk;  // cache views as 5-D tensors (64 dims, rows, 64-dim quarters of a row,
   CUtensorMap tmv;  // KV head, block), one box = a chunk's K (and V) tile, 128-byte swizzle
@@ -217,6 +218,17 @@ __device__ __forceinline__ void tma_load_5d(uint32_t dst, const CUtensorMap* map
       ".L2::cache_hint [%0], [%1, {%2, %3, %4, %5, %6}], [%7], %8;" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4),
       "r"(bar), "l"(policy)
+      : "memory");
+}
+// One box of a tensor map into L2 only (no shared memory, no completion to wait for): the
+// DRAM read of a chunk the ring has no room for yet starts now, and its later copy into
+// shared memory is served from L2.
+__device__ __forceinline__ void tma_prefetch_5d(const CUtensorMap* map, int c0, int c1, int c2,
+                                                int c3, int c4) {
+  asm volatile(
+      "cp.async.bulk.prefetch.tensor.5d.L2.global.tile [%0, {%1, %2, %3, %4, %5}];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(c4)
       : "memory");
 }
 // Programmatic dependent launch: wait for the previous grid on the stream to complete (and
@@ -849,12 +861,25 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   const uint64_t policy = l2_evict_first_policy();
   // Tensor path: arm the chunk's stage and copy its K (and V) tile; one thread.  Records the
   // stage's block id (-1 for an id outside the cache) and chunk index for the consumer.
+  // L2 prefetch of chunk i (tensor path; chunks with a bad block id are skipped).
+  auto prefetch_chunk = [&](int i) {
+    const int c = cb + i;
+    const int blk = div_p2(c, CPB, p.cpb_shift);
+    const int phys = blk - b_first < kTab ? s_tab[blk - b_first] : table[blk];
+    if (phys < 0 || (p.ncache_blocks > 0 && phys >= p.ncache_blocks)) return;
+    const int row0 = mod_p2(c, CPB, p.cpb_shift) * kChunk;
+    const int blkc = int(coff_blocks + phys);
+    tma_prefetch_5d(&p.tmk, 0, row0, 0, kvh, blkc);
+    if (p.tm_mode == 2) tma_prefetch_5d(&p.tmv, 0, row0, 0, kvh, blkc);
+  };
   auto issue_chunk = [&](int i) {
     const int stage = i % NS;
     const int c = cb + i;
     const int blk = div_p2(c, CPB, p.cpb_shift);
     const int phys = blk - b_first < kTab ? s_tab[blk - b_first] : table[blk];
     const bool phys_ok = phys >= 0 && (p.ncache_blocks <= 0 || phys < p.ncache_blocks);
+    // keep the L2 prefetch p.pf chunks ahead of the ring's copies
+    if (i >= NS && p.pf > 0 && i + p.pf < nchunks) prefetch_chunk(i + p.pf);
     meta[stage] = make_int4(phys_ok ? phys : -1, 0, c, 0);
     if (phys_ok) {
       mbar_arrive_expect_tx(full_bar(stage), L::kStageBytes);
@@ -886,6 +911,12 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
       __syncwarp();
       if (lane == 0)
         for (int i = 0; i < NS && i < nchunks; ++i) issue_chunk(i);
+      // The chunks after the ring's first fill, up to p.pf of them, start their DRAM reads
+      // now (into L2), one per lane; later ring refills keep the window p.pf chunks ahead.
+      if (p.pf > 0) {
+        const int pf_end = min(nchunks, NS + p.pf);
+        for (int i = NS + lane; i < pf_end; i += 32) prefetch_chunk(i);
+      }
       __syncwarp();
       grid_launch_dependents();
       return;
@@ -1461,7 +1492,6 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     if (SS) sumsq_tail<false>(p, sv, IPR, nrows, gstart, gcount, G, kvh, tid, s_rowss);
     return;
   }
-
   // ---- cross-split merge by the last CTA of this (group, KV head) to arrive ----
   // The barrier orders every consumer thread's partial stores before thread 0's release
   // add (release is cumulative); its acquire, passed on by the second barrier, makes the
@@ -1959,6 +1989,20 @@ bool cache_tensor_map(const MapKey& k, CUtensorMap* out) {
   return e.ok;
 }
 
+// Streaming multiprocessors of the current device (cached per device ordinal).
+int sm_count() {
+  static int counts[64] = {0};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (!counts[dev]) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n < 1)
+      n = 148;
+    counts[dev] = n;
+  }
+  return counts[dev];
+}
+
 }  // namespace
 
 extern "C" {
@@ -2283,6 +2327,21 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
   kp.multi = multi;
   kp.shared = shared;
   kp.overlap = overlap;
+  // L2 prefetch distance beyond the ring.  Automatic (0): an overlapped launch whose grid is
+  // resident at once (one wave) prefetches every chunk of a CTA's range at the CTA's start,
+  // so the reads it issues before waiting for the previous kernel cover its whole range and
+  // its copies after the wait come from L2 (config 4: 14.5 -> 13.4 us per layer-step).
+  // Plain launches keep to the ring: there the prefetches only queue ahead of the ring's
+  // own copies (config 4: 14.6 -> 16.1 us), as do grids of several waves.
+  {
+    int pf = a.prefetch_chunks;
+    if (pf == 0) {
+      const int per_sm = (HD <= 128 && nt == 1) ? 3 : 1;
+      const long long ctas = (long long)a.splits * a.num_kv_heads * a.num_tokens;
+      pf = overlap && ctas <= (long long)sm_count() * per_sm ? (1 << 20) : -1;
+    }
+    kp.pf = pf > 0 ? pf : 0;
+  }
   kp.q_stride = (raw ? a.num_heads + a.num_kv_heads : a.num_heads) * HD;
   kp.nsub = raw ? (shared ? a.num_tokens : 1) : 0;
   // Tensor maps of the K and V views.  Multi-token calls may shift the cache by whole

@@ -55,12 +55,17 @@ class DecodeAttention:
     the stream, so its prologue and K/V loads overlap that kernel's tail; the kernel right
     before a call must then not write the call's seq_lens, block tables, offsets,
     slot_mapping or the cache rows it attends (q/k/v/gate inputs are still ordered).
+    prefetch_chunks (B200 addition): how far ahead of its shared-memory ring each CTA starts
+    the DRAM reads of its K/V chunks into L2; 0 picks automatically (a CTA's whole range
+    for overlapped launches that fit in one wave of CTAs, else none), a negative value
+    turns it off.
     """
 
     def __init__(self, num_heads: int, num_kv_heads: int, head_dim: int, device: torch.device,
                  splits: int = 32, blocks_per_tile: int = 1, num_warps: int = 4,
                  num_stages: int = 2, dim_chunk: int = 64, max_tokens: int = 1,
-                 min_blocks_per_split: int = 1, overlap_launch: bool = False):
+                 min_blocks_per_split: int = 1, overlap_launch: bool = False,
+                 prefetch_chunks: int = 0):
         if num_heads % num_kv_heads:
             raise ValueError("query heads must be a multiple of KV heads")
         self.num_heads, self.num_kv_heads, self.head_dim = num_heads, num_kv_heads, head_dim
@@ -70,6 +75,7 @@ class DecodeAttention:
         self.max_tokens = max_tokens
         self.min_blocks_per_split = min_blocks_per_split
         self.overlap_launch = bool(overlap_launch)
+        self.prefetch_chunks = int(prefetch_chunks)
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise RuntimeError("DecodeAttention runs on CUDA devices only (no CPU path)")
@@ -240,5 +246,6 @@ class DecodeAttention:
         p.splits, p.blocks_per_tile = self.splits, self.blocks_per_tile
         p.min_blocks_per_split, p.max_tokens = self.min_blocks_per_split, self.max_tokens
         p.flags = flags
+        p.prefetch_chunks = self.prefetch_chunks
         stream = torch.cuda.current_stream(key_cache.device).cuda_stream
         _native.check(self._lib.dory_decode_attention(self._params_ref, stream))

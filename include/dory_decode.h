@@ -121,6 +121,10 @@ typedef struct DoryDecodeParams {
   int32_t max_tokens;             /* scratch capacity in tokens                             */
   int32_t sqk_dtype;              /* DoryDType                                               */
   uint32_t flags;                 /* DORY_FLAG_*                                             */
+  int32_t prefetch_chunks;        /* L2 prefetch distance, in 16-row chunks, ahead of the
+                                   * shared-memory ring of each CTA: 0 = automatic (the whole
+                                   * range for an OVERLAP_LAUNCH call whose grid runs in one
+                                   * wave, else none), < 0 = none, > 0 = that many chunks    */
 } DoryDecodeParams;
 
 /* ABI version of the loaded library (DORY_DECODE_ABI_VERSION). */

@@ -3,7 +3,7 @@
 Each case draws a head shape (head_dim 64/128/256, 1-16 query heads per KV head), a block
 size (16/32/64), a window, a call form (single token through from_raw, a batch with padding
 requests, a shared-cache wavefront of 1-16 tokens), a split setting (splits,
-blocks_per_tile, min_blocks_per_split), a cache layout and, half of the time, NaN in every
+blocks_per_tile, min_blocks_per_split), the L2 prefetch distance, a cache layout and, half of the time, NaN in every
 cache row no token attends.  Outputs must meet the bf16 bar (2e-2 abs / 1e-2 rel) against the oracle and the
 whole pool must be bit for bit the oracle's after the append.
 """
@@ -53,6 +53,10 @@ def draw(seed: int):
                   min_blocks_per_split=rng.choice([1, 1, 4, 32]))
     layout = rng.choice(W.LAYOUTS)
     poison = rng.random() < 0.5
+    # the L2 prefetch distance, from a second stream so the cases above stay those of
+    # earlier sweeps
+    rng2 = random.Random(seed * 7 + 1)
+    launch["prefetch_chunks"] = rng2.choice([0, 0, -1, 1, 3, 1000])
     return case, launch, layout, poison
 
 
