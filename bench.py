@@ -405,18 +405,19 @@ def make_attention(wl: DeviceWorkload, args):
 
 
 def prepare_call_path(wl: DeviceWorkload):
-    """`--path call`: each layer's bf16 query from its raw q/k (the q/k normalisation kernel,
+    """`--path call`: each layer's bf16 queries from its raw q/k (the q/k normalisation kernel,
     which also appends the layer's new k/v), made once before timing; every timed call then
     finds its K/V already in the cache, as the reference's non-raw `__call__` expects."""
     from dory_sublayer_steps import qk_norm_cache
     from dory_decode_attention import EPS
-    wl.q_call = torch.empty(wl.num_layers, 1, wl.nh * wl.hd, dtype=torch.bfloat16, device=wl.dev)
+    wl.q_call = torch.empty(wl.num_layers, wl.tokens, wl.nh * wl.hd, dtype=torch.bfloat16,
+                            device=wl.dev)
     for rep in range(wl.reps):
         for layer in range(wl.num_layers):
             key, value = wl.pool(layer, rep)
-            qk_norm_cache(wl.qk[layer][0], wl.v[layer][0], wl.sqk, W.SQK_FACTOR, EPS,
-                          wl.q_call[layer][0], wl.nh, wl.hd, key_cache=key, value_cache=value,
-                          slot_mapping=wl.slots[0:1])
+            qk_norm_cache(wl.qk[layer], wl.v[layer], wl.sqk, W.SQK_FACTOR, EPS,
+                          wl.q_call[layer], wl.nh, wl.hd, key_cache=key, value_cache=value,
+                          slot_mapping=wl.slots)
     wl.path = "call"
 
 
@@ -486,6 +487,9 @@ def layer_call(attn, wl: DeviceWorkload, app: int, layer: int, ins, out, rep: in
     sumsq = None if wl.sumsq is None else wl.sumsq[layer]
     if wl.path == "call":
         q, gate = ins
+        if hasattr(attn, "call_tokens"):  # a comparison leg that takes all tokens at once
+            attn.call_tokens(q, key, value, window, scale, gate, out)
+            return
         attn(q[0], key, value, wl.tables[0], wl.seq_lens[0:1], window, scale, gate[0], out[0],
              out_sumsq=sumsq)
         return
@@ -992,12 +996,161 @@ def bench_reference(args, world, rank, local):
     print(json.dumps(line), flush=True)
 
 
+# ---------------------------------------------------------------------------------------
+# comparison legs on the same GPU: the reference's own Triton kernel, vLLM's attention
+# ---------------------------------------------------------------------------------------
+
+class ReferenceTriton:
+    """The reference's DecodeAttention (kernels/dory_decode_attention.py:225-331, Triton),
+    installed unmodified under baseline/_ref, behind the layer calls bench.py makes."""
+    overlap_launch = False
+
+    def __init__(self, mod, wl: DeviceWorkload, splits: int):
+        self.a = mod.DecodeAttention(wl.nh, wl.nkv, wl.hd, wl.dev, splits=splits,
+                                     max_tokens=max(wl.tokens, 1))
+
+    def __call__(self, *args, out_sumsq=None):
+        self.a(*args)
+
+    def multi_from_raw(self, *args, out_sumsq=None, **kw):
+        self.a.multi_from_raw(*args, **kw)
+
+    def check_errors(self):
+        pass
+
+
+class VllmUnified:
+    """vLLM's Triton unified attention over the same paged cache, then the gate product:
+    the comparison row of the reference's own benchmark (kernels/bench_decode_attention.py:
+    71-97).  It takes normalised bf16 queries whose k/v are already cached (the non-raw
+    call); a wavefront's tokens are one sequence's causal query block, a batch's tokens one
+    query each."""
+    overlap_launch = False
+    SEGMENTS = 16  # the reference benchmark's NUM_PAR_SOFTMAX_SEGMENTS
+
+    def __init__(self, wl: DeviceWorkload):
+        from vllm.v1.attention.ops.triton_unified_attention import unified_attention
+        self.fn = unified_attention
+        T, dev = wl.tokens, wl.dev
+        self.T, self.nh, self.hd = T, wl.nh, wl.hd
+        f32 = dict(dtype=torch.float32, device=dev)
+        if wl.shared:
+            seqs = 1
+            self.cu = torch.tensor([0, T], dtype=torch.int32, device=dev)
+            self.seqused = wl.seq_lens[-1:].clone()
+            self.max_q = T
+            self.table = wl.tables[0:1]
+        else:
+            seqs = T
+            self.cu = torch.arange(T + 1, dtype=torch.int32, device=dev)
+            self.seqused = wl.seq_lens
+            self.max_q = 1
+            self.table = wl.tables
+        self.max_k = max(wl.seq_lens_list)
+        self.segm_output = torch.empty(T, wl.nh, self.SEGMENTS, wl.hd, **f32)
+        self.segm_max = torch.empty(T, wl.nh, self.SEGMENTS, **f32)
+        self.segm_expsum = torch.empty(T, wl.nh, self.SEGMENTS, **f32)
+        self.descale = torch.ones(seqs, wl.nkv, **f32)
+        self.out = torch.empty(T, wl.nh, wl.hd, dtype=torch.bfloat16, device=dev)
+
+    def call_tokens(self, q, key, value, window, scale, gate, out):
+        self.fn(q=q.view(self.T, self.nh, self.hd), k=key, v=value, out=self.out,
+                cu_seqlens_q=self.cu, max_seqlen_q=self.max_q, seqused_k=self.seqused,
+                max_seqlen_k=self.max_k, softmax_scale=scale, causal=True,
+                window_size=(window - 1, 0) if window else (-1, -1), block_table=self.table,
+                softcap=0, q_descale=None, k_descale=self.descale, v_descale=self.descale,
+                seq_threshold_3D=32, num_par_softmax_segments=self.SEGMENTS,
+                softmax_segm_output=self.segm_output, softmax_segm_max=self.segm_max,
+                softmax_segm_expsum=self.segm_expsum)
+        torch.mul(self.out.view(self.T, -1), gate.view(self.T, -1), out=out.view(self.T, -1))
+
+    def check_errors(self):
+        pass
+
+
+COMPARE_WORKLOADS = ("config1", "config2", "config3", "config4", "config5", "dory640",
+                     "dory2048", "dory8192")
+SINGLE_SEQUENCE = ("config1", "config4", "dory640", "dory2048", "dory8192")
+
+
+def load_reference_triton():
+    """The reference's decode-attention module from baseline/_ref, or (None, why not)."""
+    path = ROOT / "baseline" / "_ref" / "dory_decode_attention.py"
+    if not path.exists():
+        return None, ("baseline/_ref is not installed here (python "
+                      "baseline/install_reference.py, where the reference checkout is)")
+    import importlib.util
+    spec = importlib.util.spec_from_file_location("reference_dory_decode_attention", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod, None
+
+
+def bench_compare(args):
+    """One JSON line per (implementation, workload, path): this build, the reference's own
+    Triton kernel and vLLM's unified attention, each timed as CUDA-graph replays of the
+    same layer sequence over the same pools on one GPU (µs per layer-step, the workload's
+    algorithmic bytes over that time).  Paths: "fused" (raw q/k/v: normalisation, append,
+    attention, gate; multi_from_raw) and "call" (normalised query, k/v cached beforehand;
+    __call__), the latter for the single-sequence workloads, and for vLLM, whose attention
+    has no raw mode, on every workload."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    ref_mod, why = load_reference_triton()
+    names = COMPARE_WORKLOADS if args.workload == "config5" else (args.workload,)
+    impls = ("ours", "triton-reference", "vllm-unified")
+    for name in names:
+        spec = workload_spec(name)
+        splits, mbps = tuned_splits(name, 1)
+        for impl in impls:
+            paths = ["fused", "call"] if name in SINGLE_SEQUENCE else ["fused"]
+            if impl == "vllm-unified":
+                paths = ["call"]
+            for path in paths:
+                line = {"impl": impl, "workload": name, "path": path,
+                        "metric": "us per layer-step", "unit": "us"}
+                if impl == "triton-reference" and ref_mod is None:
+                    line["unavailable"] = why
+                    print(json.dumps(line), flush=True)
+                    continue
+                wl = DeviceWorkload(spec, list(spec.lens), dev, spec.seed)
+                if path == "call":
+                    prepare_call_path(wl)
+                if impl == "ours":
+                    a = argparse.Namespace(splits=splits, min_blocks_per_split=mbps,
+                                           overlap_launch=False, prefetch_chunks=0)
+                    attn = make_attention(wl, a)
+                    line["splits"] = splits
+                elif impl == "triton-reference":
+                    attn = ReferenceTriton(ref_mod, wl, 32)  # the reference's default split count
+                    line["splits"] = 32
+                else:
+                    attn = VllmUnified(wl)
+                    line["segments"] = VllmUnified.SEGMENTS
+                steps = -(-max(50, args.steps) // wl.reps) * wl.reps
+                ms, clocks = time_graph(attn, wl, steps, args.warmup, None, dev)
+                us = ms * 1e3 / len(spec.layers)
+                byts = wl.algorithmic_bytes_per_step() / len(spec.layers)
+                line.update({"value": round(us, 3), "us_per_layer_step": round(us, 3),
+                             "hbm_gbs": round(byts / (us * 1e-6) / 1e9, 1),
+                             "frac_of_measured_peak": round(byts / (us * 1e-6) / 1e9 / load_peaks()[0], 4),
+                             "steps": steps, "layers_per_step": len(spec.layers),
+                             "clocks": clocks})
+                print(json.dumps(line), flush=True)
+                del attn, wl
+                torch.cuda.empty_cache()
+
+
 def main() -> int:
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--impl", choices=("ours", "reference", "compare"), default="ours",
+                    help="reference: the reference semantics on the host CPU (the driver's "
+                         "reference arm); compare: this build, the reference's own Triton "
+                         "kernel (baseline/_ref) and vLLM's unified attention on this GPU, "
+                         "one JSON line each, for every workload (or --workload's)")
     ap.add_argument("--workload", default="config5", choices=WORKLOADS,
                     help="config1..5: the 32q/8kv x 128 configurations; dory640/2048/8192: "
                          "the reference benchmark's 16q/4kv x 256 shape")
@@ -1047,6 +1200,9 @@ def main() -> int:
         bench_profile(args)
     elif args.impl == "reference":
         bench_reference(args, world, rank, local)
+    elif args.impl == "compare":
+        if rank == 0:
+            bench_compare(args)
     else:
         bench_ours(args, world, rank, local)
     return 0

@@ -405,14 +405,14 @@ __device__ __forceinline__ Split split_layout(int lo, int hi, int B, int b_shift
 //    its shared-cache mode caches every token first (:294-301);
 //  * append: the chunk holding a group token's position writes its k/v to the cache
 //    (slot_mapping[0] in single-token calls, read at kernel entry into *s_slot for 256-dim
-//    heads; the table's slot in multi-token calls).
+//    heads; in multi-token calls slot_mapping[t] when given, else the table's slot).
 // Returns whether the stage was written (the caller then fences before tensor copies).
 // ------------------------------------------------------------------------------------
 // CTA constants the slow path needs, kept in shared memory so that the hot loop does not
 // hold them in registers.
 struct CtaInfo {
   long long coff, toff;
-  int lo, hi, kvh, nsub, ibase, gcount, offset_ok;
+  int lo, hi, kvh, nsub, ibase, gcount, offset_ok, tok;
 };
 
 template <int HD>
@@ -461,7 +461,11 @@ __device__ __forceinline__ bool fixup_stage(const KParams& p, uint8_t* kst, uint
     touched = true;
     if (!same || s < ibase || s >= ibase + gcount) continue;  // another CTA appends it
     long long slot;
-    if (p.multi) {
+    if (p.multi && p.slot_mapping) {
+      // the caller's per-token slot (vLLM's slot_mapping); negative: not cached
+      slot = p.slot_mapping[p.shared ? s : ci.tok];
+      if (slot < 0) continue;
+    } else if (p.multi) {
       if (phys < 0) continue;  // its block id was out of range (already recorded)
       slot = (long long)phys * B + mod_p2(pos, B, p.b_shift);
     } else {
@@ -1020,6 +1024,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     s_ci.ibase = ibase;
     s_ci.gcount = gcount;
     s_ci.offset_ok = offset_ok;
+    s_ci.tok = tok;
   }
   // (1) query rows: normalise / scale / round, as the reference, into q2 [ROWS][HD] bf16;
   // (2) new keys / values of the sub tokens: k = bf16(k * inv_norm(k)), v = bf16(v).

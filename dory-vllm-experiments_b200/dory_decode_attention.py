@@ -128,7 +128,8 @@ class DecodeAttention:
                        block_tables: torch.Tensor, block_table_offsets: torch.Tensor,
                        seq_lens: torch.Tensor, window: int, softmax_scale: float,
                        gate: torch.Tensor, out_nibble_major: torch.Tensor,
-                       shared_cache: bool = False, out_sumsq: torch.Tensor | None = None) -> None:
+                       shared_cache: bool = False, out_sumsq: torch.Tensor | None = None,
+                       slot_mapping: torch.Tensor | None = None) -> None:
         """from_raw for T tokens: qk [T, (heads + kv_heads) * head_dim], v [T, kv_heads *
         head_dim], gate [T, heads * head_dim], out_nibble_major [T, 8, heads * head_dim / 8],
         seq_lens [T].  Token t is at position seq_lens[t] - 1 and uses the cache at
@@ -146,13 +147,21 @@ class DecodeAttention:
 
         out_sumsq (optional, all three calls; no counterpart in the reference's signature):
         FP32 [T] receiving sum over e of out[t][e]^2, the gated output's squared norm that
-        the consumer's output GEMV normalises by (dory_attention.py:114-117)."""
+        the consumer's output GEMV normalises by (dory_attention.py:114-117).
+
+        slot_mapping (optional, no counterpart in the reference's signature): int64 [>= T];
+        token t then writes its key and value at slot_mapping[t] instead of the slot its
+        block table gives (a negative slot writes nothing), as vLLM's slot_mapping specifies
+        it, padded rows included."""
         tokens = qk.shape[0]
         if (tokens > self.max_tokens or cache_offsets.dtype != torch.int64
                 or block_table_offsets.dtype != torch.int64):
             raise ValueError("too many tokens for the scratch buffers, or non-int64 offsets")
+        if slot_mapping is not None and (slot_mapping.numel() < tokens
+                                         or not slot_mapping.is_contiguous()):
+            raise ValueError("slot_mapping needs one contiguous int64 entry per token")
         self._launch(qk, key_cache, value_cache, block_tables, seq_lens, window, softmax_scale,
-                     gate, out_nibble_major, raw=(v, sqk, sqk_factor, eps, None),
+                     gate, out_nibble_major, raw=(v, sqk, sqk_factor, eps, slot_mapping),
                      tokens=tokens, cache_offsets=cache_offsets,
                      block_table_offsets=block_table_offsets, shared=shared_cache,
                      out_sumsq=out_sumsq)

@@ -17,9 +17,9 @@ does that step for a decode batch:
   one layer from the metadata's `seq_lens` (int32 [num_reqs], the new token included) and
   `block_table` (int32 [num_reqs, max_blocks], a row per request) as
   DecodeAttention.multi_from_raw, token t = request t.  The new token's k / v go to the
-  slot its block table gives at seq_len - 1, which is how vLLM builds `slot_mapping` for a
-  decode token (block_table[t, pos // block_size] * block_size + pos % block_size); padded
-  requests (seq_len 0, slot -1 in vLLM's CUDA-graph padding) write nothing and output zero.
+  slot the metadata's `slot_mapping` (int64 [num_tokens]) gives, as vLLM's backends write
+  the cache (`reshape_and_cache`): a negative slot writes nothing; padded requests (seq_len
+  0, slot -1 in vLLM's CUDA-graph padding) write nothing and output zero.
 
 Only decode batches (max_query_len == 1) are taken: prefill stays on vLLM's attention, as in
 the reference.  vLLM itself is not imported: the metadata is read by attribute.  Row
@@ -81,8 +81,12 @@ class VllmDecodeBinding:
             raise ValueError("metadata covers fewer requests than qk has rows")
         if table.dim() != 2 or table.stride(1) != 1:
             raise ValueError("block_table must be [num_reqs, max_blocks] with unit last stride")
+        slots = metadata.slot_mapping
+        if slots.dtype != torch.int64 or slots.numel() < tokens:
+            raise ValueError("slot_mapping must be int64 with one entry per token")
         a = self.attention
         key, value = kv_cache_views(kv_cache, a.num_kv_heads, a.head_dim)
         a.multi_from_raw(qk, v, sqk, sqk_factor, eps, self._cache_offsets[:tokens], key, value,
                          table, self._rows(table.stride(0))[:tokens], seq_lens[:tokens], window,
-                         softmax_scale, gate, out_nibble_major, out_sumsq=out_sumsq)
+                         softmax_scale, gate, out_nibble_major, out_sumsq=out_sumsq,
+                         slot_mapping=slots[:tokens])

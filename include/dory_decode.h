@@ -84,7 +84,12 @@ typedef struct DoryDecodeParams {
   const void* q;
   const float* v;                 /* RAW_QKV: FP32 [T, NKV * HD]                          */
   const void* sqk;                /* RAW_QKV: [NH * HD] of sqk_dtype                        */
-  const int64_t* slot_mapping;    /* RAW_QKV single-token: int64 [1]; < 0 = padding, no write */
+  const int64_t* slot_mapping;    /* RAW_QKV single-token: int64 [1]; < 0 = padding, no write.
+                                   * RAW_QKV | MULTI_TOKEN: optional int64 [T] (NULL: each
+                                   * token's slot is its block table's at seq_len - 1); token t
+                                   * appends at slot_mapping[t], < 0 = no write (vLLM's
+                                   * slot_mapping, padded rows -1).  No counterpart in the
+                                   * reference's multi_from_raw.                              */
   void* key_cache;                /* BF16 view [num_cache_blocks, block_size, NKV, HD]      */
   void* value_cache;              /* same strides as key_cache, unit last stride            */
   const int32_t* block_table;     /* int32; the sequence's row (single) or the table base   */

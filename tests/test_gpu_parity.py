@@ -388,3 +388,22 @@ def test_normalised_query_equals_reference_bits_but_one():
             assert np.array_equal(k_out.view(torch.int16).cpu().numpy().reshape(g["k_new"][t].shape),
                                   g["k_new"][t]), (name, t)
     assert diffs == QUERY_DIFFERENCES, diffs
+
+
+@pytest.mark.parametrize("name", ["batched", "wavefront", "wavefront_window"])
+def test_multi_token_slot_mapping_equal_to_table_slots_changes_nothing(name):
+    """multi_from_raw(slot_mapping=...) with the slots the block tables give: the same output
+    and cache bits as without it (batched and shared-cache calls)."""
+    case = CASES[name]()
+    out_a, d_a, _ = run(case, "triton")
+    d = W.to_device(case, "triton", "cuda")
+    attn = DecodeAttention(case.num_heads, case.num_kv_heads, case.head_dim,
+                           torch.device("cuda"), splits=32, max_tokens=case.tokens)
+    attn.multi_from_raw(d["qk"], d["v"], d["sqk"], case.sqk_factor, EPS, d["cache_offsets"],
+                        d["key"], d["value"], d["tables"], d["table_offsets"], d["seq_lens"],
+                        case.window, case.scale, d["gate"], d["out"], shared_cache=case.shared,
+                        slot_mapping=d["slots"])
+    torch.cuda.synchronize()
+    attn.check_errors()
+    assert torch.equal(d["out"].cpu(), out_a)
+    assert torch.equal(d["raw"].cpu().view(torch.int16), d_a["raw"].cpu().view(torch.int16))

@@ -145,3 +145,44 @@ def test_graph_capture_after_first_call():
     torch.cuda.synchronize()
     assert torch.equal(out, eager)
     attn.check_errors()
+
+
+def test_slot_mapping_decides_where_rows_go():
+    """The metadata's slot_mapping, not the block table, says where each new row is cached:
+    a request whose slot points into a block no table uses gets its row there, a request
+    with slot -1 writes nothing, a padded row writes nothing.  Attention is unchanged (each
+    token uses its new key and value at its own position either way)."""
+    case = W.batched(seed=964, lens=[300, 40, 777], pool_factor=1.5)
+    kv, meta, slots = vllm_batch(case, "vllm", padded=1)
+    B, T = case.block_size, case.tokens
+    used = set(case.tables.flatten().tolist())
+    spare = next(b for b in range(case.num_blocks) if b not in used)
+    custom = list(slots)
+    custom[0] = spare * B + 5  # request 0: a row of an unused block
+    custom[1] = -1             # request 1: not cached
+    meta.slot_mapping = torch.tensor(custom, dtype=torch.int64, device=DEV)
+    before = kv.clone()
+    NH, NKV, HD = case.num_heads, case.num_kv_heads, case.head_dim
+    pad = lambda x, n: torch.cat([x, torch.zeros(1, n)])  # noqa: E731
+    qk = pad(case.qk, (NH + NKV) * HD).contiguous().to(DEV)
+    v = pad(case.v, NKV * HD).contiguous().to(DEV)
+    gate = pad(case.gate, NH * HD).contiguous().to(DEV)
+    out = torch.full((T + 1, 8, NH * HD // 8), float("nan"), device=DEV)
+    attn = DecodeAttention(NH, NKV, HD, DEV, splits=8, max_tokens=8)
+    VllmDecodeBinding(attn).decode(meta, kv, qk, v, case.sqk.to(DEV), case.sqk_factor, EPS,
+                                   case.window, case.scale, gate, out)
+    torch.cuda.synchronize()
+    attn.check_errors()
+    assert_close(out[:T].cpu(), oracle_out(case))
+    assert torch.equal(out[T:].cpu(), torch.zeros_like(out[T:].cpu()))
+    key_b, val_b = kv_cache_views(before.cpu(), NKV, HD)
+    key_a, val_a = kv_cache_views(kv.cpu(), NKV, HD)
+    changed = (key_a != key_b).any(-1).any(-1) | (val_a != val_b).any(-1).any(-1)
+    rows = oracle_rows(case)
+    expect = torch.zeros_like(changed)
+    for t in (0, 2):
+        s = custom[t]
+        expect[s // B, s % B] = True
+        assert torch.equal(key_a[s // B, s % B].view(torch.int16), rows[t][0].view(torch.int16))
+        assert torch.equal(val_a[s // B, s % B].view(torch.int16), rows[t][1].view(torch.int16))
+    assert not (changed & ~expect).any()  # request 1's table slot and the padded row: untouched
