@@ -269,6 +269,14 @@ __device__ __forceinline__ void prefetch_range(const void* ptr, int bytes, int l
 __device__ __forceinline__ void named_barrier_consumers() {
   asm volatile("bar.sync 1, %0;" ::"n"(kConsumerWarps * 32) : "memory");
 }
+// Barrier 2: the producer warp announces that the pipeline's mbarriers are initialised
+// (arrive, no wait); the consumer warps wait for it before their first stage.
+__device__ __forceinline__ void pipeline_ready_arrive() {
+  asm volatile("bar.arrive 2, %0;" ::"n"(kThreads) : "memory");
+}
+__device__ __forceinline__ void pipeline_ready_wait() {
+  asm volatile("bar.sync 2, %0;" ::"n"(kThreads) : "memory");
+}
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& a0, uint32_t& a1, uint32_t& a2,
                                         uint32_t& a3) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
@@ -708,7 +716,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   // Per-token info, indexed by token for shared-cache calls and by 0 otherwise.
   __shared__ int s_len[kMaxSub], s_phys[kMaxSub];
   __shared__ long long s_coff[kMaxSub], s_toff[kMaxSub];
-  __shared__ int s_grouped, s_last;
+  __shared__ int s_grouped, s_last, s_fail;
   // 256-dim heads: edge stages read a zero row in place of each V row outside the attended
   // range (pv_accumulate), and a single-token call's slot is read at entry.  Narrower heads
   // keep the zeroing slow path: that code measured faster for them.
@@ -760,7 +768,10 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
       if (p.tm_mode == 2) prefetch_tensormap(&p.tmv);
     }
   }
-  if (tid == 0) s_grouped = 1;
+  if (tid == 0) {
+    s_grouped = 1;
+    s_fail = 0;
+  }
   if (tid < ninfo) {
     const int t = p.shared ? tid : tok;
     s_len[tid] = p.seq_lens[t];
@@ -851,16 +862,6 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   const long long coff_blocks = coff == 0 ? 0 : (coff % p.sb == 0 ? coff / p.sb : -1);
   const bool use_tma = p.tm_mode != 0 && offset_ok && coff_blocks >= 0 &&
                        coff_blocks + p.ncache_blocks <= p.tm_blocks;
-  if (tid == 0) {
-    for (int s = 0; s < NS; ++s) {
-      // tensor path: the producer's arrive.expect_tx; copy path: 32 lanes' completions + 1
-      mbar_init(full_bar(s), use_tma ? 1 : 33);
-      mbar_init(empty_bar(s), 1);  // the consumer warp that read the stage
-    }
-    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-    if (!offset_ok) record_error(p.err, DORY_DEVERR_OFFSET_ALIGN);
-  }
-  __syncthreads();
 
   const uint64_t policy = l2_evict_first_policy();
   // Tensor path: arm the chunk's stage and copy its K (and V) tile; one thread.  Records the
@@ -901,6 +902,20 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
 
   if (warp == kConsumerWarps) {
     // =============================== producer warp ===============================
+    // The pipeline's barriers are set up here, not by the whole CTA: the consumer warps go
+    // straight on to their query rows (below) while this warp reads the block ids and
+    // issues the first copies, and wait for the set-up only before their first stage.
+    if (lane == 0) {
+      for (int s = 0; s < NS; ++s) {
+        // tensor path: the producer's arrive.expect_tx; copy path: 32 lanes' completions + 1
+        mbar_init(full_bar(s), use_tma ? 1 : 33);
+        mbar_init(empty_bar(s), 1);  // the consumer warp that read the stage
+      }
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+      if (!offset_ok) record_error(p.err, DORY_DEVERR_OFFSET_ALIGN);
+    }
+    __syncwarp();
+    pipeline_ready_arrive();
     // Tensor path (the usual one): lane 0 publishes the stage's block id, arms full[stage]
     // with the stage's byte count and issues one box copy of the chunk's K and V tiles
     // (two, K then V, when V does not directly follow K in memory): 16 rows from row 0 of
@@ -1240,6 +1255,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     }
   }
   named_barrier_consumers();
+  pipeline_ready_wait();  // the producer has initialised the stages' barriers
 
   // (4) B fragments of Q^T (k = dims, n = query rows), resident for the whole loop.
   const int g = lane >> 2;
@@ -1407,20 +1423,23 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
       l[nt][i] = v;
     }
 
+  if (failed && lane == 0) s_fail = 1;
   grid_launch_dependents();  // streaming is done: the next grid may start its prologue
-  // Drain: every copy this CTA issued must have landed before its shared memory is reused
-  // or released (only matters after a timeout; otherwise these waits return at once).
   named_barrier_consumers();
-  if (tid == 0) {
-    bool drained = true;
-    for (int s = 0; s < NS && s < nchunks; ++s) {
-      const int last = s + ((nchunks - 1 - s) / NS) * NS;
-      if (!mbar_wait(full_bar(s), (last / NS) & 1)) drained = false;
+  // Every chunk this CTA copied has been waited for by its consumer warp unless a wait gave
+  // up; only then can copies still be in flight, and they must land before the ring's
+  // shared memory is reused or released (the drain's waits are bounded too).
+  if (s_fail) {
+    if (tid == 0) {
+      bool drained = true;
+      for (int s = 0; s < NS && s < nchunks; ++s) {
+        const int last = s + ((nchunks - 1 - s) / NS) * NS;
+        if (!mbar_wait(full_bar(s), (last / NS) & 1)) drained = false;
+      }
+      if (!drained) record_error(p.err, DORY_DEVERR_WAIT_TIMEOUT);
     }
-    if (!drained) record_error(p.err, DORY_DEVERR_WAIT_TIMEOUT);
+    named_barrier_consumers();
   }
-  (void)failed;
-  named_barrier_consumers();
 
   // ---- merge the four consumer warps (shared memory, aliasing the drained ring) ----
   constexpr int OST = HD + 4;  // padded row stride of the per-warp O buffers (floats)
