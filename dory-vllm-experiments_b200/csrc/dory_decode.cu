@@ -701,7 +701,7 @@ __device__ __forceinline__ void sumsq_tail(const KParams& p, const float* sv, in
 // ------------------------------------------------------------------------------------
 // The kernel.  grid = (splits, NKV, T); block = 160 threads (4 consumer warps + producer).
 // ------------------------------------------------------------------------------------
-template <int HD, int NT, int NS, bool SS>
+template <int HD, int NT, int NS, bool SS, bool DM>
 __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     decode_kernel(const __grid_constant__ KParams p) {
   using L = Smem<HD, NS>;
@@ -1516,20 +1516,49 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     if (SS) sumsq_tail<false>(p, sv, IPR, nrows, gstart, gcount, G, kvh, tid, s_rowss);
     return;
   }
-  // ---- cross-split merge by the last CTA of this (group, KV head) to arrive ----
+  // ---- cross-split merge of this (group, KV head) ----
   // The barrier orders every consumer thread's partial stores before thread 0's release
-  // add (release is cumulative); its acquire, passed on by the second barrier, makes the
-  // other CTAs' partials visible to this CTA when it is the last.
+  // (release is cumulative).
   named_barrier_consumers();
-  if (tid == 0) {
+  if constexpr (DM) {
+    // One wave (every CTA of the grid resident at once): the last active split, which
+    // holds the newest positions and usually finishes last, merges.  The others publish
+    // their partials with a release add that they do not wait for, and exit; the merger
+    // waits (bounded) for all of them with acquire loads, then resets the counter for the
+    // next launch.  Its poll typically finds them done: no round trip of its own atomic.
     int32_t* counter = p.counters + gstart * p.NKV + kvh;
-    int prev;
-    asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(prev) : "l"(counter) : "memory");
-    s_last = (prev == sp.active - 1);
-    if (s_last) *counter = 0;  // self-reset for the next launch
+    if (split != sp.active - 1) {
+      if (tid == 0) asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(counter) : "memory");
+      return;
+    }
+    if (tid == 0) {
+      int seen = 0;
+      long long start = 0;
+      for (;;) {
+        asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(seen) : "l"(counter) : "memory");
+        if (seen >= sp.active - 1) break;
+        if (start == 0) start = clock64();
+        else if (clock64() - start > kWaitLimitCycles) {
+          record_error(p.err, DORY_DEVERR_WAIT_TIMEOUT);
+          break;
+        }
+      }
+      *counter = 0;  // for the next launch (stream order puts it after this grid)
+    }
+    named_barrier_consumers();
+  } else {
+    // Several waves: the last CTA of this (group, KV head) to arrive merges; its acquire,
+    // passed on by the second barrier, makes the other CTAs' partials visible to it.
+    if (tid == 0) {
+      int32_t* counter = p.counters + gstart * p.NKV + kvh;
+      int prev;
+      asm volatile("atom.add.acq_rel.gpu.s32 %0, [%1], 1;" : "=r"(prev) : "l"(counter) : "memory");
+      s_last = (prev == sp.active - 1);
+      if (s_last) *counter = 0;  // self-reset for the next launch
+    }
+    named_barrier_consumers();
+    if (!s_last) return;
   }
-  named_barrier_consumers();
-  if (!s_last) return;
   // Merge over the splits in registers, per (row, 4 dims) unit: batches of SB splits whose
   // (max, sum) and partial outputs are all in flight together (one L2 round trip per
   // batch; the gate rides along the first), each batch folded in with one max, independent
@@ -1879,9 +1908,9 @@ int32_t fail(int32_t status, const char* fmt, ...) {
   return status;
 }
 
-template <int HD, int NT, int NS, bool SS>
+template <int HD, int NT, int NS, bool SS, bool DM>
 int32_t launch(const KParams& kp, dim3 grid, int smem_bytes, cudaStream_t stream) {
-  auto fn = decode_kernel<HD, NT, NS, SS>;
+  auto fn = decode_kernel<HD, NT, NS, SS, DM>;
   static int configured[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return fail(DORY_ERR_CUDA, "cudaGetDevice failed");
@@ -1910,6 +1939,36 @@ int32_t launch(const KParams& kp, dim3 grid, int smem_bytes, cudaStream_t stream
   return DORY_OK;
 }
 
+int sm_count();
+
+// Whether `grid` CTAs of `fn` with `smem` bytes of dynamic shared memory are all resident
+// at once on the current device (occupancy per SM x SMs), cached per kernel and size.
+template <typename F>
+bool one_wave(F fn, dim3 grid, int smem) {
+  struct Entry {
+    const void* fn;
+    int dev, smem, per_sm;
+  };
+  static Entry cache[64];
+  static int used = 0;
+  static std::mutex mu;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  const long long ctas = (long long)grid.x * grid.y * grid.z;
+  std::lock_guard<std::mutex> lock(mu);
+  for (int i = 0; i < used; ++i)
+    if (cache[i].fn == (const void*)fn && cache[i].dev == dev && cache[i].smem == smem)
+      return ctas <= (long long)cache[i].per_sm * sm_count();
+  int per_sm = 0;
+  if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           Smem<256, 8>::bytes(kMaxSub)) != cudaSuccess ||
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, smem) != cudaSuccess)
+    per_sm = 0;
+  cudaGetLastError();
+  if (used < 64) cache[used++] = Entry{(const void*)fn, dev, smem, per_sm};
+  return ctas <= (long long)per_sm * sm_count();
+}
+
 // Ring stages per instantiation: a multiple of the four consumer warps, so every stage keeps
 // one consumer, which refills it; two stages per warp let each warp compute one chunk while
 // its next one is in flight (64 KB of ring for 128-dim heads at 3 CTAs/SM; 128 KB for
@@ -1928,10 +1987,18 @@ int32_t dispatch(const KParams& kp, dim3 grid, cudaStream_t stream) {
   constexpr int NS = Depth<HD, NT>::value;
   static_assert(kConsumerWarps * NT * 8 * (HD + 4) * 4 <= NS * Smem<HD, NS>::kStageBytes,
                 "the warps' merge buffer must fit in the ring");
+  const int smem = Smem<HD, NS>::bytes(kp.nsub);
+  // The designated merger waits for the other splits of its (group, KV head) to finish:
+  // only when every CTA of the grid is resident at once, so that none of them can be
+  // waiting for a slot the merger holds.
+  const bool dm = one_wave(decode_kernel<HD, NT, NS, false, true>, grid, smem);
   // The sum-of-squares epilogue is a separate instantiation: compiled in, even unused, it
   // measured ~0.5 us slower on single-sequence calls.
-  if (kp.sumsq) return launch<HD, NT, NS, true>(kp, grid, Smem<HD, NS>::bytes(kp.nsub), stream);
-  return launch<HD, NT, NS, false>(kp, grid, Smem<HD, NS>::bytes(kp.nsub), stream);
+  if (kp.sumsq)
+    return dm ? launch<HD, NT, NS, true, true>(kp, grid, smem, stream)
+              : launch<HD, NT, NS, true, false>(kp, grid, smem, stream);
+  return dm ? launch<HD, NT, NS, false, true>(kp, grid, smem, stream)
+            : launch<HD, NT, NS, false, false>(kp, grid, smem, stream);
 }
 
 template <int HD>
