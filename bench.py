@@ -743,8 +743,71 @@ def measure_other_configs(args, dev) -> dict:
         del wl
         torch.cuda.empty_cache()
         entry["cpu_baseline"] = cpu_baseline(name, budget)
+        if name == "config2":
+            entry["wavefront_step"] = measure_wavefront_step(args, dev)
         out[name] = entry
     return out
+
+
+def measure_wavefront_step(args, dev, layers: int = 20) -> dict:
+    """A whole wavefront step of the recurrent block's attention sublayers at configuration
+    2's shape, replayed as one CUDA graph (WavefrontRecurrentBlock): for each of the 20
+    recurrent attention layers, the q/k/v/gate epilogue on seeded GEMV partials, the four
+    rows' multi_from_raw on the layer's shared "last_loop" cache (loop pattern 3, 2, 1, 0)
+    with the output statistic, and the residual update fed it (the NVFP4 GEMVs between
+    them are not part of this build; their split-K partials are the seeded inputs).  Each
+    layer reads its own 11 MB cache, 220 MB per step, more than L2."""
+    from dory_decode_attention import EPS, DecodeAttention
+    from wavefront_binding import AttentionSublayer, WavefrontLayer, WavefrontRecurrentBlock
+    spec = workload_spec("config2")
+    rows, position = spec.tokens_per_seq, spec.lens[0]
+    need = -(-(position + rows) // BLOCK)
+    gd = torch.Generator(device=dev).manual_seed(2027)
+    table = torch.randperm(need + 8, device=dev, generator=gd)[:need].to(torch.int32)[None]
+    cos_sin = torch.randn(position + rows + 4, HD, device=dev, generator=gd)
+    subs = []
+    for _ in range(layers):
+        kv = torch.empty(need + 8, NKV, BLOCK, 2 * HD, dtype=torch.bfloat16, device=dev)
+        kv.normal_(generator=gd)
+        subs.append(AttentionSublayer(
+            WavefrontLayer([kv] * rows, [0] * rows, table.shape[1], NKV, HD),
+            (torch.rand(NH * HD, device=dev, generator=gd) + 0.5).to(torch.bfloat16),
+            (torch.rand(NH * HD, device=dev, generator=gd) + 0.5).to(torch.bfloat16), cos_sin,
+            (torch.randn(NH * HD, device=dev, generator=gd) * 0.02).to(torch.bfloat16), 0,
+            HD ** -0.5))
+    splits, mbps = tuned_splits("config2", 1)
+    attn = DecodeAttention(NH, NKV, HD, dev, splits=splits, max_tokens=rows,
+                           min_blocks_per_split=mbps)
+    block = WavefrontRecurrentBlock(attn, subs, table, NH * HD, W.SQK_FACTOR, 0.9, 2.5, EPS)
+    for i in range(layers):
+        block.qkvg_partials(i, rows).normal_(generator=gd)
+        block.out_partials(i, rows).normal_(generator=gd)
+    positions = torch.arange(position, position + rows, dtype=torch.int64, device=dev)
+    seq_lens = (positions + 1).to(torch.int32)
+    h_in = torch.randn(rows, NH * HD, device=dev, generator=gd).to(torch.bfloat16)
+    block.replay(rows, positions, seq_lens, h_in)  # plain launches, then the capture
+    for _ in range(args.warmup):
+        block.replay(rows, positions, seq_lens, h_in)
+    steps = OTHER_STEPS
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(dev) as clocks:
+        start.record()
+        for _ in range(steps):
+            block.replay(rows, positions, seq_lens, h_in)
+        end.record()
+        torch.cuda.synchronize(dev)
+    attn.check_errors()
+    us = start.elapsed_time(end) * 1e3 / steps
+    lens = [position + t + 1 for t in range(rows)]
+    per_layer = algorithmic_bytes(lens, True, 0, NH, NKV, HD, QKVG_SPLIT_K, NH * HD)
+    return {"what": "20 recurrent attention sublayers of one wavefront step (4 rows at loop "
+                    "depths 3..0, positions 2710..2713): q/k/v/gate epilogue, multi_from_raw "
+                    "on the shared cache with the output statistic, residual update; one CUDA "
+                    "graph, GEMV partials seeded",
+            "us_per_wavefront_step": round(us, 3), "us_per_layer": round(us / layers, 3),
+            "launches_per_step": 3 * layers, "steps": steps,
+            "hbm_gbs": round(per_layer * layers / (us * 1e-6) / 1e9, 1), "clocks": clocks.summary()}
 
 
 def l2_note(wl: DeviceWorkload) -> str:

@@ -24,6 +24,9 @@ module is that binding on this build:
 * `entry_slots(block_tables, position, block_size)`: the slot of a new token at `position`
   in each block table, as `_enter` computes it for its single-token `from_raw` calls
   (:372-374).
+* `WavefrontRecurrentBlock`: every non-GEMM step of the recurrent block's attention
+  sublayers for a k-row call (`_recurrent` / `_multi_block`, :405-432), the GEMVs' split-K
+  partials given, launched plainly or replayed as one CUDA graph per k (`_run`, :336-347).
 """
 
 from __future__ import annotations
@@ -143,5 +146,111 @@ def entry_slots(block_tables: torch.Tensor, position: torch.Tensor, block_size: 
     return slots
 
 
+class AttentionSublayer:
+    """One attention layer of the recurrent block: its bound caches (WavefrontLayer) and the
+    per-layer inputs of the non-GEMM steps of `MultiTokenSublayers.attention`
+    (kernels/dory_multi_token.py:183-210): sqk for the q normalisation, s_gate and the
+    rotary cos/sin table for the q/k/v/gate epilogue, alpha for the residual update, and the
+    layer's window and softmax scale."""
+
+    def __init__(self, layer: WavefrontLayer, sqk: torch.Tensor, s_gate: torch.Tensor,
+                 cos_sin: torch.Tensor, alpha: torch.Tensor, window: int, softmax_scale: float):
+        self.layer, self.sqk, self.s_gate, self.cos_sin = layer, sqk, s_gate, cos_sin
+        self.alpha, self.window, self.softmax_scale = alpha, int(window), float(softmax_scale)
+
+
+class WavefrontRecurrentBlock:
+    """The attention sublayers of the wavefront engine's recurrent block for one k-row call
+    (`_recurrent` / `_multi_block`, kernels/dory_wavefront_engine.py:405-432): for every
+    attention layer in order, the q/k/v/gate epilogue on the layer's q/k/v/gate GEMV
+    partials, the rows' multi_from_raw at loop pattern (k - 1, ..., 0) with the output's
+    sum of squares, and the residual update on the layer's output-GEMV partials fed that
+    statistic; each layer's h is the next layer's residual input (ping-pong buffers).
+
+    The two GEMVs of each sublayer (NVFP4, outside this build) are the caller's: it writes
+    their split-K partials into `qkvg_partials(i, k)` / `out_partials(i, k)` (the engine's
+    prefix views, [split_k, k, rows]) before a call.  `run(k, ...)` launches the block;
+    `replay(k, ...)` runs it as one CUDA graph per k, the first call for a k running it
+    plainly and then capturing it (`_run`, :336-347).  shared_cache: the recurrent layers'
+    "last_loop" caches (one per layer, written and read by every loop)."""
+
+    def __init__(self, attention: DecodeAttention, layers: list[AttentionSublayer],
+                 block_tables: torch.Tensor, hidden: int, sqk_factor: float,
+                 s_gate_factor: float, alpha_scale: float, eps: float,
+                 shared_cache: bool = True, qkvg_split_k: int = 2, out_split_k: int = 4):
+        a = attention
+        self.wave = WavefrontAttention(a)
+        self.layers, self.block_tables = layers, block_tables
+        self.NH, self.NKV, self.HD = a.num_heads, a.num_kv_heads, a.head_dim
+        self.hidden, self.sqk_factor, self.s_gate_factor = hidden, sqk_factor, s_gate_factor
+        self.alpha_scale, self.eps, self.shared_cache = alpha_scale, eps, shared_cache
+        self.qkvg_split_k, self.out_split_k = qkvg_split_k, out_split_k
+        rows, dev = a.max_tokens, a.device
+        Q, KV = self.NH * self.HD, self.NKV * self.HD
+        self.qkvg_rows = 2 * (Q + KV)
+        f32 = dict(dtype=torch.float32, device=dev)
+        self._qkvg = [torch.zeros(qkvg_split_k * rows * self.qkvg_rows, **f32) for _ in layers]
+        self._out = [torch.zeros(out_split_k * rows * hidden, **f32) for _ in layers]
+        self.qk = torch.empty(rows, Q + KV, **f32)
+        self.v = torch.empty(rows, KV, **f32)
+        self.gate = torch.empty(rows, Q, **f32)
+        self.attention_out = torch.empty(rows, 8, Q // 8, **f32)
+        self.sumsq = torch.empty(rows, **f32)
+        self.h = [torch.empty(rows, hidden, dtype=torch.bfloat16, device=dev) for _ in range(2)]
+        self.h_nm = [torch.empty(rows, 8, hidden // 8, **f32) for _ in range(2)]
+        self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+
+    def qkvg_partials(self, i: int, k: int) -> torch.Tensor:
+        """Layer i's q/k/v/gate GEMV partials for a k-row call, FP32 [split_k, k, rows]."""
+        n = self.qkvg_split_k * k * self.qkvg_rows
+        return self._qkvg[i][:n].view(self.qkvg_split_k, k, self.qkvg_rows)
+
+    def out_partials(self, i: int, k: int) -> torch.Tensor:
+        """Layer i's output-GEMV partials for a k-row call, FP32 [split_k, k, hidden]."""
+        n = self.out_split_k * k * self.hidden
+        return self._out[i][:n].view(self.out_split_k, k, self.hidden)
+
+    def run(self, k: int, positions: torch.Tensor, seq_lens: torch.Tensor,
+            h_in: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """The block for rows 0 .. k-1 (row t at loop k - 1 - t; positions int64 [k],
+        seq_lens int32 [k] = positions + 1) from the block input h_in (BF16 [k, hidden]);
+        returns the last layer's h (BF16 [k, hidden]) and its nibble-major FP32 copy."""
+        from dory_sublayer_steps import qkvg_epilogue, residual_tokens
+        pattern = recurrent_pattern(k)
+        overlap = self.wave.attention.overlap_launch
+        x = h_in
+        out = nm = None
+        for i, sub in enumerate(self.layers):
+            qkvg_epilogue(self.qkvg_partials(i, k), positions[:k], sub.cos_sin, sub.s_gate,
+                          self.s_gate_factor, self.qk[:k], self.v[:k], self.gate[:k], self.NH,
+                          self.NKV, self.HD, overlap_launch=overlap)
+            self.wave.attention_call(sub.layer, pattern, self.qk[:k], self.v[:k], sub.sqk,
+                                     self.sqk_factor, self.eps, self.block_tables, seq_lens[:k],
+                                     sub.window, sub.softmax_scale, self.gate[:k],
+                                     self.attention_out[:k], shared_cache=self.shared_cache,
+                                     out_sumsq=self.sumsq[:k])
+            out, nm = self.h[i % 2][:k], self.h_nm[i % 2][:k]
+            residual_tokens(self.out_partials(i, k), None, x, sub.alpha, self.alpha_scale,
+                            self.eps, out, nm, x_sumsq=self.sumsq[:k], overlap_launch=overlap)
+            x = out
+        return out, nm
+
+    def replay(self, k: int, positions: torch.Tensor, seq_lens: torch.Tensor,
+               h_in: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """`run` as one CUDA graph per k (fixed tensors: positions, seq_lens and h_in must be
+        the same tensors, updated in place, on every call with this k)."""
+        graph = self.graphs.get(k)
+        if graph is None:
+            out = self.run(k, positions, seq_lens, h_in)
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                self.run(k, positions, seq_lens, h_in)
+            self.graphs[k] = graph
+            return out
+        graph.replay()
+        n = len(self.layers)
+        return self.h[(n - 1) % 2][:k], self.h_nm[(n - 1) % 2][:k]
+
+
 __all__ = ["recurrent_pattern", "call_patterns", "loop_cache_offsets", "WavefrontLayer",
-           "WavefrontAttention", "entry_slots"]
+           "WavefrontAttention", "entry_slots", "AttentionSublayer", "WavefrontRecurrentBlock"]
