@@ -44,6 +44,14 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "dory-vllm-experiments_b200"))
 
+if int(os.environ.get("WORLD_SIZE", "1")) > 1 and "NCCL_DEBUG" not in os.environ:
+    # NCCL's communicator set-up lines (ranks, devices) on stderr, so that a multi-GPU run
+    # shows how many ranks joined; stdout keeps the one JSON line.  NCCL reads these once,
+    # when the library is first loaded, hence before torch is imported.
+    os.environ["NCCL_DEBUG"] = "INFO"
+    os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+
 import torch  # noqa: E402
 
 import workloads as W  # noqa: E402

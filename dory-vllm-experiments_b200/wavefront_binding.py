@@ -167,9 +167,14 @@ class WavefrontRecurrentBlock:
     sum of squares, and the residual update on the layer's output-GEMV partials fed that
     statistic; each layer's h is the next layer's residual input (ping-pong buffers).
 
-    The two GEMVs of each sublayer (NVFP4, outside this build) are the caller's: it writes
-    their split-K partials into `qkvg_partials(i, k)` / `out_partials(i, k)` (the engine's
-    prefix views, [split_k, k, rows]) before a call.  `run(k, ...)` launches the block;
+    The two GEMVs of each sublayer (NVFP4, outside this build) are the caller's, in one of
+    two ways.  Given as hooks, `qkvg_gemv(i, h_nm, partials)` (layer i's input h, FP32
+    nibble-major [k, 8, hidden / 8], into its q/k/v/gate partials) and `out_gemv(i,
+    attention_out, partials)` (the gated attention output, FP32 nibble-major [k, 8, Q / 8],
+    into its output-GEMV partials) are called at their places in the chain, so a graph
+    replay includes them; without hooks, the caller writes the partials into
+    `qkvg_partials(i, k)` / `out_partials(i, k)` (the engine's prefix views, [split_k, k,
+    rows]) before a call, e.g. seeded stand-ins.  `run(k, ...)` launches the block;
     `replay(k, ...)` runs it as one CUDA graph per k, the first call for a k running it
     plainly and then capturing it (`_run`, :336-347).  shared_cache: the recurrent layers'
     "last_loop" caches (one per layer, written and read by every loop)."""
@@ -177,8 +182,10 @@ class WavefrontRecurrentBlock:
     def __init__(self, attention: DecodeAttention, layers: list[AttentionSublayer],
                  block_tables: torch.Tensor, hidden: int, sqk_factor: float,
                  s_gate_factor: float, alpha_scale: float, eps: float,
-                 shared_cache: bool = True, qkvg_split_k: int = 2, out_split_k: int = 4):
+                 shared_cache: bool = True, qkvg_split_k: int = 2, out_split_k: int = 4,
+                 qkvg_gemv=None, out_gemv=None):
         a = attention
+        self.qkvg_gemv, self.out_gemv = qkvg_gemv, out_gemv
         self.wave = WavefrontAttention(a)
         self.layers, self.block_tables = layers, block_tables
         self.NH, self.NKV, self.HD = a.num_heads, a.num_kv_heads, a.head_dim
@@ -211,16 +218,20 @@ class WavefrontRecurrentBlock:
         return self._out[i][:n].view(self.out_split_k, k, self.hidden)
 
     def run(self, k: int, positions: torch.Tensor, seq_lens: torch.Tensor,
-            h_in: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+            h_in: torch.Tensor, h_in_nm: torch.Tensor | None = None
+            ) -> tuple[torch.Tensor, torch.Tensor]:
         """The block for rows 0 .. k-1 (row t at loop k - 1 - t; positions int64 [k],
-        seq_lens int32 [k] = positions + 1) from the block input h_in (BF16 [k, hidden]);
-        returns the last layer's h (BF16 [k, hidden]) and its nibble-major FP32 copy."""
+        seq_lens int32 [k] = positions + 1) from the block input h_in (BF16 [k, hidden];
+        h_in_nm, its FP32 nibble-major copy, for a qkvg_gemv hook); returns the last layer's
+        h (BF16 [k, hidden]) and its nibble-major FP32 copy."""
         from dory_sublayer_steps import qkvg_epilogue, residual_tokens
         pattern = recurrent_pattern(k)
         overlap = self.wave.attention.overlap_launch
-        x = h_in
+        x, x_nm = h_in, h_in_nm
         out = nm = None
         for i, sub in enumerate(self.layers):
+            if self.qkvg_gemv is not None:
+                self.qkvg_gemv(i, x_nm, self.qkvg_partials(i, k))
             qkvg_epilogue(self.qkvg_partials(i, k), positions[:k], sub.cos_sin, sub.s_gate,
                           self.s_gate_factor, self.qk[:k], self.v[:k], self.gate[:k], self.NH,
                           self.NKV, self.HD, overlap_launch=overlap)
@@ -229,22 +240,25 @@ class WavefrontRecurrentBlock:
                                      sub.window, sub.softmax_scale, self.gate[:k],
                                      self.attention_out[:k], shared_cache=self.shared_cache,
                                      out_sumsq=self.sumsq[:k])
+            if self.out_gemv is not None:
+                self.out_gemv(i, self.attention_out[:k], self.out_partials(i, k))
             out, nm = self.h[i % 2][:k], self.h_nm[i % 2][:k]
             residual_tokens(self.out_partials(i, k), None, x, sub.alpha, self.alpha_scale,
                             self.eps, out, nm, x_sumsq=self.sumsq[:k], overlap_launch=overlap)
-            x = out
+            x, x_nm = out, nm
         return out, nm
 
     def replay(self, k: int, positions: torch.Tensor, seq_lens: torch.Tensor,
-               h_in: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
-        """`run` as one CUDA graph per k (fixed tensors: positions, seq_lens and h_in must be
-        the same tensors, updated in place, on every call with this k)."""
+               h_in: torch.Tensor, h_in_nm: torch.Tensor | None = None
+               ) -> tuple[torch.Tensor, torch.Tensor]:
+        """`run` as one CUDA graph per k (fixed tensors: positions, seq_lens, h_in and h_in_nm
+        must be the same tensors, updated in place, on every call with this k)."""
         graph = self.graphs.get(k)
         if graph is None:
-            out = self.run(k, positions, seq_lens, h_in)
+            out = self.run(k, positions, seq_lens, h_in, h_in_nm)
             graph = torch.cuda.CUDAGraph()
             with torch.cuda.graph(graph):
-                self.run(k, positions, seq_lens, h_in)
+                self.run(k, positions, seq_lens, h_in, h_in_nm)
             self.graphs[k] = graph
             return out
         graph.replay()
