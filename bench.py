@@ -409,7 +409,8 @@ def make_attention(wl: DeviceWorkload, args):
                            max_tokens=max(wl.tokens, 1),
                            min_blocks_per_split=args.min_blocks_per_split,
                            overlap_launch=getattr(args, "overlap_launch", False),
-                           prefetch_chunks=getattr(args, "prefetch_chunks", 0))
+                           prefetch_chunks=getattr(args, "prefetch_chunks", 0),
+                           consumer=getattr(args, "consumer", "mma"))
 
 
 def prepare_call_path(wl: DeviceWorkload):
@@ -667,6 +668,7 @@ def bench_ours(args, world, rank, local):
               "l2": l2_note(wl),
               "splits": args.splits, "min_blocks_per_split": args.min_blocks_per_split,
               "overlap_launch": args.overlap_launch, "path": args.path,
+              "consumer": args.consumer,
               "out_sumsq": bool(args.sumsq)}
     del attn, wl
     torch.cuda.synchronize(dev)
@@ -675,7 +677,8 @@ def bench_ours(args, world, rank, local):
     cpu, extra = None, None
     if rank == 0 and world == 1:
         cpu = cpu_baseline(args.workload, args.cpu_seconds)
-        if args.all_configs and args.workload == "config5" and args.path == "fused":
+        if (args.all_configs and args.workload == "config5" and args.path == "fused"
+                and args.consumer == "mma"):
             extra = measure_other_configs(args, dev)
 
     line = {
@@ -1243,6 +1246,10 @@ def main() -> int:
     ap.add_argument("--prefetch-chunks", type=int, default=0,
                     help="L2 prefetch distance ahead of each CTA's ring, in 16-row chunks "
                          "(0: automatic, < 0: none)")
+    ap.add_argument("--consumer", choices=("mma", "fma"), default="mma",
+                    help="dot products of the chunk step: mma.sync tensor-core tiles (the "
+                         "product) or FP32 FMAs on the CUDA cores (the measured alternative; "
+                         "128-dim heads, no shared cache)")
     ap.add_argument("--sumsq", action="store_true",
                     help="also produce each token's sum of squared outputs (out_sumsq)")
     ap.add_argument("--all-configs", action=argparse.BooleanOptionalAction, default=True,

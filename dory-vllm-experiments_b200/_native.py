@@ -13,7 +13,7 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 LIBRARY = HERE / "libdory_decode.so"
 
-ABI_VERSION = 6
+ABI_VERSION = 7
 
 # DoryStatus
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_ALIGNMENT, ERR_CUDA = range(5)
@@ -21,6 +21,7 @@ OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_ALIGNMENT, ERR_CUDA = range(5)
 DTYPE_F32, DTYPE_BF16, DTYPE_F16 = range(3)
 # DORY_FLAG_*
 FLAG_RAW_QKV, FLAG_MULTI_TOKEN, FLAG_SHARED_CACHE, FLAG_OVERLAP_LAUNCH = 1, 2, 4, 8
+FLAG_FMA_CONSUMER = 16
 # DORY_QKNORM_*
 QKNORM_WRITE_CACHE = 1
 # DORY_DEVERR_*

@@ -333,6 +333,103 @@ __device__ __forceinline__ float fast_exp2(float x) {
 }
 __device__ __forceinline__ void record_error(uint32_t* err, uint32_t bit) { atomicOr(err, bit); }
 
+// ------------------------------------------------------------------------------------
+// CUDA-core (FP32 FMA) form of a consumer warp's chunk step, 128-dim heads and at most 4
+// query rows: the measured alternative to the mma.sync tiles (DORY_FLAG_FMA_CONSUMER).
+// Lane l owns dims [4l, 4l + 4) of every row.  Per half chunk (8 tokens) it forms its 4-dim
+// share of the 8 x 4 scores with FMAs; a transposing butterfly (each of 5 steps keeps half of
+// the lane's values and adds the partner's share of them, received for the half it gives
+// away) then leaves lane l the complete score of row l / 8 at token l % 8 of that half.
+// Softmax as the tensor-core path: log2 domain, the running sum from unrounded P, P rounded
+// to bf16 for P.V, which goes through a per-warp [16 tokens][4 rows] buffer and FMAs into
+// this lane's 4 dims of each row's output.
+// ------------------------------------------------------------------------------------
+struct FmaRows {
+  float o[4][4];  // [row][this lane's 4 dims]
+  float m[4];     // running max of each row (log2 units), the same in every lane
+  float l;        // this lane's share of the running sum of row lane / 8
+};
+__device__ __forceinline__ void unpack_bf16x4(uint2 w, float (&x)[4]) {
+  x[0] = __uint_as_float(w.x << 16);
+  x[1] = __uint_as_float(w.x & 0xffff0000u);
+  x[2] = __uint_as_float(w.y << 16);
+  x[3] = __uint_as_float(w.y & 0xffff0000u);
+}
+__device__ __forceinline__ void fma_chunk(FmaRows& st, const float (&q)[4][4], const uint8_t* kst,
+                                          const uint8_t* vst, float* pbuf, int lane, int c,
+                                          int rfirst, int rlen) {
+  const int d8 = 8 * (lane >> 1);     // this lane's 16-byte piece of a row ...
+  const int half8 = (lane & 1) * 8;   // ... and its 8-byte half
+  float x[2];                         // x[h]: score (token 8h + lane % 8, row lane / 8)
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    float v[32];                      // v[r * 8 + t]: this lane's share of score (8h + t, r)
+#pragma unroll
+    for (int t = 0; t < 8; ++t) {
+      float k[4];
+      unpack_bf16x4(*reinterpret_cast<const uint2*>(kst + tile_off(8 * h + t, d8) + half8), k);
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+        v[r * 8 + t] =
+            fmaf(q[r][3], k[3], fmaf(q[r][2], k[2], fmaf(q[r][1], k[1], q[r][0] * k[0])));
+    }
+#pragma unroll
+    for (int lev = 0; lev < 5; ++lev) {
+      const int half = 16 >> lev, mask = 16 >> lev;
+      const bool up = lane & mask;
+#pragma unroll
+      for (int i = 0; i < half; ++i) {
+        const float send = up ? v[i] : v[i + half];
+        const float keep = up ? v[i + half] : v[i];
+        v[i] = keep + __shfl_xor_sync(0xffffffffu, send, mask);
+      }
+    }
+    x[h] = v[0];
+  }
+  const int r = lane >> 3;
+  const int tk = lane & 7;
+  const int pos0 = c * kChunk + tk;
+  const float x0 = (pos0 >= rfirst && pos0 < rlen) ? x[0] * kLog2e : -INFINITY;
+  const float x1 = (pos0 + 8 >= rfirst && pos0 + 8 < rlen) ? x[1] * kLog2e : -INFINITY;
+  float tmax = fmaxf(x0, x1);
+  tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 1));
+  tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 2));
+  tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
+  float alpha[4], a_own = 1.0f, m_own = 0.0f;
+#pragma unroll
+  for (int rr = 0; rr < 4; ++rr) {
+    const float mnew = fmaxf(st.m[rr], __shfl_sync(0xffffffffu, tmax, rr * 8));
+    const float muse = (mnew == -INFINITY) ? 0.0f : mnew;
+    alpha[rr] = fast_exp2(st.m[rr] - muse);
+    st.m[rr] = mnew;
+    if (rr == r) {
+      a_own = alpha[rr];
+      m_own = muse;
+    }
+  }
+  const float p0 = fast_exp2(x0 - m_own), p1 = fast_exp2(x1 - m_own);
+  st.l = st.l * a_own + p0 + p1;
+  pbuf[tk * 4 + r] = __bfloat162float(__float2bfloat16_rn(p0));
+  pbuf[(tk + 8) * 4 + r] = __bfloat162float(__float2bfloat16_rn(p1));
+  __syncwarp();
+#pragma unroll
+  for (int rr = 0; rr < 4; ++rr)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) st.o[rr][j] *= alpha[rr];
+#pragma unroll
+  for (int t = 0; t < kChunk; ++t) {
+    float vv[4];
+    unpack_bf16x4(*reinterpret_cast<const uint2*>(vst + tile_off(t, d8) + half8), vv);
+    const float4 pp = *reinterpret_cast<const float4*>(pbuf + t * 4);
+    const float pr[4] = {pp.x, pp.y, pp.z, pp.w};
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) st.o[rr][j] = fmaf(pr[rr], vv[j], st.o[rr][j]);
+  }
+  __syncwarp();  // the buffer is rewritten by this warp's next chunk
+}
+
 __device__ __forceinline__ float load_sqk(const void* sqk, int dtype, int64_t i) {
   if (dtype == DORY_DTYPE_BF16) return __bfloat162float(static_cast<const __nv_bfloat16*>(sqk)[i]);
   if (dtype == DORY_DTYPE_F16) return __half2float(static_cast<const __half*>(sqk)[i]);
@@ -701,9 +798,10 @@ __device__ __forceinline__ void sumsq_tail(const KParams& p, const float* sv, in
 // ------------------------------------------------------------------------------------
 // The kernel.  grid = (splits, NKV, T); block = 160 threads (4 consumer warps + producer).
 // ------------------------------------------------------------------------------------
-template <int HD, int NT, int NS, bool SS, bool DM>
+template <int HD, int NT, int NS, bool SS, bool DM, bool FMA = false>
 __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     decode_kernel(const __grid_constant__ KParams p) {
+  static_assert(!FMA || (HD == 128 && NT == 1), "the CUDA-core consumer is 128-dim, one tile");
   using L = Smem<HD, NS>;
   constexpr int KT = HD / 16;          // MMA k-steps over head_dim / m-tiles of O^T
   constexpr int ROWS = NT * 8;         // query rows per CTA
@@ -1295,6 +1393,60 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   }
 
   bool failed = false;
+  // CUDA-core consumer state (FMA instantiations only): the query rows as FP32 (the same
+  // bf16 values as the tensor-core B fragments), the attended range of this lane's row.
+  FmaRows fst;
+  float fq[4][4];
+  int f_first = 0, f_len = 0;
+  // Per-warp P buffer: the upper half of the query area (one 8-row tile uses the lower half).
+  float* pbuf = reinterpret_cast<float*>(smem + L::kQ + 8 * HD * 2) + warp * 64;
+  if constexpr (FMA) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const uint2 w = *reinterpret_cast<const uint2*>(q2 + r * HD + 4 * lane);
+      unpack_bf16x4(w, fq[r]);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) fst.o[r][j] = 0.0f;
+      fst.m[r] = -INFINITY;
+    }
+    fst.l = 0.0f;
+    const int r = lane >> 3;
+    f_len = r < nrows ? s_len[ibase + r / G] : 0;
+    f_first = (p.window > 0) ? max(f_len - p.window, 0) : 0;
+    for (int i = warp; i < nchunks; i += kConsumerWarps) {
+      const int stage = i % NS;
+      if (!mbar_wait(full_bar(stage), (i / NS) & 1)) {
+        if (lane == 0) record_error(p.err, DORY_DEVERR_WAIT_TIMEOUT);
+        failed = true;
+        break;
+      }
+      const int4 mt = meta[stage];
+      const int phys = mt.x;
+      const int c = mt.z;
+      uint8_t* kst = smem + L::kStages + stage * L::kStageBytes;
+      uint8_t* vst = kst + TILE;
+      bool touched = false;
+      const bool partial = use_tma && (c < c_full_lo || c >= c_full_hi || phys < 0);
+      if (partial || (c >= sub_lo && c <= sub_hi) || any_foreign)
+        touched = fixup_stage<HD>(p, kst, vst, c, phys, partial, lane, s_ci, s_len, s_phys,
+                                  s_coff, s_toff, subkv, &s_slot);
+      __syncwarp();
+      fma_chunk(fst, fq, kst, vst, pbuf, lane, c, f_first, f_len);
+      if (use_tma) {
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0 && i + NS < nchunks) issue_chunk(i + NS);
+      } else {
+        if (touched) fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(empty_bar(stage));
+      }
+    }
+    // Row sums: the 8 lanes of a row hold disjoint token pairs of it.
+    fst.l += __shfl_xor_sync(0xffffffffu, fst.l, 1);
+    fst.l += __shfl_xor_sync(0xffffffffu, fst.l, 2);
+    fst.l += __shfl_xor_sync(0xffffffffu, fst.l, 4);
+  } else {
   for (int i = warp; i < nchunks; i += kConsumerWarps) {
     const int stage = i % NS;
     const uint32_t parity = (i / NS) & 1;
@@ -1422,6 +1574,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
       v += __shfl_xor_sync(0xffffffffu, v, 16);
       l[nt][i] = v;
     }
+  }  // tensor-core consumer
 
   if (failed && lane == 0) s_fail = 1;
   grid_launch_dependents();  // streaming is done: the next grid may start its prologue
@@ -1444,6 +1597,22 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   // ---- merge the four consumer warps (shared memory, aliasing the drained ring) ----
   constexpr int OST = HD + 4;  // padded row stride of the per-warp O buffers (floats)
   float* wo = reinterpret_cast<float*>(smem + L::kStages);  // [warps][ROWS][OST]
+  if constexpr (FMA) {
+    // Rows 0-3 only: the CUDA-core consumer serves at most 4 rows (nrows <= 4).
+    const int r = lane >> 3;
+    if ((lane & 7) == 0) {
+      float mr = fst.m[0];
+#pragma unroll
+      for (int rr = 1; rr < 4; ++rr)
+        if (rr == r) mr = fst.m[rr];
+      s_wm[warp][r] = mr;
+      s_wl[warp][r] = fst.l;
+    }
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr)
+      *reinterpret_cast<float4*>(wo + (warp * ROWS + rr) * OST + 4 * lane) =
+          make_float4(fst.o[rr][0], fst.o[rr][1], fst.o[rr][2], fst.o[rr][3]);
+  } else {
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
@@ -1460,6 +1629,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
         dst[kk * 16 + g + 8] = o[nt][kk][2 + i];
       }
     }
+  }
   named_barrier_consumers();
 
   // Items: (row, 8 consecutive dims).  Each thread merges its items across warps.
@@ -1908,9 +2078,9 @@ int32_t fail(int32_t status, const char* fmt, ...) {
   return status;
 }
 
-template <int HD, int NT, int NS, bool SS, bool DM>
+template <int HD, int NT, int NS, bool SS, bool DM, bool FMA = false>
 int32_t launch(const KParams& kp, dim3 grid, int smem_bytes, cudaStream_t stream) {
-  auto fn = decode_kernel<HD, NT, NS, SS, DM>;
+  auto fn = decode_kernel<HD, NT, NS, SS, DM, FMA>;
   static int configured[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return fail(DORY_ERR_CUDA, "cudaGetDevice failed");
@@ -1999,6 +2169,19 @@ int32_t dispatch(const KParams& kp, dim3 grid, cudaStream_t stream) {
               : launch<HD, NT, NS, true, false>(kp, grid, smem, stream);
   return dm ? launch<HD, NT, NS, false, true>(kp, grid, smem, stream)
             : launch<HD, NT, NS, false, false>(kp, grid, smem, stream);
+}
+
+// The CUDA-core consumer (DORY_FLAG_FMA_CONSUMER): 128-dim heads, one tile of at most 4
+// rows; the same ring, prologue, merge and launch rules as the tensor-core kernel.
+int32_t dispatch_fma(const KParams& kp, dim3 grid, cudaStream_t stream) {
+  constexpr int NS = Depth<128, 1>::value;
+  const int smem = Smem<128, NS>::bytes(kp.nsub);
+  const bool dm = one_wave(decode_kernel<128, 1, NS, false, true, true>, grid, smem);
+  if (kp.sumsq)
+    return dm ? launch<128, 1, NS, true, true, true>(kp, grid, smem, stream)
+              : launch<128, 1, NS, true, false, true>(kp, grid, smem, stream);
+  return dm ? launch<128, 1, NS, false, true, true>(kp, grid, smem, stream)
+            : launch<128, 1, NS, false, false, true>(kp, grid, smem, stream);
 }
 
 template <int HD>
@@ -2316,6 +2499,7 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
   const bool multi = a.flags & DORY_FLAG_MULTI_TOKEN;
   const bool shared = a.flags & DORY_FLAG_SHARED_CACHE;
   const bool overlap = a.flags & DORY_FLAG_OVERLAP_LAUNCH;
+  const bool fma = a.flags & DORY_FLAG_FMA_CONSUMER;
   if (a.num_tokens < 0) return fail(DORY_ERR_INVALID_ARGUMENT, "negative token count");
   if (a.num_tokens > a.max_tokens)
     return fail(DORY_ERR_INVALID_ARGUMENT, "too many tokens for the scratch buffers");
@@ -2340,6 +2524,10 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
     return fail(DORY_ERR_UNSUPPORTED, "block_size %d is not a multiple of 16", a.block_size);
   const int G = a.num_heads / a.num_kv_heads;
   if (G > 16) return fail(DORY_ERR_UNSUPPORTED, "%d query heads per KV head (max 16)", G);
+  if (fma && (HD != 128 || G > 4 || shared))
+    return fail(DORY_ERR_UNSUPPORTED,
+                "the CUDA-core consumer takes 128-dim heads, at most 4 query heads per KV head "
+                "and no shared cache");
   if (shared && a.num_tokens > kMaxSub)
     return fail(DORY_ERR_UNSUPPORTED, "shared-cache calls take at most %d tokens", kMaxSub);
   if (a.sqk_dtype < 0 || a.sqk_dtype > 2) return fail(DORY_ERR_INVALID_ARGUMENT, "sqk dtype");
@@ -2464,7 +2652,7 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
   cudaStream_t s = (cudaStream_t)stream;
   dim3 grid(a.splits, a.num_kv_heads, a.num_tokens);
   if (HD == 64) return dispatch_nt<64>(kp, nt, grid, s);
-  if (HD == 128) return dispatch_nt<128>(kp, nt, grid, s);
+  if (HD == 128) return fma ? dispatch_fma(kp, grid, s) : dispatch_nt<128>(kp, nt, grid, s);
   return dispatch_nt<256>(kp, nt, grid, s);
 }
 

@@ -58,14 +58,16 @@ class DecodeAttention:
     prefetch_chunks (B200 addition): how far ahead of its shared-memory ring each CTA starts
     the DRAM reads of its K/V chunks into L2; 0 picks automatically (a CTA's whole range
     for overlapped launches that fit in one wave of CTAs, else none), a negative value
-    turns it off.
+    turns it off.  consumer (B200 addition): "mma" (default) computes the score and P.V dot
+    products with mma.sync tensor-core tiles, "fma" with FP32 FMAs on the CUDA cores, the
+    measured alternative (128-dim heads, at most 4 query heads per KV head, no shared cache).
     """
 
     def __init__(self, num_heads: int, num_kv_heads: int, head_dim: int, device: torch.device,
                  splits: int = 32, blocks_per_tile: int = 1, num_warps: int = 4,
                  num_stages: int = 2, dim_chunk: int = 64, max_tokens: int = 1,
                  min_blocks_per_split: int = 1, overlap_launch: bool = False,
-                 prefetch_chunks: int = 0):
+                 prefetch_chunks: int = 0, consumer: str = "mma"):
         if num_heads % num_kv_heads:
             raise ValueError("query heads must be a multiple of KV heads")
         self.num_heads, self.num_kv_heads, self.head_dim = num_heads, num_kv_heads, head_dim
@@ -76,6 +78,9 @@ class DecodeAttention:
         self.min_blocks_per_split = min_blocks_per_split
         self.overlap_launch = bool(overlap_launch)
         self.prefetch_chunks = int(prefetch_chunks)
+        if consumer not in ("mma", "fma"):
+            raise ValueError("consumer must be 'mma' or 'fma'")
+        self.consumer = consumer
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise RuntimeError("DecodeAttention runs on CUDA devices only (no CPU path)")
@@ -207,6 +212,8 @@ class DecodeAttention:
             raise ValueError("block tables and seq_lens must be int32")
         p = self._params
         flags = _native.FLAG_OVERLAP_LAUNCH if self.overlap_launch else 0
+        if self.consumer == "fma":
+            flags |= _native.FLAG_FMA_CONSUMER
         if raw is not None:
             v, sqk, sqk_factor, eps, slot_mapping = raw
             if q.dtype != torch.float32 or v.dtype != torch.float32:

@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define DORY_DECODE_ABI_VERSION 6
+#define DORY_DECODE_ABI_VERSION 7
 
 /* Status codes returned by every entry point. */
 typedef enum DoryStatus {
@@ -60,7 +60,13 @@ enum {
    * immediately before this call on the stream must not write this call's seq_lens, block
    * tables, offsets, slot_mapping or the cache rows it attends (q/k/v/gate and all outputs
    * are ordered as usual).  No counterpart in the reference (Triton launches). */
-  DORY_FLAG_OVERLAP_LAUNCH = 8u
+  DORY_FLAG_OVERLAP_LAUNCH = 8u,
+  /* Score and P.V dot products on the CUDA cores (FP32 FMA) instead of mma.sync tensor-core
+   * tiles; everything else (ring, normalisation, append, merge, outputs) is the same kernel.
+   * The measured alternative that decides where the tensor-core tiles pay; head_dim 128, at
+   * most 4 query heads per KV head, no SHARED_CACHE (DORY_ERR_UNSUPPORTED otherwise).  No
+   * counterpart in the reference (its Triton kernel always uses tl.dot). */
+  DORY_FLAG_FMA_CONSUMER = 16u
 };
 
 /* Device error bits, accumulated in the scratch header and read back with

@@ -15,7 +15,7 @@ ATOL, RTOL = 2e-2, 1e-2
 
 def run(case: W.Case, layout: str = "triton", splits: int = 32, blocks_per_tile: int = 1,
         min_blocks_per_split: int = 1, single_entry: bool | None = None, attn=None,
-        device: str = "cuda", prefetch_chunks: int = 0):
+        device: str = "cuda", prefetch_chunks: int = 0, consumer: str = "mma"):
     """Runs the case once; returns (out [T, 8, Q/8] on CPU, device dict, raw cache before)."""
     dev = torch.device(device)
     d = W.to_device(case, layout, dev)
@@ -25,7 +25,7 @@ def run(case: W.Case, layout: str = "triton", splits: int = 32, blocks_per_tile:
         attn = DecodeAttention(case.num_heads, case.num_kv_heads, case.head_dim, dev,
                                splits=splits, blocks_per_tile=blocks_per_tile,
                                max_tokens=max(T, 1), min_blocks_per_split=min_blocks_per_split,
-                               prefetch_chunks=prefetch_chunks)
+                               prefetch_chunks=prefetch_chunks, consumer=consumer)
     if single_entry is None:
         single_entry = T == 1 and not case.shared
     if single_entry:
