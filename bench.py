@@ -44,13 +44,18 @@ from pathlib import Path
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "dory-vllm-experiments_b200"))
 
+NCCL_LOG = None
 if int(os.environ.get("WORLD_SIZE", "1")) > 1 and "NCCL_DEBUG" not in os.environ:
-    # NCCL's communicator set-up lines (ranks, devices) on stderr, so that a multi-GPU run
-    # shows how many ranks joined; stdout keeps the one JSON line.  NCCL reads these once,
+    # NCCL's communicator set-up lines (ranks, devices) go to a per-process file that
+    # init_dist copies to stderr once the communicator exists, so that a multi-GPU run shows
+    # how many ranks joined while stdout keeps the one JSON line.  (NCCL opens its debug
+    # file for writing, which would truncate a shared stderr file.)  NCCL reads these once,
     # when the library is first loaded, hence before torch is imported.
+    import tempfile
+    NCCL_LOG = os.path.join(tempfile.gettempdir(), f"dory_bench_nccl_{os.getpid()}.log")
     os.environ["NCCL_DEBUG"] = "INFO"
     os.environ["NCCL_DEBUG_SUBSYS"] = "INIT"
-    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+    os.environ["NCCL_DEBUG_FILE"] = NCCL_LOG
 
 import torch  # noqa: E402
 
@@ -81,6 +86,11 @@ def init_dist(world: int, local: int):
     torch.cuda.set_device(local)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                             device_id=torch.device("cuda", local))
+    dist.barrier()  # the communicator exists (and has logged its set-up) after this
+    if NCCL_LOG is not None and os.path.exists(NCCL_LOG):
+        with open(NCCL_LOG) as f:
+            sys.stderr.write(f.read())
+        sys.stderr.flush()
     return dist
 
 
