@@ -509,15 +509,15 @@ __device__ __forceinline__ Split split_layout(int lo, int hi, int B, int b_shift
 //    reference uses the new token from registers (dory_decode_attention.py:141-145) and
 //    its shared-cache mode caches every token first (:294-301);
 //  * append: the chunk holding a group token's position writes its k/v to the cache
-//    (slot_mapping[0] in single-token calls, read at kernel entry into *s_slot for 256-dim
-//    heads; in multi-token calls slot_mapping[t] when given, else the table's slot).
+//    in shared-cache calls (slot_mapping[t] when given, else the table's slot); other raw
+//    calls leave the new row out of the chunk loop and append it in the prologue.
 // Returns whether the stage was written (the caller then fences before tensor copies).
 // ------------------------------------------------------------------------------------
 // CTA constants the slow path needs, kept in shared memory so that the hot loop does not
 // hold them in registers.
 struct CtaInfo {
   long long coff, toff;
-  int lo, hi, kvh, nsub, ibase, gcount, offset_ok, tok;
+  int lo, hi, kvh, nsub, ibase, gcount, offset_ok, tok, reg_new;
 };
 
 template <int HD>
@@ -525,7 +525,7 @@ __device__ __forceinline__ bool fixup_stage(const KParams& p, uint8_t* kst, uint
                                          int phys, bool zero_rows, int lane,
                                          const CtaInfo& ci, const int* s_len, const int* s_phys,
                                          const long long* s_coff, const long long* s_toff,
-                                         const __nv_bfloat16* subkv, const long long* s_slot) {
+                                         const __nv_bfloat16* subkv) {
   const long long coff = ci.coff, toff = ci.toff;
   const int lo = ci.lo, hi = ci.hi, kvh = ci.kvh, nsub = ci.nsub, ibase = ci.ibase;
   const int gcount = ci.gcount;
@@ -543,7 +543,7 @@ __device__ __forceinline__ bool fixup_stage(const KParams& p, uint8_t* kst, uint
     }
     touched = true;
   }
-  if (!p.raw) return touched;
+  if (!p.raw || ci.reg_new) return touched;  // reg_new: the new row is masked, added apart
   for (int s = 0; s < nsub; ++s) {
     const int len = s_len[s];
     if (len <= 0) continue;
@@ -574,8 +574,7 @@ __device__ __forceinline__ bool fixup_stage(const KParams& p, uint8_t* kst, uint
       if (phys < 0) continue;  // its block id was out of range (already recorded)
       slot = (long long)phys * B + mod_p2(pos, B, p.b_shift);
     } else {
-      slot = HD == 256 ? *s_slot : p.slot_mapping[0];
-      if (slot < 0) continue;  // padding token: vLLM does not cache it
+      continue;  // single-token calls append outside the chunk loop (reg_new)
     }
     const long long blk = slot / B;
     if (blk < 0 || (p.ncache_blocks > 0 && blk >= p.ncache_blocks) || !offset_ok) {
@@ -819,12 +818,12 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   // range (pv_accumulate), and a single-token call's slot is read at entry.  Narrower heads
   // keep the zeroing slow path: that code measured faster for them.
   constexpr bool kRowMask = HD == 256;
-  __shared__ long long s_slot;
   __shared__ uint4 s_zero_row;
   __shared__ int s_tab[kTab];  // block ids of the first kTab blocks of this CTA's range
   __shared__ CtaInfo s_ci;
   __shared__ float s_wm[kConsumerWarps][ROWS], s_wl[kConsumerWarps][ROWS];
   __shared__ float s_rowss[16];  // per-row sums of squared outputs (sumsq)
+  __shared__ float s_newm[16];   // reg_new: the new token's score per row (log2 units)
 
   const int split = blockIdx.x;
   const int kvh = blockIdx.y;
@@ -877,7 +876,6 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     s_toff[tid] = p.multi ? p.table_offsets[t] : 0;
   }
   if (kRowMask) {
-    if (tid == 32) s_slot = (p.raw && !p.multi) ? p.slot_mapping[0] : -1;
     if (tid == 64) s_zero_row = make_uint4(0u, 0u, 0u, 0u);
   }
   __syncthreads();
@@ -917,6 +915,12 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   const int nsub = p.nsub;
   const Split sp = split_layout(lo, hi, B, p.b_shift, p.S, p.bpt, p.tps_min);
   const int nrows = gcount * G;
+  // Raw calls whose tokens each read their own cache (not shared): the new token's row
+  // (position seq_len - 1) is left out of the chunk loop (attended cache rows [lo, hi_c))
+  // and enters the merge from the k/v the kernel normalises, in the CTA that holds its
+  // position, which also appends it in the prologue (off the chunk loop's critical path).
+  const bool reg_new = p.raw && !p.shared;
+  const int hi_c = reg_new ? hi - 1 : hi;
 
   if (sp.tiles == 0) {
     // Padding request(s): the reference's combine writes 0 * gate.
@@ -942,8 +946,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   const int be = min(sp.first_block + tile_end * p.bpt, sp.first_block + sp.nblocks);
   const int CPB = B / kChunk;
   const int cb = max(bb * CPB, lo / kChunk);
-  const int ce = min(be * CPB, (hi + kChunk - 1) / kChunk);
-  const int nchunks = ce - cb;
+  const int ce = min(be * CPB, (hi_c + kChunk - 1) / kChunk);
+  const int nchunks = max(ce - cb, 0);
 
   const uint32_t bars = smem_u32(smem + L::kBars);
   auto full_bar = [&](int s) { return bars + 8u * s; };
@@ -1079,7 +1083,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
         const int jj = is_v ? j - kChunk * VEC : j;
         const int r = jj / VEC, w = jj % VEC;
         const int pos = c * kChunk + r;
-        const bool valid = phys_ok && pos >= lo && pos < hi;
+        const bool valid = phys_ok && pos >= lo && pos < hi_c;
         const __nv_bfloat16* src =
             valid ? (is_v ? vbase : kbase) + block_off + int64_t(r) * p.so + w * 8 : p.kc;
         cp_async_16((is_v ? vt : kt) + tile_off(r, w * 8), src, valid ? 16u : 0u, policy);
@@ -1111,9 +1115,25 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     const bool same = s_coff[lane] == coff && s_toff[lane] == toff;
     s_phys[lane] = (len > 0 && !same) ? p.table[s_toff[lane] + (len - 1) / B] : -1;
   }
+  // The CTA holding the new token's position (the last active split) adds its row in the
+  // merge and appends it; its slot is read now, in flight with the query rows' loads.
+  const bool add_new = reg_new && split == sp.active - 1;
+  long long slot_new = -1;
+  if (add_new && p.raw && tid == 0) {
+    const int pos = s_len[0] - 1;
+    if (!p.multi) {
+      slot_new = p.slot_mapping[0];
+    } else if (p.slot_mapping) {
+      slot_new = p.slot_mapping[tok];
+    } else {
+      const int ph = table[div_p2(pos, B, p.b_shift)];
+      if (ph >= 0) slot_new = (long long)ph * B + mod_p2(pos, B, p.b_shift);
+      else record_error(p.err, DORY_DEVERR_BLOCK_OOB);
+    }
+  }
   int sub_lo = 0x7fffffff, sub_hi = -1;  // chunks that may hold a same-table new row
   bool any_foreign = false;
-  if (p.raw) {
+  if (p.raw && !reg_new) {
     for (int s2 = 0; s2 < nsub; ++s2) {
       const int len = s_len[s2];
       if (len <= 0) continue;
@@ -1126,17 +1146,18 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     }
   }
   const int c_full_lo = (lo + kChunk - 1) / kChunk;  // chunks in [c_full_lo, c_full_hi) have
-  const int c_full_hi = hi / kChunk;                 // every row inside [lo, hi)
+  const int c_full_hi = hi_c / kChunk;               // every row inside [lo, hi_c)
   if (tid == 0) {
     s_ci.coff = coff;
     s_ci.toff = toff;
     s_ci.lo = lo;
-    s_ci.hi = hi;
+    s_ci.hi = hi_c;
     s_ci.kvh = kvh;
     s_ci.nsub = nsub;
     s_ci.ibase = ibase;
     s_ci.gcount = gcount;
     s_ci.offset_ok = offset_ok;
+    s_ci.reg_new = reg_new;
     s_ci.tok = tok;
   }
   // (1) query rows: normalise / scale / round, as the reference, into q2 [ROWS][HD] bf16;
@@ -1145,7 +1166,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   // before any of the arithmetic: one L2 round trip, not one per dependent step.
   constexpr int RPW = ROWS / kConsumerWarps;  // query rows per consumer warp
   if constexpr (HD == 256) {
-    const bool sub0 = p.raw && warp < nsub;
+    const bool sub0 = p.raw && warp < nsub && (!reg_new || add_new);
     // 256-dim heads: 16-byte loads where the bases allow them (every row offset is a
     // multiple of 16 bytes), and in raw mode the FP64 sums of all of this warp's rows (its
     // query rows and its new token's k row) taken together, each in row_inv_norm's order
@@ -1288,7 +1309,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
         for (int i = 0; i < PER_LANE; ++i) qv[j][i] = __bfloat162float(src[lane * PER_LANE + i]);
       }
     }
-    const bool sub0 = p.raw && warp < nsub;
+    const bool sub0 = p.raw && warp < nsub && (!reg_new || add_new);
     if (sub0) {
       const int t = p.shared ? warp : tok;
       const float* ksrc =
@@ -1354,6 +1375,41 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   }
   named_barrier_consumers();
   pipeline_ready_wait();  // the producer has initialised the stages' barriers
+  if (add_new) {
+    // The new token's score against each query row (bf16 operands, FP32 sum), for the merge.
+    for (int r = warp; r < nrows; r += kConsumerWarps) {
+      float dot = 0.0f;
+      for (int d = 2 * lane; d < HD; d += 64) {
+        const float2 qv2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(q2 + r * HD + d));
+        const float2 kv2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(subkv + d));
+        dot = fmaf(qv2.x, kv2.x, dot);
+        dot = fmaf(qv2.y, kv2.y, dot);
+      }
+#pragma unroll
+      for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+      if (lane == 0) s_newm[r] = dot * kLog2e;
+    }
+    // The append: the new k and v rows at the token's slot (a negative slot is a padding
+    // token, which vLLM does not cache; a slot outside the cache is recorded and skipped).
+    if (p.raw && warp == 0) {
+      const long long slot = __shfl_sync(0xffffffffu, slot_new, 0);
+      if (slot >= 0) {
+        const long long blk = slot / B;
+        if ((p.ncache_blocks > 0 && blk >= p.ncache_blocks) || !offset_ok) {
+          if (lane == 0) record_error(p.err, DORY_DEVERR_SLOT_OOB);
+        } else {
+          constexpr int kVec = HD / 8;
+          const long long base = coff + blk * p.sb + (slot % B) * p.so + (long long)kvh * p.sh;
+          for (int idx = lane; idx < 2 * kVec; idx += 32) {
+            const bool is_v = idx >= kVec;
+            const int w = is_v ? idx - kVec : idx;
+            const uint4 val = reinterpret_cast<const uint4*>(subkv + (is_v ? HD : 0))[w];
+            reinterpret_cast<uint4*>((is_v ? p.vc : p.kc) + base)[w] = val;
+          }
+        }
+      }
+    }
+  }
 
   // (4) B fragments of Q^T (k = dims, n = query rows), resident for the whole loop.
   const int g = lane >> 2;
@@ -1376,7 +1432,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
       const int r = nt * 8 + 2 * t4 + i;
       int len = 0;
       if (r < nrows) len = s_len[ibase + r / G];
-      rlen[nt][i] = len;
+      rlen[nt][i] = (reg_new && len > 0) ? len - 1 : len;
       rfirst[nt][i] = (p.window > 0) ? max(len - p.window, 0) : 0;
     }
 
@@ -1411,8 +1467,9 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     }
     fst.l = 0.0f;
     const int r = lane >> 3;
-    f_len = r < nrows ? s_len[ibase + r / G] : 0;
-    f_first = (p.window > 0) ? max(f_len - p.window, 0) : 0;
+    const int f_seq = r < nrows ? s_len[ibase + r / G] : 0;
+    f_first = (p.window > 0) ? max(f_seq - p.window, 0) : 0;
+    f_len = (reg_new && f_seq > 0) ? f_seq - 1 : f_seq;
     for (int i = warp; i < nchunks; i += kConsumerWarps) {
       const int stage = i % NS;
       if (!mbar_wait(full_bar(stage), (i / NS) & 1)) {
@@ -1429,7 +1486,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
       const bool partial = use_tma && (c < c_full_lo || c >= c_full_hi || phys < 0);
       if (partial || (c >= sub_lo && c <= sub_hi) || any_foreign)
         touched = fixup_stage<HD>(p, kst, vst, c, phys, partial, lane, s_ci, s_len, s_phys,
-                                  s_coff, s_toff, subkv, &s_slot);
+                                  s_coff, s_toff, subkv);
       __syncwarp();
       fma_chunk(fst, fq, kst, vst, pbuf, lane, c, f_first, f_len);
       if (use_tma) {
@@ -1466,7 +1523,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     const bool partial = use_tma && (c < c_full_lo || c >= c_full_hi || phys < 0);
     if ((partial && !kRowMask) || (c >= sub_lo && c <= sub_hi) || any_foreign)
       touched = fixup_stage<HD>(p, kst, vst, c, phys, partial && !kRowMask, lane, s_ci, s_len,
-                                s_phys, s_coff, s_toff, subkv, &s_slot);
+                                s_phys, s_coff, s_toff, subkv);
     __syncwarp();
 
     // S^T = K Q^T : [16 tokens x 8 rows] per n-tile, as two independent MMA chains (even
@@ -1646,6 +1703,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < kConsumerWarps; ++w) M = fmaxf(M, s_wm[w][r]);
+    if (add_new) M = fmaxf(M, s_newm[r]);
     const float Muse = (M == -INFINITY) ? 0.0f : M;
     float Lsum = 0.0f, acc[8];
 #pragma unroll
@@ -1658,6 +1716,14 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
       const float4 a = src[0], b = src[1];
       acc[0] += wt * a.x; acc[1] += wt * a.y; acc[2] += wt * a.z; acc[3] += wt * a.w;
       acc[4] += wt * b.x; acc[5] += wt * b.y; acc[6] += wt * b.z; acc[7] += wt * b.w;
+    }
+    if (add_new) {
+      // the new token's row: P = exp2(score - M), V from the registers' bf16 copy
+      const float wt = fast_exp2(s_newm[r] - Muse);
+      Lsum += wt;
+      const __nv_bfloat16* vn = subkv + HD + k8 * 8;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += wt * __bfloat162float(vn[e]);
     }
     const int t = gstart + r / G;
     const int head = kvh * G + r % G;
