@@ -761,6 +761,8 @@ def measure_other_configs(args, dev) -> dict:
             else:
                 entry.update(res)
             del attn
+        if name in ("config1", "dory640"):
+            entry["host_issue"] = measure_host_issue(args, wl, splits, mbps)
         del wl
         torch.cuda.empty_cache()
         entry["cpu_baseline"] = cpu_baseline(name, budget)
@@ -768,6 +770,29 @@ def measure_other_configs(args, dev) -> dict:
             entry["wavefront_step"] = measure_wavefront_step(args, dev)
         out[name] = entry
     return out
+
+
+def measure_host_issue(args, wl: DeviceWorkload, splits: int, mbps: int) -> dict:
+    """Host cost of the Python boundary: the layer sequence issued eagerly (DecodeAttention
+    from Python, ctypes into the C ABI, one kernel launch per call) `reps` times.  host_us is
+    the wall time to issue one call (no synchronisation inside the loop); eager_us the time
+    per call until the GPU has finished them all, against the graph replay's per-call time."""
+    a = argparse.Namespace(splits=splits, min_blocks_per_split=mbps, overlap_launch=False)
+    attn = make_attention(wl, a)
+    run_step(attn, wl)
+    torch.cuda.synchronize(wl.dev)
+    reps = 10
+    calls = reps * len(wl.layers)
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        run_step(attn, wl)
+    t1 = time.perf_counter()
+    torch.cuda.synchronize(wl.dev)
+    t2 = time.perf_counter()
+    attn.check_errors()
+    return {"calls": calls, "host_us_per_call": round((t1 - t0) / calls * 1e6, 2),
+            "eager_us_per_call": round((t2 - t0) / calls * 1e6, 2),
+            "what": "DecodeAttention.multi_from_raw issued from Python per layer, no graph"}
 
 
 def measure_wavefront_step(args, dev, layers: int = 20) -> dict:

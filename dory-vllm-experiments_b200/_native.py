@@ -168,6 +168,14 @@ def check_devices(device, *tensors) -> None:
             raise ValueError(f"a tensor argument is on {t.device}; this call runs on {device}")
 
 
+def check_device_index(index: int, *tensors) -> None:
+    """check_devices by device index (Tensor.get_device(): -1 for host memory), the form the
+    per-call launch paths use: comparing torch.device objects costs more than the launch."""
+    for t in tensors:
+        if t is not None and t.get_device() != index:
+            raise ValueError(f"a tensor argument is on {t.device}; this call runs on cuda:{index}")
+
+
 def check(status: int) -> None:
     """Maps a DoryStatus to the reference's exception types (ValueError for bad arguments)."""
     if status == OK:

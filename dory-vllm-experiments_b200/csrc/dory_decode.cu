@@ -1757,8 +1757,9 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   // (release is cumulative).
   named_barrier_consumers();
   if constexpr (DM) {
-    // One wave (every CTA of the grid resident at once): the last active split, which
-    // holds the newest positions and usually finishes last, merges.  The others publish
+    // Designated merger (see one_wave: the grid is resident at once, or its mergers cannot
+    // hold every slot): the last active split, which holds the newest positions and
+    // usually finishes last, merges.  The others publish
     // their partials with a release add that they do not wait for, and exit; the merger
     // waits (bounded) for all of them with acquire loads, then resets the counter for the
     // next launch.  Its poll typically finds them done: no round trip of its own atomic.
@@ -1783,7 +1784,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     }
     named_barrier_consumers();
   } else {
-    // Several waves: the last CTA of this (group, KV head) to arrive merges; its acquire,
+    // Otherwise: the last CTA of this (group, KV head) to arrive merges; its acquire,
     // passed on by the second barrier, makes the other CTAs' partials visible to it.
     if (tid == 0) {
       int32_t* counter = p.counters + gstart * p.NKV + kvh;
@@ -2177,8 +2178,14 @@ int32_t launch(const KParams& kp, dim3 grid, int smem_bytes, cudaStream_t stream
 
 int sm_count();
 
-// Whether `grid` CTAs of `fn` with `smem` bytes of dynamic shared memory are all resident
-// at once on the current device (occupancy per SM x SMs), cached per kernel and size.
+// Whether the designated-merger scheme may run `grid` CTAs of `fn` with `smem` bytes of
+// dynamic shared memory (occupancy per SM x SMs = the resident slots, cached per kernel and
+// size).  Only the mergers wait, one per (token, KV head): the others always run to their
+// end.  So the grid cannot stall when the whole grid is resident at once, or when the
+// mergers alone (grid.y x grid.z at most) leave a slot free, through which every sibling a
+// merger waits for is eventually dispatched (a programmatic dependent grid is launched only
+// once every CTA of the previous one has started, so its CTAs never hold slots that one
+// still needs).
 template <typename F>
 bool one_wave(F fn, dim3 grid, int smem) {
   struct Entry {
@@ -2191,10 +2198,15 @@ bool one_wave(F fn, dim3 grid, int smem) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return false;
   const long long ctas = (long long)grid.x * grid.y * grid.z;
+  const long long mergers = (long long)grid.y * grid.z;
+  auto fits = [&](int per_sm) {
+    const long long slots = (long long)per_sm * sm_count();
+    return ctas <= slots || mergers < slots;
+  };
   std::lock_guard<std::mutex> lock(mu);
   for (int i = 0; i < used; ++i)
     if (cache[i].fn == (const void*)fn && cache[i].dev == dev && cache[i].smem == smem)
-      return ctas <= (long long)cache[i].per_sm * sm_count();
+      return fits(cache[i].per_sm);
   int per_sm = 0;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            Smem<256, 8>::bytes(kMaxSub)) != cudaSuccess ||
@@ -2202,7 +2214,7 @@ bool one_wave(F fn, dim3 grid, int smem) {
     per_sm = 0;
   cudaGetLastError();
   if (used < 64) cache[used++] = Entry{(const void*)fn, dev, smem, per_sm};
-  return ctas <= (long long)per_sm * sm_count();
+  return fits(per_sm);
 }
 
 // Ring stages per instantiation: a multiple of the four consumer warps, so every stage keeps

@@ -100,6 +100,16 @@ class DecodeAttention:
                                                              stream))
         self._params = _native.DoryDecodeParams()
         self._params_ref = ctypes.byref(self._params)
+        self._dev_index = self.scratch.get_device()
+        # Fields fixed for this instance are set once; _launch sets the per-call ones.
+        p = self._params
+        p.scratch, p.scratch_bytes = self.scratch.data_ptr(), self.scratch.numel()
+        p.num_heads, p.num_kv_heads, p.head_dim = num_heads, num_kv_heads, head_dim
+        p.splits, p.blocks_per_tile = splits, blocks_per_tile
+        p.min_blocks_per_split, p.max_tokens = min_blocks_per_split, max_tokens
+        p.prefetch_chunks = self.prefetch_chunks
+        self._base_flags = ((_native.FLAG_OVERLAP_LAUNCH if self.overlap_launch else 0) |
+                            (_native.FLAG_FMA_CONSUMER if consumer == "fma" else 0))
 
     # ---- the reference's three entry points ----
 
@@ -200,20 +210,20 @@ class DecodeAttention:
             raise ValueError("key and value caches must be bfloat16")
         if not key_cache.is_cuda:
             raise RuntimeError("DecodeAttention runs on CUDA tensors only (no CPU path)")
-        if key_cache.device != self.scratch.device:
+        dev = self._dev_index
+        if key_cache.get_device() != dev:
             raise ValueError(f"caches on {key_cache.device}, this instance's scratch on "
                              f"{self.scratch.device}")
-        _native.check_devices(key_cache.device, q, value_cache, block_table, seq_lens, gate,
-                              out_nibble_major, out_sumsq, cache_offsets, block_table_offsets,
-                              *(raw[:2] + raw[4:] if raw is not None else ()))
+        _native.check_device_index(dev, q, value_cache, block_table, seq_lens, gate,
+                                   out_nibble_major, out_sumsq, cache_offsets,
+                                   block_table_offsets,
+                                   *(raw[:2] + raw[4:] if raw is not None else ()))
         if key_cache.shape[-1] != self.head_dim or key_cache.shape[-2] != self.num_kv_heads:
             raise ValueError("cache view must be [blocks, block_size, kv_heads, head_dim]")
         if block_table.dtype != torch.int32 or seq_lens.dtype != torch.int32:
             raise ValueError("block tables and seq_lens must be int32")
         p = self._params
-        flags = _native.FLAG_OVERLAP_LAUNCH if self.overlap_launch else 0
-        if self.consumer == "fma":
-            flags |= _native.FLAG_FMA_CONSUMER
+        flags = self._base_flags
         if raw is not None:
             v, sqk, sqk_factor, eps, slot_mapping = raw
             if q.dtype != torch.float32 or v.dtype != torch.float32:
@@ -253,15 +263,15 @@ class DecodeAttention:
             p.out_sumsq = out_sumsq.data_ptr()
         else:
             p.out_sumsq = None
-        p.scratch, p.scratch_bytes = self.scratch.data_ptr(), self.scratch.numel()
-        p.stride_block, p.stride_offset, p.stride_head = key_cache.stride(0), key_cache.stride(1), key_cache.stride(2)
-        p.num_cache_blocks = key_cache.shape[0]
+        ks = key_cache.stride()
+        p.stride_block, p.stride_offset, p.stride_head = ks[0], ks[1], ks[2]
+        shape = key_cache.shape
+        p.num_cache_blocks, p.block_size = shape[0], shape[1]
         p.softmax_scale = float(softmax_scale)
-        p.num_tokens, p.num_heads, p.num_kv_heads = tokens, self.num_heads, self.num_kv_heads
-        p.head_dim, p.block_size, p.window = self.head_dim, key_cache.shape[1], int(window)
-        p.splits, p.blocks_per_tile = self.splits, self.blocks_per_tile
-        p.min_blocks_per_split, p.max_tokens = self.min_blocks_per_split, self.max_tokens
-        p.flags = flags
-        p.prefetch_chunks = self.prefetch_chunks
-        stream = torch.cuda.current_stream(key_cache.device).cuda_stream
-        _native.check(self._lib.dory_decode_attention(self._params_ref, stream))
+        p.num_tokens, p.window, p.flags = tokens, int(window), flags
+        # the current stream's handle (torch.cuda.current_stream(dev).cuda_stream, without
+        # building the Stream object)
+        stream = torch._C._cuda_getCurrentRawStream(dev)
+        status = self._lib.dory_decode_attention(self._params_ref, stream)
+        if status:
+            _native.check(status)
