@@ -822,38 +822,46 @@ def measure_wavefront_step(args, dev, layers: int = 20) -> dict:
             (torch.randn(NH * HD, device=dev, generator=gd) * 0.02).to(torch.bfloat16), 0,
             HD ** -0.5))
     splits, mbps = tuned_splits("config2", 1)
-    attn = DecodeAttention(NH, NKV, HD, dev, splits=splits, max_tokens=rows,
-                           min_blocks_per_split=mbps)
-    block = WavefrontRecurrentBlock(attn, subs, table, NH * HD, W.SQK_FACTOR, 0.9, 2.5, EPS)
-    for i in range(layers):
-        block.qkvg_partials(i, rows).normal_(generator=gd)
-        block.out_partials(i, rows).normal_(generator=gd)
     positions = torch.arange(position, position + rows, dtype=torch.int64, device=dev)
     seq_lens = (positions + 1).to(torch.int32)
     h_in = torch.randn(rows, NH * HD, device=dev, generator=gd).to(torch.bfloat16)
-    block.replay(rows, positions, seq_lens, h_in)  # plain launches, then the capture
-    for _ in range(args.warmup):
-        block.replay(rows, positions, seq_lens, h_in)
-    steps = OTHER_STEPS
-    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize(dev)
-    with ClockSampler(dev) as clocks:
-        start.record()
-        for _ in range(steps):
-            block.replay(rows, positions, seq_lens, h_in)
-        end.record()
-        torch.cuda.synchronize(dev)
-    attn.check_errors()
-    us = start.elapsed_time(end) * 1e3 / steps
     lens = [position + t + 1 for t in range(rows)]
     per_layer = algorithmic_bytes(lens, True, 0, NH, NKV, HD, QKVG_SPLIT_K, NH * HD)
-    return {"what": "20 recurrent attention sublayers of one wavefront step (4 rows at loop "
-                    "depths 3..0, positions 2710..2713): q/k/v/gate epilogue, multi_from_raw "
-                    "on the shared cache with the output statistic, residual update; one CUDA "
-                    "graph, GEMV partials seeded",
-            "us_per_wavefront_step": round(us, 3), "us_per_layer": round(us / layers, 3),
-            "launches_per_step": 3 * layers, "steps": steps,
-            "hbm_gbs": round(per_layer * layers / (us * 1e-6) / 1e9, 1), "clocks": clocks.summary()}
+    out = {"what": "20 recurrent attention sublayers of one wavefront step (4 rows at loop "
+                   "depths 3..0, positions 2710..2713): q/k/v/gate epilogue, multi_from_raw "
+                   "on the shared cache with the output statistic, residual update; one CUDA "
+                   "graph, GEMV partials seeded",
+           "launches_per_step": 3 * layers}
+    for overlap in (False, True):
+        attn = DecodeAttention(NH, NKV, HD, dev, splits=splits, max_tokens=rows,
+                               min_blocks_per_split=mbps, overlap_launch=overlap)
+        block = WavefrontRecurrentBlock(attn, subs, table, NH * HD, W.SQK_FACTOR, 0.9, 2.5, EPS)
+        for i in range(layers):
+            block.qkvg_partials(i, rows).normal_(generator=gd)
+            block.out_partials(i, rows).normal_(generator=gd)
+        block.replay(rows, positions, seq_lens, h_in)  # plain launches, then the capture
+        for _ in range(args.warmup):
+            block.replay(rows, positions, seq_lens, h_in)
+        steps = OTHER_STEPS
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        with ClockSampler(dev) as clocks:
+            start.record()
+            for _ in range(steps):
+                block.replay(rows, positions, seq_lens, h_in)
+            end.record()
+            torch.cuda.synchronize(dev)
+        attn.check_errors()
+        us = start.elapsed_time(end) * 1e3 / steps
+        res = {"us_per_wavefront_step": round(us, 3), "us_per_layer": round(us / layers, 3),
+               "steps": steps, "hbm_gbs": round(per_layer * layers / (us * 1e-6) / 1e9, 1),
+               "clocks": clocks.summary()}
+        if overlap:
+            out["overlap_launch"] = res  # the three kernels of each layer chained as PDL
+        else:
+            out.update(res)
+        del block, attn
+    return out
 
 
 def l2_note(wl: DeviceWorkload) -> str:
