@@ -273,14 +273,15 @@ def workload_spec(name: str) -> Spec:
 
 
 def algorithmic_bytes(seq_lens, shared: bool, window: int, nh: int, nkv: int, hd: int,
-                      split_k: int = 0, residual_hidden: int = 0) -> int:
+                      split_k: int = 0, residual_hidden: int = 0, kv_bytes: int = 2) -> int:
     """Bytes one launch must move: unique attended positions x the K/V row bytes (the new
     rows written, the rest read) + per-token q/k/v/gate reads and out writes (FP32) + sqk
     + the block-table entries of the attended range + seq_lens.  With a sliding window w a
     token attends [max(seq_len - w, 0), seq_len); a shared-cache group reads the union of
     its tokens' ranges once.  split_k: the q/k/v/gate epilogue's I/O replaces the q/k/v/gate
-    reads; residual_hidden: the residual update's I/O is added (the sublayer chain)."""
-    kv_row = nkv * hd * 2 * 2
+    reads; residual_hidden: the residual update's I/O is added (the sublayer chain);
+    kv_bytes: bytes per cache element (2 bf16, 1 e4m3)."""
+    kv_row = nkv * hd * 2 * kv_bytes
     token_io = ((nh + nkv) * hd + nkv * hd + 2 * nh * hd) * 4
     extra = 0
     if split_k:
@@ -326,12 +327,14 @@ class DeviceWorkload:
     the pool count, and `reps` is the smallest count whose distinct pools exceed
     MIN_REPLAY_BYTES (1 for every workload whose layers alone exceed it)."""
 
-    def __init__(self, spec: Spec, lens, dev, seed, mem_fraction=0.5):
+    def __init__(self, spec: Spec, lens, dev, seed, mem_fraction=0.5, kv_dtype: str = "bf16"):
         tokens_per_seq, shared, layers = spec.tokens_per_seq, spec.shared, spec.layers
         pool_factor = spec.pool_factor
         self.spec = spec
         self.nh, self.nkv, self.hd = NH_, NKV_, HD_ = spec.nh, spec.nkv, spec.hd
-        self.kv_row_bytes = NKV_ * HD_ * 2 * 2  # K and V of one position, all KV heads
+        self.kv8 = kv_dtype == "fp8"
+        self.kv_bytes = 1 if self.kv8 else 2
+        self.kv_row_bytes = NKV_ * HD_ * 2 * self.kv_bytes  # K and V of one position
         self.dev = dev
         self.lens = lens
         self.shared = shared
@@ -382,8 +385,18 @@ class DeviceWorkload:
         gd = torch.Generator(device=dev).manual_seed(seed)
         self.raws, self.keys, self.values = [], [], []
         for _ in range(self.num_pools):
-            raw, key, value = W.cache_views(blocks, BLOCK, NKV_, HD_, "triton", dev)
-            raw.normal_(generator=gd)
+            if self.kv8:
+                # e4m3 bytes of N(0, 1) values (scales 1), drawn in slices to bound the
+                # temporary FP32 buffer
+                raw, key, value = W.cache_views(blocks, BLOCK, NKV_, HD_, "triton", dev,
+                                                torch.uint8)
+                for i in range(0, blocks, 4096):
+                    part = raw[i:i + 4096]
+                    part.copy_(W.e4m3_bytes(torch.randn(part.shape, device=dev, generator=gd),
+                                            1.0))
+            else:
+                raw, key, value = W.cache_views(blocks, BLOCK, NKV_, HD_, "triton", dev)
+                raw.normal_(generator=gd)
             self.raws.append(raw)
             self.keys.append(key)
             self.values.append(value)
@@ -407,7 +420,8 @@ class DeviceWorkload:
         return algorithmic_bytes(self.seq_lens_list, self.shared, self.window(layer),
                                  self.nh, self.nkv, self.hd,
                                  QKVG_SPLIT_K if self.path in ("qkvg", "sublayer") else 0,
-                                 self.hidden if self.path == "sublayer" else 0)
+                                 self.hidden if self.path == "sublayer" else 0,
+                                 self.kv_bytes)
 
     def algorithmic_bytes_per_step(self) -> int:
         return sum(self.algorithmic_bytes_per_application(layer) for layer in self.layers)
@@ -420,7 +434,8 @@ def make_attention(wl: DeviceWorkload, args):
                            min_blocks_per_split=args.min_blocks_per_split,
                            overlap_launch=getattr(args, "overlap_launch", False),
                            prefetch_chunks=getattr(args, "prefetch_chunks", 0),
-                           consumer=getattr(args, "consumer", "mma"))
+                           consumer=getattr(args, "consumer", "mma"),
+                           kv_cache_dtype="fp8" if wl.kv8 else "auto")
 
 
 def prepare_call_path(wl: DeviceWorkload):
@@ -641,9 +656,11 @@ def bench_ours(args, world, rank, local):
         mine = rank_sequences(args.workload, lens_all, world, rank)
         scaling = "strong"
     lens = [lens_all[i] for i in mine]
-    wl = DeviceWorkload(spec, lens, dev, spec.seed + 1000 * rank)
+    wl = DeviceWorkload(spec, lens, dev, spec.seed + 1000 * rank, kv_dtype=args.kv_dtype)
     if args.sumsq:
         wl.sumsq = torch.zeros(wl.num_layers, wl.tokens, device=dev)
+    if args.kv_dtype == "fp8" and (args.path != "fused" or spec.shared):
+        raise SystemExit("--kv-dtype fp8 takes the fused path of unshared workloads")
     if args.path in ("separate", "call") and wl.tokens != 1:
         raise SystemExit(f"--path {args.path} takes single-sequence workloads "
                          "(config1, config4, dory*)")
@@ -678,17 +695,17 @@ def bench_ours(args, world, rank, local):
               "l2": l2_note(wl),
               "splits": args.splits, "min_blocks_per_split": args.min_blocks_per_split,
               "overlap_launch": args.overlap_launch, "path": args.path,
-              "consumer": args.consumer,
+              "consumer": args.consumer, "kv_dtype": args.kv_dtype,
               "out_sumsq": bool(args.sumsq)}
     del attn, wl
     torch.cuda.synchronize(dev)
     torch.cuda.empty_cache()
 
     cpu, extra = None, None
-    if rank == 0 and world == 1:
+    if rank == 0 and world == 1 and args.kv_dtype == "bf16":
         cpu = cpu_baseline(args.workload, args.cpu_seconds)
         if (args.all_configs and args.workload == "config5" and args.path == "fused"
-                and args.consumer == "mma"):
+                and args.consumer == "mma" and args.kv_dtype == "bf16"):
             extra = measure_other_configs(args, dev)
 
     line = {
@@ -1293,6 +1310,9 @@ def main() -> int:
                     help="dot products of the chunk step: mma.sync tensor-core tiles (the "
                          "product) or FP32 FMAs on the CUDA cores (the measured alternative; "
                          "128-dim heads, no shared cache)")
+    ap.add_argument("--kv-dtype", choices=("bf16", "fp8"), default="bf16",
+                    help="cache element type: bf16 (the reference's) or fp8 e4m3 (vLLM's fp8 "
+                         "kv_cache_dtype, scales 1; single sequences and independent batches)")
     ap.add_argument("--sumsq", action="store_true",
                     help="also produce each token's sum of squared outputs (out_sumsq)")
     ap.add_argument("--all-configs", action=argparse.BooleanOptionalAction, default=True,

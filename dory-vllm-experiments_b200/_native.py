@@ -13,12 +13,12 @@ from pathlib import Path
 HERE = Path(__file__).resolve().parent
 LIBRARY = HERE / "libdory_decode.so"
 
-ABI_VERSION = 7
+ABI_VERSION = 8
 
 # DoryStatus
 OK, ERR_INVALID_ARGUMENT, ERR_UNSUPPORTED, ERR_ALIGNMENT, ERR_CUDA = range(5)
 # DoryDType
-DTYPE_F32, DTYPE_BF16, DTYPE_F16 = range(3)
+DTYPE_F32, DTYPE_BF16, DTYPE_F16, DTYPE_FP8_E4M3 = range(4)
 # DORY_FLAG_*
 FLAG_RAW_QKV, FLAG_MULTI_TOKEN, FLAG_SHARED_CACHE, FLAG_OVERLAP_LAUNCH = 1, 2, 4, 8
 FLAG_FMA_CONSUMER = 16
@@ -59,7 +59,8 @@ class DoryDecodeParams(ctypes.Structure):
         ("num_tokens", _i32), ("num_heads", _i32), ("num_kv_heads", _i32), ("head_dim", _i32),
         ("block_size", _i32), ("window", _i32), ("splits", _i32), ("blocks_per_tile", _i32),
         ("min_blocks_per_split", _i32), ("max_tokens", _i32), ("sqk_dtype", _i32),
-        ("flags", _u32), ("prefetch_chunks", _i32),
+        ("flags", _u32), ("prefetch_chunks", _i32), ("kv_dtype", _i32),
+        ("k_scale", _f32), ("v_scale", _f32),
     ]
 
 

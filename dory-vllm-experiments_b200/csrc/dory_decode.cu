@@ -105,6 +105,7 @@ struct alignas(64) KParams {
   int min_bps, sqk_dtype, overlap;
   int pf;        // L2 prefetch distance in chunks beyond the ring (0: none)
   int tm_mode;   // 0: no tensor maps; 1: tmk covers K and V (V right after K); 2: tmk, tmv
+  float k_scale, v_scale;  // FP8 cache: K = e4m3 * k_scale, V = e4m3 * v_scale
   CUtensorMap tmk;  // cache views as 5-D tensors (64 dims, rows, 64-dim quarters of a row,
   CUtensorMap tmv;  // KV head, block), one box = a chunk's K (and V) tile, 128-byte swizzle
 };
@@ -155,12 +156,23 @@ constexpr int kBoxBytes = kChunk * 128;
 __host__ __device__ constexpr uint32_t tile_off(int r, int d) {  // d: a multiple of 8
   return uint32_t((d >> 6) * kBoxBytes + r * 128 + ((((d >> 3) & 7) ^ (r & 7)) << 4));
 }
-template <int HD, int NS>
+// FP8 (e4m3) caches: a 16-row tile is HD / 128 boxes of [16 rows][128 dims] bytes in the same
+// 128-byte swizzle; piece j (dims 16j .. 16j + 15) of row r of a box sits at
+// r * 128 + ((j ^ (r % 8)) * 16).  d: a multiple of 16.
+__host__ __device__ constexpr uint32_t tile_off8(int r, int d) {
+  return uint32_t((d >> 7) * kBoxBytes + r * 128 + ((((d >> 4) & 7) ^ (r & 7)) << 4));
+}
+template <int HD, int NS, bool KV8 = false>
 struct Smem {
-  static constexpr int kTileBytes = (HD / 64) * kBoxBytes;    // one K (or V) tile
+  static constexpr int kTile16 = (HD / 64) * kBoxBytes;       // a 16-bit K (or V) tile
+  static constexpr int kTileBytes = KV8 ? (HD / 128) * kBoxBytes : kTile16;  // as copied
   static constexpr int kStageBytes = 2 * kTileBytes;
   static constexpr int kStages = 0;                           // 1024-byte aligned at run time
-  static constexpr int kBars = kStages + NS * kStageBytes;    // full[NS], empty[NS]
+  // FP8: each consumer warp's K and V tiles dequantized to f16 (the 16-bit tile layout)
+  static constexpr int kStaging = kStages + NS * kStageBytes;
+  static constexpr int kStagingBytes = KV8 ? kConsumerWarps * 2 * kTile16 : 0;
+  static constexpr int kRegion = NS * kStageBytes + kStagingBytes;  // reused after the loop
+  static constexpr int kBars = kStaging + kStagingBytes;      // full[NS], empty[NS]
   static constexpr int kMeta = kBars + 2 * NS * 8;            // int4 {phys, -, chunk, -}
   static constexpr int kQ = kMeta + NS * 16;                  // bf16 [16][HD]
   static constexpr int kSub = kQ + 16 * HD * 2;               // bf16 [nsub][2][HD]
@@ -298,11 +310,96 @@ __device__ __forceinline__ void mma_bf16(float (&d)[4], uint32_t a0, uint32_t a1
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ void mma_f16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                        uint32_t a3, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// Two e4m3 values (the low byte is the lower element) to f16x2: every e4m3 value is an f16.
+__device__ __forceinline__ uint32_t e4m3x2_to_f16x2(uint32_t two_bytes) {
+  uint32_t r;
+  asm("cvt.rn.f16x2.e4m3x2 %0, %1;" : "=r"(r) : "h"(static_cast<uint16_t>(two_bytes)));
+  return r;
+}
+// Two FP32 values to e4m3 (round to nearest even, saturating at +-448): lo in the low byte.
+__device__ __forceinline__ uint32_t f32x2_to_e4m3x2(float lo, float hi) {
+  uint16_t r;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// bf16x2 (lower element in the low half) to f16x2, exact for the normal f16 range.
+__device__ __forceinline__ uint32_t bf16x2_to_f16x2(uint32_t x) {
+  const float lo = __uint_as_float(x << 16), hi = __uint_as_float(x & 0xffff0000u);
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+// P for an f16 MMA: each value rounded to bf16 first (the P.V operand precision of the
+// bf16 path), then packed as f16x2 (exact for the rounded values of the normal f16 range).
+__device__ __forceinline__ uint32_t pack_p_f16x2(float lo, float hi) {
+  const float l = __bfloat162float(__float2bfloat16_rn(lo));
+  const float h = __bfloat162float(__float2bfloat16_rn(hi));
+  uint32_t r;
+  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(h), "f"(l));
+  return r;
+}
+// x rounded to the nearest e4m3 value (ties to even, saturating at +-448), as FP32.
+__device__ __forceinline__ float e4m3_round(float x) {
+  const uint32_t h2 = e4m3x2_to_f16x2(f32x2_to_e4m3x2(x, 0.0f));
+  return __half2float(__ushort_as_half(static_cast<unsigned short>(h2 & 0xffffu)));
+}
+// A new token's k (normalised) or v value as the kernel keeps it: bf16, or for an FP8 cache
+// the e4m3 value of bf16(x) / scale (as bf16, exact), the value appended and attended.
+template <bool KV8>
+__device__ __forceinline__ __nv_bfloat16 new_kv(float x, float scale) {
+  if constexpr (KV8)
+    return __float2bfloat16_rn(e4m3_round(__bfloat162float(__float2bfloat16_rn(x)) / scale));
+  else
+    return __float2bfloat16_rn(x);
+}
+template <bool F16>
+__device__ __forceinline__ void mma16(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2,
+                                      uint32_t a3, uint32_t b0, uint32_t b1) {
+  if constexpr (F16) mma_f16(d, a0, a1, a2, a3, b0, b1);
+  else mma_bf16(d, a0, a1, a2, a3, b0, b1);
+}
+// FP8 stage -> this warp's f16 tiles: K and V of a 16-row chunk (K first) into the 16-bit
+// tile layout (tile_off), rows outside [lo, hi) or of a bad block (phys < 0) as zeros.
+template <int HD>
+__device__ __forceinline__ void dequant_stage(const uint8_t* st8, uint8_t* k16, int c, int phys,
+                                              int lo, int hi, int lane) {
+  constexpr int TILE8 = (HD / 128) * kBoxBytes, TILE16 = (HD / 64) * kBoxBytes;
+  constexpr int PIECES = kChunk * (HD / 16);  // 16-byte pieces of 16 e4m3 per tile
+#pragma unroll
+  for (int k = 0; k < 2 * PIECES / 32; ++k) {
+    const int idx = k * 32 + lane;
+    const bool is_v = idx >= PIECES;
+    const int j = is_v ? idx - PIECES : idx;
+    const int r = j / (HD / 16), d = (j % (HD / 16)) * 16;
+    const int pos = c * kChunk + r;
+    const bool ok = phys >= 0 && pos >= lo && pos < hi;
+    uint4 lo8 = make_uint4(0u, 0u, 0u, 0u), hi8 = make_uint4(0u, 0u, 0u, 0u);
+    if (ok) {
+      const uint4 w = *reinterpret_cast<const uint4*>(st8 + (is_v ? TILE8 : 0) + tile_off8(r, d));
+      lo8 = make_uint4(e4m3x2_to_f16x2(w.x & 0xffffu), e4m3x2_to_f16x2(w.x >> 16),
+                       e4m3x2_to_f16x2(w.y & 0xffffu), e4m3x2_to_f16x2(w.y >> 16));
+      hi8 = make_uint4(e4m3x2_to_f16x2(w.z & 0xffffu), e4m3x2_to_f16x2(w.z >> 16),
+                       e4m3x2_to_f16x2(w.w & 0xffffu), e4m3x2_to_f16x2(w.w >> 16));
+    }
+    uint8_t* dst = k16 + (is_v ? TILE16 : 0);
+    *reinterpret_cast<uint4*>(dst + tile_off(r, d)) = lo8;
+    *reinterpret_cast<uint4*>(dst + tile_off(r, d + 8)) = hi8;
+  }
+}
+
 // O^T += V^T P^T over one 16-row stage (256-dim heads): [16 dims x 8 rows] per m-tile (k-step
 // kk) and n-tile.  Lane l gives ldmatrix the address of V row (l & 7) + 8 * (l >> 4) of its
 // matrix; MASK: a lane whose row is outside the attended range (row_ok false) gives the
 // address of a zeroed 16-byte row instead, so that row enters the MMA as zeros.
-template <int KT, int NT, bool MASK>
+template <int KT, int NT, bool MASK, bool F16 = false>
 __device__ __forceinline__ void pv_accumulate(float (&o)[NT][KT][4], uint32_t vbase_s, int lane,
                                               const uint32_t (&pb)[NT][2], bool row_ok,
                                               uint32_t zero_row) {
@@ -313,7 +410,7 @@ __device__ __forceinline__ void pv_accumulate(float (&o)[NT][KT][4], uint32_t vb
     const uint32_t addr = vbase_s + tile_off(vr, kk * 16 + vd);
     ldsm_x4_t((MASK && !row_ok) ? zero_row : addr, a0, a1, a2, a3);
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) mma_bf16(o[nt][kk], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+    for (int nt = 0; nt < NT; ++nt) mma16<F16>(o[nt][kk], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
   }
 }
 __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
@@ -797,11 +894,12 @@ __device__ __forceinline__ void sumsq_tail(const KParams& p, const float* sv, in
 // ------------------------------------------------------------------------------------
 // The kernel.  grid = (splits, NKV, T); block = 160 threads (4 consumer warps + producer).
 // ------------------------------------------------------------------------------------
-template <int HD, int NT, int NS, bool SS, bool DM, bool FMA = false>
+template <int HD, int NT, int NS, bool SS, bool DM, bool FMA = false, bool KV8 = false>
 __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     decode_kernel(const __grid_constant__ KParams p) {
   static_assert(!FMA || (HD == 128 && NT == 1), "the CUDA-core consumer is 128-dim, one tile");
-  using L = Smem<HD, NS>;
+  static_assert(!KV8 || (NT == 1 && !FMA && HD >= 128), "FP8 caches: 128/256-dim, one tile");
+  using L = Smem<HD, NS, KV8>;
   constexpr int KT = HD / 16;          // MMA k-steps over head_dim / m-tiles of O^T
   constexpr int ROWS = NT * 8;         // query rows per CTA
   constexpr int PER_LANE = HD / 32;    // elements per lane in row-wise prologue math
@@ -1018,6 +1116,12 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     }
     __syncwarp();
     pipeline_ready_arrive();
+    if (KV8 && !use_tma) {
+      // FP8 caches are copied by tensor maps only (a cache offset that is not whole blocks,
+      // or a cache beyond the map): recorded, and the consumers skip the chunks.
+      if (lane == 0) record_error(p.err, DORY_DEVERR_OFFSET_ALIGN);
+      return;
+    }
     // Tensor path (the usual one): lane 0 publishes the stage's block id, arms full[stage]
     // with the stage's byte count and issues one box copy of the chunk's K and V tiles
     // (two, K then V, when V does not directly follow K in memory): 16 rows from row 0 of
@@ -1269,8 +1373,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
 #pragma unroll
         for (int i = 0; i < PER_LANE; ++i) {
           const int d = lane * PER_LANE + i;
-          subkv[(warp * 2 + 0) * HD + d] = __float2bfloat16_rn(__fmul_rn(kv0[i], rn));
-          subkv[(warp * 2 + 1) * HD + d] = __float2bfloat16_rn(vv0[i]);
+          subkv[(warp * 2 + 0) * HD + d] = new_kv<KV8>(__fmul_rn(kv0[i], rn), p.k_scale);
+          subkv[(warp * 2 + 1) * HD + d] = new_kv<KV8>(vv0[i], p.v_scale);
         }
       }
     } else {
@@ -1349,8 +1453,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
 #pragma unroll
       for (int i = 0; i < PER_LANE; ++i) {
         const int d = lane * PER_LANE + i;
-        subkv[(warp * 2 + 0) * HD + d] = __float2bfloat16_rn(__fmul_rn(kv0[i], rn));
-        subkv[(warp * 2 + 1) * HD + d] = __float2bfloat16_rn(vv0[i]);
+        subkv[(warp * 2 + 0) * HD + d] = new_kv<KV8>(__fmul_rn(kv0[i], rn), p.k_scale);
+        subkv[(warp * 2 + 1) * HD + d] = new_kv<KV8>(vv0[i], p.v_scale);
       }
     }
   }
@@ -1387,7 +1491,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
       }
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
-      if (lane == 0) s_newm[r] = dot * kLog2e;
+      if (lane == 0) s_newm[r] = dot * (KV8 ? kLog2e * p.k_scale : kLog2e);
     }
     // The append: the new k and v rows at the token's slot (a negative slot is a padding
     // token, which vLLM does not cache; a slot outside the cache is recorded and skipped).
@@ -1398,13 +1502,31 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
         if ((p.ncache_blocks > 0 && blk >= p.ncache_blocks) || !offset_ok) {
           if (lane == 0) record_error(p.err, DORY_DEVERR_SLOT_OOB);
         } else {
-          constexpr int kVec = HD / 8;
           const long long base = coff + blk * p.sb + (slot % B) * p.so + (long long)kvh * p.sh;
+          if constexpr (KV8) {
+            // e4m3 bytes (base in bytes): 16 per piece, from the exact e4m3 values in subkv
+            constexpr int kVec8 = HD / 16;
+            for (int idx = lane; idx < 2 * kVec8; idx += 32) {
+              const bool is_v = idx >= kVec8;
+              const int w = is_v ? idx - kVec8 : idx;
+              const __nv_bfloat16* src = subkv + (is_v ? HD : 0) + w * 16;
+              uint32_t b[8];
+#pragma unroll
+              for (int e = 0; e < 8; ++e)
+                b[e] = f32x2_to_e4m3x2(__bfloat162float(src[2 * e]), __bfloat162float(src[2 * e + 1]));
+              const uint4 val = make_uint4(b[0] | (b[1] << 16), b[2] | (b[3] << 16),
+                                           b[4] | (b[5] << 16), b[6] | (b[7] << 16));
+              uint8_t* dst = reinterpret_cast<uint8_t*>(is_v ? p.vc : p.kc) + base;
+              reinterpret_cast<uint4*>(dst)[w] = val;
+            }
+          } else {
+          constexpr int kVec = HD / 8;
           for (int idx = lane; idx < 2 * kVec; idx += 32) {
             const bool is_v = idx >= kVec;
             const int w = is_v ? idx - kVec : idx;
             const uint4 val = reinterpret_cast<const uint4*>(subkv + (is_v ? HD : 0))[w];
             reinterpret_cast<uint4*>((is_v ? p.vc : p.kc) + base)[w] = val;
+          }
           }
         }
       }
@@ -1420,8 +1542,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
 #pragma unroll
     for (int kk = 0; kk < KT; ++kk) {
       const uint32_t* row = reinterpret_cast<const uint32_t*>(q2 + (nt * 8 + g) * HD + kk * 16);
-      qb[nt][kk][0] = row[t4];
-      qb[nt][kk][1] = row[t4 + 4];
+      qb[nt][kk][0] = KV8 ? bf16x2_to_f16x2(row[t4]) : row[t4];
+      qb[nt][kk][1] = KV8 ? bf16x2_to_f16x2(row[t4 + 4]) : row[t4 + 4];
     }
   // Row bounds of the two query rows this lane accumulates per n-tile.
   int rfirst[NT][2], rlen[NT][2];
@@ -1447,6 +1569,11 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     m[nt][0] = m[nt][1] = -INFINITY;
     l[nt][0] = l[nt][1] = 0.0f;
   }
+  // FP8 caches: scores carry k_scale (folded into the log2 factor), outputs v_scale (applied
+  // to each warp's accumulator); the chunks run only with tensor-map copies.
+  const float kscore = KV8 ? kLog2e * p.k_scale : kLog2e;
+  const int nloop = (KV8 && !use_tma) ? 0 : nchunks;
+  uint8_t* k16 = smem + L::kStaging + warp * 2 * L::kTile16;  // KV8: this warp's f16 tiles
 
   bool failed = false;
   // CUDA-core consumer state (FMA instantiations only): the query rows as FP32 (the same
@@ -1504,7 +1631,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     fst.l += __shfl_xor_sync(0xffffffffu, fst.l, 2);
     fst.l += __shfl_xor_sync(0xffffffffu, fst.l, 4);
   } else {
-  for (int i = warp; i < nchunks; i += kConsumerWarps) {
+  for (int i = warp; i < nloop; i += kConsumerWarps) {
     const int stage = i % NS;
     const uint32_t parity = (i / NS) & 1;
     if (!mbar_wait(full_bar(stage), parity)) {
@@ -1520,11 +1647,22 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     // Boundary chunks, bad blocks and chunks holding a new token's row take the slow path
     // (zeroing, substitution, the append itself); the rest go straight to the math.
     bool touched = false;
-    const bool partial = use_tma && (c < c_full_lo || c >= c_full_hi || phys < 0);
+    const bool partial = !KV8 && use_tma && (c < c_full_lo || c >= c_full_hi || phys < 0);
+    if constexpr (KV8) {
+      // FP8: the stage to this warp's f16 tiles (rows outside the range as zeros), and the
+      // stage goes straight back to the ring.
+      dequant_stage<HD>(kst, k16, c, phys, s_ci.lo, s_ci.hi, lane);
+      kst = k16;
+      vst = k16 + L::kTile16;
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && i + NS < nchunks) issue_chunk(i + NS);
+    } else {
     if ((partial && !kRowMask) || (c >= sub_lo && c <= sub_hi) || any_foreign)
       touched = fixup_stage<HD>(p, kst, vst, c, phys, partial && !kRowMask, lane, s_ci, s_len,
                                 s_phys, s_coff, s_toff, subkv);
     __syncwarp();
+    }
 
     // S^T = K Q^T : [16 tokens x 8 rows] per n-tile, as two independent MMA chains (even
     // and odd k-steps) to halve the dependent latency.
@@ -1542,7 +1680,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
         ldsm_x4(kbase_s + tile_off(kr, kk * 16 + kd), a0, a1, a2, a3);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt)
-          mma_bf16((kk & 1) ? sc2[nt] : sc[nt], a0, a1, a2, a3, qb[nt][kk][0], qb[nt][kk][1]);
+          mma16<KV8>((kk & 1) ? sc2[nt] : sc[nt], a0, a1, a2, a3, qb[nt][kk][0], qb[nt][kk][1]);
       }
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
@@ -1561,8 +1699,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
       for (int i = 0; i < 2; ++i) {
         const bool v0 = pos0 >= rfirst[nt][i] && pos0 < rlen[nt][i];
         const bool v1 = pos1 >= rfirst[nt][i] && pos1 < rlen[nt][i];
-        const float x0 = v0 ? sc[nt][i] * kLog2e : -INFINITY;
-        const float x1 = v1 ? sc[nt][2 + i] * kLog2e : -INFINITY;
+        const float x0 = v0 ? sc[nt][i] * kscore : -INFINITY;
+        const float x1 = v1 ? sc[nt][2 + i] * kscore : -INFINITY;
         float tmax = fmaxf(x0, x1);
         tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 4));
         tmax = fmaxf(tmax, __shfl_xor_sync(0xffffffffu, tmax, 8));
@@ -1583,8 +1721,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
         o[nt][kk][3] *= alpha[1];
       }
       // accumulator [tok][row] -> operand P^T [k = tok][n = row] via 8x8 transposes
-      pb[nt][0] = movmatrix_t(pack_bf16x2(pv[0], pv[1]));
-      pb[nt][1] = movmatrix_t(pack_bf16x2(pv[2], pv[3]));
+      pb[nt][0] = movmatrix_t(KV8 ? pack_p_f16x2(pv[0], pv[1]) : pack_bf16x2(pv[0], pv[1]));
+      pb[nt][1] = movmatrix_t(KV8 ? pack_p_f16x2(pv[2], pv[3]) : pack_bf16x2(pv[2], pv[3]));
     }
     // O^T += V^T P^T : [16 dims x 8 rows] per m-tile and n-tile.
     if constexpr (kRowMask) {
@@ -1595,7 +1733,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
         const bool row_ok = phys >= 0 && pos >= s_ci.lo && pos < s_ci.hi;
         pv_accumulate<KT, NT, true>(o, smem_u32(vst), lane, pb, row_ok, smem_u32(&s_zero_row));
       } else {
-        pv_accumulate<KT, NT, false>(o, smem_u32(vst), lane, pb, true, 0u);
+        pv_accumulate<KT, NT, false, KV8>(o, smem_u32(vst), lane, pb, true, 0u);
       }
     } else {
       const uint32_t vbase_s = smem_u32(vst);
@@ -1605,10 +1743,12 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
         uint32_t a0, a1, a2, a3;
         ldsm_x4_t(vbase_s + tile_off(vr, kk * 16 + vd), a0, a1, a2, a3);
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) mma_bf16(o[nt][kk], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
+        for (int nt = 0; nt < NT; ++nt) mma16<KV8>(o[nt][kk], a0, a1, a2, a3, pb[nt][0], pb[nt][1]);
       }
     }
-    if (use_tma) {
+    if constexpr (KV8) {
+      // the stage was refilled after its dequantisation
+    } else if (use_tma) {
       // This warp's reads (and writes) of the stage, ordered before the copy that refills it.
       fence_proxy_async_smem();
       __syncwarp();
@@ -1680,10 +1820,11 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
         s_wl[warp][r] = l[nt][i];
       }
       float* dst = wo + (warp * ROWS + r) * OST;
+      const float vsc = KV8 ? p.v_scale : 1.0f;
 #pragma unroll
       for (int kk = 0; kk < KT; ++kk) {
-        dst[kk * 16 + g] = o[nt][kk][i];
-        dst[kk * 16 + g + 8] = o[nt][kk][2 + i];
+        dst[kk * 16 + g] = KV8 ? o[nt][kk][i] * vsc : o[nt][kk][i];
+        dst[kk * 16 + g + 8] = KV8 ? o[nt][kk][2 + i] * vsc : o[nt][kk][2 + i];
       }
     }
   }
@@ -1696,7 +1837,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   const int64_t S = p.S;
   // Squares of the stored outputs (sumsq), after the warps' buffers in the drained ring.
   constexpr int kSvOff = (kConsumerWarps * ROWS * OST * 4 + 15) & ~15;
-  static_assert(kSvOff + ROWS * (HD / 4) * 4 <= NS * L::kStageBytes, "sumsq buffer fits the ring");
+  static_assert(kSvOff + ROWS * (HD / 4) * 4 <= L::kRegion, "sumsq buffer fits the ring");
   float* sv = reinterpret_cast<float*>(smem + L::kStages + kSvOff);
   for (int it = tid; it < items; it += kConsumerWarps * 32) {
     const int r = it / IPR, k8 = it % IPR;
@@ -1722,8 +1863,9 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
       const float wt = fast_exp2(s_newm[r] - Muse);
       Lsum += wt;
       const __nv_bfloat16* vn = subkv + HD + k8 * 8;
+      const float vsn = KV8 ? wt * p.v_scale : wt;
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] += wt * __bfloat162float(vn[e]);
+      for (int e = 0; e < 8; ++e) acc[e] += vsn * __bfloat162float(vn[e]);
     }
     const int t = gstart + r / G;
     const int head = kvh * G + r % G;
@@ -2145,15 +2287,15 @@ int32_t fail(int32_t status, const char* fmt, ...) {
   return status;
 }
 
-template <int HD, int NT, int NS, bool SS, bool DM, bool FMA = false>
+template <int HD, int NT, int NS, bool SS, bool DM, bool FMA = false, bool KV8 = false>
 int32_t launch(const KParams& kp, dim3 grid, int smem_bytes, cudaStream_t stream) {
-  auto fn = decode_kernel<HD, NT, NS, SS, DM, FMA>;
+  auto fn = decode_kernel<HD, NT, NS, SS, DM, FMA, KV8>;
   static int configured[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return fail(DORY_ERR_CUDA, "cudaGetDevice failed");
   if (dev >= 0 && dev < 64 && !configured[dev]) {
     // The largest dynamic size any call of this instantiation can ask for.
-    const int max_bytes = Smem<HD, NS>::bytes(kMaxSub);
+    const int max_bytes = Smem<HD, NS, KV8>::bytes(kMaxSub);
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, max_bytes);
     if (e != cudaSuccess)
       return fail(DORY_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
@@ -2262,6 +2404,21 @@ int32_t dispatch_fma(const KParams& kp, dim3 grid, cudaStream_t stream) {
             : launch<128, 1, NS, false, false, true>(kp, grid, smem, stream);
 }
 
+// FP8 (e4m3) caches: one 8-row tile, the FP8 ring and per-warp f16 tiles.
+template <int HD>
+int32_t dispatch_kv8(const KParams& kp, dim3 grid, cudaStream_t stream) {
+  constexpr int NS = Depth<HD, 1>::value;
+  static_assert(kConsumerWarps * 8 * (HD + 4) * 4 <= Smem<HD, NS, true>::kRegion,
+                "the warps' merge buffer must fit in the ring and staging tiles");
+  const int smem = Smem<HD, NS, true>::bytes(kp.nsub);
+  const bool dm = one_wave(decode_kernel<HD, 1, NS, false, true, false, true>, grid, smem);
+  if (kp.sumsq)
+    return dm ? launch<HD, 1, NS, true, true, false, true>(kp, grid, smem, stream)
+              : launch<HD, 1, NS, true, false, false, true>(kp, grid, smem, stream);
+  return dm ? launch<HD, 1, NS, false, true, false, true>(kp, grid, smem, stream)
+            : launch<HD, 1, NS, false, false, false, true>(kp, grid, smem, stream);
+}
+
 template <int HD>
 int32_t dispatch_nt(const KParams& kp, int nt, dim3 grid, cudaStream_t stream) {
   if (nt == 1) return dispatch<HD, 1>(kp, grid, stream);
@@ -2288,9 +2445,10 @@ struct MapKey {
   const void* base;
   int64_t blocks, sb, so, sh;
   int B, NKV, quarters;
+  int esize;  // bytes per element: 2 (bf16), 1 (e4m3)
   bool operator==(const MapKey& o) const {
     return base == o.base && blocks == o.blocks && sb == o.sb && so == o.so && sh == o.sh &&
-           B == o.B && NKV == o.NKV && quarters == o.quarters;
+           B == o.B && NKV == o.NKV && quarters == o.quarters && esize == o.esize;
   }
 };
 struct MapEntry {
@@ -2319,13 +2477,18 @@ bool cache_tensor_map(const MapKey& k, CUtensorMap* out) {
   memset(&e.map, 0, sizeof(e.map));
   auto encode = tensor_map_encoder();
   if (encode && k.blocks > 0 && k.blocks <= 0x7fffffff && k.quarters <= 8) {
-    cuuint64_t dims[5] = {64, cuuint64_t(k.B), cuuint64_t(k.quarters), cuuint64_t(k.NKV),
+    // 128-byte rows of the box: 64 bf16 dims, or 128 e4m3 dims ("quarters" then counts
+    // 128-dim pieces)
+    const cuuint64_t inner = 128 / k.esize, es = cuuint64_t(k.esize);
+    cuuint64_t dims[5] = {inner, cuuint64_t(k.B), cuuint64_t(k.quarters), cuuint64_t(k.NKV),
                           cuuint64_t(k.blocks)};
-    cuuint64_t strides[4] = {cuuint64_t(k.so) * 2, 128, cuuint64_t(k.sh) * 2,
-                             cuuint64_t(k.sb) * 2};
-    cuuint32_t box[5] = {64, cuuint32_t(kChunk), cuuint32_t(k.quarters), 1, 1};
+    cuuint64_t strides[4] = {cuuint64_t(k.so) * es, 128, cuuint64_t(k.sh) * es,
+                             cuuint64_t(k.sb) * es};
+    cuuint32_t box[5] = {cuuint32_t(inner), cuuint32_t(kChunk), cuuint32_t(k.quarters), 1, 1};
     cuuint32_t estr[5] = {1, 1, 1, 1, 1};
-    CUresult r = encode(&e.map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 5, const_cast<void*>(k.base),
+    CUresult r = encode(&e.map, k.esize == 1 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                             : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                        5, const_cast<void*>(k.base),
                         dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                         CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                         CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -2578,6 +2741,9 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
   const bool shared = a.flags & DORY_FLAG_SHARED_CACHE;
   const bool overlap = a.flags & DORY_FLAG_OVERLAP_LAUNCH;
   const bool fma = a.flags & DORY_FLAG_FMA_CONSUMER;
+  if (a.kv_dtype != 0 && a.kv_dtype != DORY_DTYPE_BF16 && a.kv_dtype != DORY_DTYPE_FP8_E4M3)
+    return fail(DORY_ERR_INVALID_ARGUMENT, "kv_dtype %d (bf16 or fp8 e4m3)", a.kv_dtype);
+  const bool kv8 = a.kv_dtype == DORY_DTYPE_FP8_E4M3;
   if (a.num_tokens < 0) return fail(DORY_ERR_INVALID_ARGUMENT, "negative token count");
   if (a.num_tokens > a.max_tokens)
     return fail(DORY_ERR_INVALID_ARGUMENT, "too many tokens for the scratch buffers");
@@ -2602,6 +2768,12 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
     return fail(DORY_ERR_UNSUPPORTED, "block_size %d is not a multiple of 16", a.block_size);
   const int G = a.num_heads / a.num_kv_heads;
   if (G > 16) return fail(DORY_ERR_UNSUPPORTED, "%d query heads per KV head (max 16)", G);
+  if (kv8 && (HD < 128 || G > 8 || shared || fma || a.num_cache_blocks <= 0))
+    return fail(DORY_ERR_UNSUPPORTED,
+                "FP8 caches take 128/256-dim heads, at most 8 query heads per KV head, a "
+                "known block count, no shared cache and the tensor-core consumer");
+  if (kv8 && !(a.k_scale > 0.0f && a.v_scale > 0.0f && a.k_scale < 3.4e38f && a.v_scale < 3.4e38f))
+    return fail(DORY_ERR_INVALID_ARGUMENT, "FP8 caches need positive, finite k/v scales");
   if (fma && (HD != 128 || G > 4 || shared))
     return fail(DORY_ERR_UNSUPPORTED,
                 "the CUDA-core consumer takes 128-dim heads, at most 4 query heads per KV head "
@@ -2612,8 +2784,8 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
   if (reinterpret_cast<uintptr_t>(a.gate) & 15)
     return fail(DORY_ERR_ALIGNMENT, "gate needs a 16-byte aligned base");
   if ((reinterpret_cast<uintptr_t>(a.key_cache) & 15) ||
-      (reinterpret_cast<uintptr_t>(a.value_cache) & 15) || (a.stride_block & 7) ||
-      (a.stride_offset & 7) || (a.stride_head & 7))
+      (reinterpret_cast<uintptr_t>(a.value_cache) & 15) || (a.stride_block & (kv8 ? 15 : 7)) ||
+      (a.stride_offset & (kv8 ? 15 : 7)) || (a.stride_head & (kv8 ? 15 : 7)))
     return fail(DORY_ERR_ALIGNMENT,
                 "key/value caches need 16-byte aligned bases and strides (multiples of 8)");
   ScratchLayout SL;
@@ -2660,6 +2832,8 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
   kp.sh = a.stride_head;
   kp.ncache_blocks = a.num_cache_blocks;
   kp.scale = a.softmax_scale;
+  kp.k_scale = kv8 ? a.k_scale : 1.0f;
+  kp.v_scale = kv8 ? a.v_scale : 1.0f;
   kp.sqk_factor = a.sqk_factor;
   kp.eps = a.eps;
   kp.T = a.num_tokens;
@@ -2707,19 +2881,20 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
   {
     const int64_t nb = a.num_cache_blocks > 0 ? a.num_cache_blocks : 0;
     const int64_t extent = multi ? (nb * 64 < 0x7fffffff ? nb * 64 : 0x7fffffff) : nb;
-    const int q = HD / 64;
+    const int esize = kv8 ? 1 : 2;
+    const int q = kv8 ? HD / 128 : HD / 64;  // 128-byte pieces of a row's K (or V)
     kp.tm_mode = 0;
     kp.tm_blocks = extent;
     if (nb > 0) {
       const bool adjacent = static_cast<const char*>(a.value_cache) ==
-                            static_cast<const char*>(a.key_cache) + HD * 2;
+                            static_cast<const char*>(a.key_cache) + HD * esize;
       MapKey both{a.key_cache, extent, a.stride_block, a.stride_offset, a.stride_head,
-                  a.block_size, a.num_kv_heads, 2 * q};
+                  a.block_size, a.num_kv_heads, 2 * q, esize};
       if (adjacent && cache_tensor_map(both, &kp.tmk)) {
         kp.tm_mode = 1;
       } else {
         MapKey kk{a.key_cache, extent, a.stride_block, a.stride_offset, a.stride_head,
-                  a.block_size, a.num_kv_heads, q};
+                  a.block_size, a.num_kv_heads, q, esize};
         MapKey vk = kk;
         vk.base = a.value_cache;
         if (cache_tensor_map(kk, &kp.tmk) && cache_tensor_map(vk, &kp.tmv)) kp.tm_mode = 2;
@@ -2729,6 +2904,11 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
 
   cudaStream_t s = (cudaStream_t)stream;
   dim3 grid(a.splits, a.num_kv_heads, a.num_tokens);
+  if (kv8) {
+    if (kp.tm_mode == 0)
+      return fail(DORY_ERR_UNSUPPORTED, "FP8 caches need a tensor map of the cache view");
+    return HD == 128 ? dispatch_kv8<128>(kp, grid, s) : dispatch_kv8<256>(kp, grid, s);
+  }
   if (HD == 64) return dispatch_nt<64>(kp, nt, grid, s);
   if (HD == 128) return fma ? dispatch_fma(kp, grid, s) : dispatch_nt<128>(kp, nt, grid, s);
   return dispatch_nt<256>(kp, nt, grid, s);

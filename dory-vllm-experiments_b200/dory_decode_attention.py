@@ -35,6 +35,12 @@ _SQK_DTYPES = {torch.float32: _native.DTYPE_F32, torch.bfloat16: _native.DTYPE_B
                torch.float16: _native.DTYPE_F16}
 
 
+# kv_cache_dtype names (vLLM's) -> DoryDecodeParams.kv_dtype
+_KV_DTYPES = {"auto": _native.DTYPE_BF16, "bf16": _native.DTYPE_BF16,
+              "fp8": _native.DTYPE_FP8_E4M3, "fp8_e4m3": _native.DTYPE_FP8_E4M3}
+_FP8_CACHE_DTYPES = (torch.float8_e4m3fn, torch.uint8)
+
+
 def _ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
 
@@ -61,13 +67,21 @@ class DecodeAttention:
     turns it off.  consumer (B200 addition): "mma" (default) computes the score and P.V dot
     products with mma.sync tensor-core tiles, "fma" with FP32 FMAs on the CUDA cores, the
     measured alternative (128-dim heads, at most 4 query heads per KV head, no shared cache).
+    kv_cache_dtype (B200 addition, vLLM's name): "auto" / "bf16" for bf16 caches (the
+    reference's), "fp8" / "fp8_e4m3" for caches of e4m3 bytes (torch.float8_e4m3fn or uint8
+    views of the same shape), K = e4m3 * k_scale and V = e4m3 * v_scale, the scales passed
+    to each call (vLLM's per-layer k_scale / v_scale, default 1.0); a raw call appends
+    e4m3(bf16(k) / k_scale) and e4m3(bf16(v) / v_scale) (round to nearest even, saturated at
+    +-448) and attends those values.  128/256-dim heads, at most 8 query heads per KV head,
+    no shared cache.
     """
 
     def __init__(self, num_heads: int, num_kv_heads: int, head_dim: int, device: torch.device,
                  splits: int = 32, blocks_per_tile: int = 1, num_warps: int = 4,
                  num_stages: int = 2, dim_chunk: int = 64, max_tokens: int = 1,
                  min_blocks_per_split: int = 1, overlap_launch: bool = False,
-                 prefetch_chunks: int = 0, consumer: str = "mma"):
+                 prefetch_chunks: int = 0, consumer: str = "mma",
+                 kv_cache_dtype: str = "auto"):
         if num_heads % num_kv_heads:
             raise ValueError("query heads must be a multiple of KV heads")
         self.num_heads, self.num_kv_heads, self.head_dim = num_heads, num_kv_heads, head_dim
@@ -81,6 +95,10 @@ class DecodeAttention:
         if consumer not in ("mma", "fma"):
             raise ValueError("consumer must be 'mma' or 'fma'")
         self.consumer = consumer
+        if kv_cache_dtype not in _KV_DTYPES:
+            raise ValueError(f"kv_cache_dtype must be one of {sorted(_KV_DTYPES)}")
+        self.kv_cache_dtype = kv_cache_dtype
+        self._kv8 = _KV_DTYPES[kv_cache_dtype] == _native.DTYPE_FP8_E4M3
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise RuntimeError("DecodeAttention runs on CUDA devices only (no CPU path)")
@@ -110,32 +128,37 @@ class DecodeAttention:
         p.prefetch_chunks = self.prefetch_chunks
         self._base_flags = ((_native.FLAG_OVERLAP_LAUNCH if self.overlap_launch else 0) |
                             (_native.FLAG_FMA_CONSUMER if consumer == "fma" else 0))
+        p.kv_dtype = _KV_DTYPES[kv_cache_dtype]
+        p.k_scale = p.v_scale = 1.0
 
     # ---- the reference's three entry points ----
 
     def __call__(self, q: torch.Tensor, key_cache: torch.Tensor, value_cache: torch.Tensor,
                  block_table: torch.Tensor, seq_lens: torch.Tensor, window: int,
                  softmax_scale: float, gate: torch.Tensor, out_nibble_major: torch.Tensor,
-                 out_sumsq: torch.Tensor | None = None) -> None:
+                 out_sumsq: torch.Tensor | None = None, *, k_scale: float = 1.0,
+                 v_scale: float = 1.0) -> None:
         """q: BF16 [heads * head_dim], already in the cache's k and v; block_table:
         [max_blocks] of this sequence; seq_lens: [1] tokens including this one;
         window: 0 for full attention; gate: FP32 [heads * head_dim];
         out_nibble_major: FP32 [8, heads * head_dim / 8]."""
         self._launch(q, key_cache, value_cache, block_table, seq_lens, window, softmax_scale,
                      gate, out_nibble_major, raw=None, tokens=1, cache_offsets=None,
-                     out_sumsq=out_sumsq)
+                     out_sumsq=out_sumsq, k_scale=k_scale, v_scale=v_scale)
 
     def from_raw(self, qk: torch.Tensor, v: torch.Tensor, sqk: torch.Tensor, sqk_factor: float,
                  eps: float, slot_mapping: torch.Tensor, key_cache: torch.Tensor,
                  value_cache: torch.Tensor, block_table: torch.Tensor, seq_lens: torch.Tensor,
                  window: int, softmax_scale: float, gate: torch.Tensor,
-                 out_nibble_major: torch.Tensor, out_sumsq: torch.Tensor | None = None) -> None:
+                 out_nibble_major: torch.Tensor, out_sumsq: torch.Tensor | None = None, *,
+                 k_scale: float = 1.0, v_scale: float = 1.0) -> None:
         """Like __call__, from the rotated, unnormalized q and k heads (FP32
         [(heads + kv_heads) * head_dim]) and v (FP32 [kv_heads * head_dim]); also
         writes this token's k and v into the cache at slot_mapping[0]."""
         self._launch(qk, key_cache, value_cache, block_table, seq_lens, window, softmax_scale,
                      gate, out_nibble_major, raw=(v, sqk, sqk_factor, eps, slot_mapping),
-                     tokens=1, cache_offsets=None, out_sumsq=out_sumsq)
+                     tokens=1, cache_offsets=None, out_sumsq=out_sumsq, k_scale=k_scale,
+                     v_scale=v_scale)
 
     def multi_from_raw(self, qk: torch.Tensor, v: torch.Tensor, sqk: torch.Tensor,
                        sqk_factor: float, eps: float, cache_offsets: torch.Tensor,
@@ -144,7 +167,8 @@ class DecodeAttention:
                        seq_lens: torch.Tensor, window: int, softmax_scale: float,
                        gate: torch.Tensor, out_nibble_major: torch.Tensor,
                        shared_cache: bool = False, out_sumsq: torch.Tensor | None = None,
-                       slot_mapping: torch.Tensor | None = None) -> None:
+                       slot_mapping: torch.Tensor | None = None, *, k_scale: float = 1.0,
+                       v_scale: float = 1.0) -> None:
         """from_raw for T tokens: qk [T, (heads + kv_heads) * head_dim], v [T, kv_heads *
         head_dim], gate [T, heads * head_dim], out_nibble_major [T, 8, heads * head_dim / 8],
         seq_lens [T].  Token t is at position seq_lens[t] - 1 and uses the cache at
@@ -179,7 +203,7 @@ class DecodeAttention:
                      gate, out_nibble_major, raw=(v, sqk, sqk_factor, eps, slot_mapping),
                      tokens=tokens, cache_offsets=cache_offsets,
                      block_table_offsets=block_table_offsets, shared=shared_cache,
-                     out_sumsq=out_sumsq)
+                     out_sumsq=out_sumsq, k_scale=k_scale, v_scale=v_scale)
 
     # ---- diagnostics ----
 
@@ -203,11 +227,14 @@ class DecodeAttention:
 
     def _launch(self, q, key_cache, value_cache, block_table, seq_lens, window, softmax_scale,
                 gate, out_nibble_major, raw, tokens, cache_offsets,
-                block_table_offsets=None, shared=False, out_sumsq=None) -> None:
+                block_table_offsets=None, shared=False, out_sumsq=None, k_scale=1.0,
+                v_scale=1.0) -> None:
         if key_cache.stride() != value_cache.stride() or key_cache.stride(-1) != 1:
             raise ValueError("key and value caches need equal strides and unit last stride")
-        if key_cache.dtype != torch.bfloat16 or value_cache.dtype != torch.bfloat16:
-            raise ValueError("key and value caches must be bfloat16")
+        want = _FP8_CACHE_DTYPES if self._kv8 else (torch.bfloat16,)
+        if key_cache.dtype not in want or value_cache.dtype not in want:
+            raise ValueError("key and value caches must be bfloat16" if not self._kv8 else
+                             "fp8 key and value caches must be float8_e4m3fn or uint8")
         if not key_cache.is_cuda:
             raise RuntimeError("DecodeAttention runs on CUDA tensors only (no CPU path)")
         dev = self._dev_index
@@ -268,6 +295,8 @@ class DecodeAttention:
         shape = key_cache.shape
         p.num_cache_blocks, p.block_size = shape[0], shape[1]
         p.softmax_scale = float(softmax_scale)
+        if self._kv8:
+            p.k_scale, p.v_scale = float(k_scale), float(v_scale)
         p.num_tokens, p.window, p.flags = tokens, int(window), flags
         # the current stream's handle (torch.cuda.current_stream(dev).cuda_stream, without
         # building the Stream object)

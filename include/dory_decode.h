@@ -29,7 +29,7 @@
 extern "C" {
 #endif
 
-#define DORY_DECODE_ABI_VERSION 7
+#define DORY_DECODE_ABI_VERSION 8
 
 /* Status codes returned by every entry point. */
 typedef enum DoryStatus {
@@ -41,7 +41,12 @@ typedef enum DoryStatus {
 } DoryStatus;
 
 /* Element type of the per-dimension query scale `sqk` (the checkpoint's dtype). */
-typedef enum DoryDType { DORY_DTYPE_F32 = 0, DORY_DTYPE_BF16 = 1, DORY_DTYPE_F16 = 2 } DoryDType;
+typedef enum DoryDType {
+  DORY_DTYPE_F32 = 0,
+  DORY_DTYPE_BF16 = 1,
+  DORY_DTYPE_F16 = 2,
+  DORY_DTYPE_FP8_E4M3 = 3 /* DoryDecodeParams.kv_dtype only */
+} DoryDType;
 
 /* Call kinds (bit flags of DoryDecodeParams.flags). */
 enum {
@@ -136,6 +141,18 @@ typedef struct DoryDecodeParams {
                                    * shared-memory ring of each CTA: 0 = automatic (the whole
                                    * range for an OVERLAP_LAUNCH call whose grid runs in one
                                    * wave, else none), < 0 = none, > 0 = that many chunks    */
+  int32_t kv_dtype;               /* cache element type: 0 or DORY_DTYPE_BF16 (bf16), or
+                                   * DORY_DTYPE_FP8_E4M3: key_cache / value_cache hold e4m3
+                                   * bytes (strides in bytes, multiples of 16), K = e4m3 *
+                                   * k_scale and V = e4m3 * v_scale, and a raw call appends
+                                   * e4m3(bf16(k) / k_scale) and e4m3(bf16(v) / v_scale),
+                                   * rounded to nearest even and saturated at +-448, the
+                                   * values it attends.  128/256-dim heads, at most 8 query
+                                   * heads per KV head, no SHARED_CACHE, num_cache_blocks > 0.
+                                   * No counterpart in the reference (its caches are bf16;
+                                   * vLLM's "fp8" kv_cache_dtype).                           */
+  float k_scale;                  /* FP8 caches: positive, finite                           */
+  float v_scale;
 } DoryDecodeParams;
 
 /* ABI version of the loaded library (DORY_DECODE_ABI_VERSION). */

@@ -27,7 +27,10 @@ chrisbennight/dory-vllm-experiments:
 * multi-token calls (:270-305): token t uses cache_offsets[t] and block_table_offsets[t];
   shared_cache=True caches every token's k/v before any attention (:294-301), which the
   reference's own test checks against single-token calls in position order
-  (kernels/bench_multi_token.py:160-197).
+  (kernels/bench_multi_token.py:160-197);
+* FP8 (e4m3) caches, which the reference does not have (its docs/FUTURE_WORK.md lists them):
+  the format of vLLM's fp8 kv_cache_dtype, restated in e4m3_quantize / e4m3_dequantize and
+  the *_fp8 calls ("parity unpinned" for these: no reference output exists).
 
 Normalisation arithmetic (bit-exact cache contract).  Sum x^2 is accumulated in FP64 and
 rounded once to FP32, eps is added in FP32, and the inverse square root is the correctly
@@ -356,6 +359,60 @@ def residual_tokens(partials, x, x_sumsq, a, alpha, alpha_scale: float, eps: flo
     h = normalize(z, eps)
     h_t = torch.from_numpy(h.copy())
     return h_t, h_t.to(torch.bfloat16), h_t.reshape(T, H // 8, 8).transpose(1, 2).contiguous()
+
+
+# ---------------------------------------------------------------------------------------
+# FP8 (e4m3) KV cache (no counterpart in the reference, whose caches are bf16; the format
+# of vLLM's "fp8" kv_cache_dtype: e4m3 bytes with per-layer scales).  Stored value
+# e4m3(x / scale), round to nearest even, saturating at +-448; read back as e4m3 * scale.
+# The appended k and v are the reference's bf16 rows (raw_qkv) quantised this way, and the
+# attention reads every cache row, the new one included, dequantised.
+# ---------------------------------------------------------------------------------------
+
+E4M3_MAX = 448.0
+
+
+def e4m3_quantize(x: torch.Tensor, scale: float) -> torch.Tensor:
+    """FP32 (or bf16) values -> e4m3 bytes (uint8) of x / scale (FP32 division), rounded to
+    nearest even with saturation at +-448."""
+    return (x.float() / scale).clamp(-E4M3_MAX, E4M3_MAX).to(torch.float8_e4m3fn).view(
+        torch.uint8)
+
+
+def e4m3_dequantize(b: torch.Tensor, scale: float) -> torch.Tensor:
+    """e4m3 bytes (uint8) -> FP32 values times scale."""
+    return b.view(torch.float8_e4m3fn).float() * scale
+
+
+def call_fp8(q, key8, value8, block_table, seq_len: int, window: int, softmax_scale: float,
+             gate, num_heads: int, k_scale: float, v_scale: float) -> torch.Tensor:
+    """DecodeAttention.__call__ over e4m3 caches [blocks, B, NKV, HD] (uint8)."""
+    return call(q, e4m3_dequantize(key8, k_scale), e4m3_dequantize(value8, v_scale),
+                block_table, seq_len, window, softmax_scale, gate, num_heads)
+
+
+def from_raw_fp8(qk, v, sqk, sqk_factor, eps, slot: int, key8, value8, block_table,
+                 seq_len: int, window: int, softmax_scale: float, gate, num_heads: int,
+                 num_kv_heads: int, k_scale: float, v_scale: float) -> torch.Tensor:
+    """DecodeAttention.from_raw over e4m3 caches: the new bf16 k / v quantised with their
+    scales, attended as such at position seq_len - 1 and appended at `slot` (if >= 0)."""
+    HD = key8.shape[-1]
+    B = key8.shape[1]
+    q, k_new, v_new = raw_qkv(qk, v, sqk, sqk_factor, eps, num_heads, num_kv_heads, HD)
+    k8, v8 = e4m3_quantize(k_new, k_scale), e4m3_quantize(v_new, v_scale)
+    if seq_len <= 0:
+        return nibble_major(torch.zeros(num_heads * HD) * gate.float().cpu())
+    pos = seq_len - 1
+    phys = int(block_table[pos // B])
+    key = e4m3_dequantize(key8, k_scale)
+    value = e4m3_dequantize(value8, v_scale)
+    key[phys, pos % B] = e4m3_dequantize(k8, k_scale)
+    value[phys, pos % B] = e4m3_dequantize(v8, v_scale)
+    out = attention(q, key, value, block_table, seq_len, window, num_heads, B, softmax_scale)
+    if slot >= 0:
+        key8[slot // B, slot % B] = k8
+        value8[slot // B, slot % B] = v8
+    return nibble_major(out * gate.float().cpu())
 
 
 def relative_error(x: torch.Tensor, reference: torch.Tensor) -> float:

@@ -237,12 +237,23 @@ def partition(lens: list[int], parts: int) -> list[list[int]]:
     return [sorted(part) for part in out]
 
 
-def to_device(case: Case, layout: str, device, copy_cache: bool = True):
+def e4m3_bytes(x: torch.Tensor, scale: float) -> torch.Tensor:
+    """Synthetic FP8 cache contents: e4m3 bytes (uint8) of x / scale, round to nearest even,
+    saturating at +-448."""
+    return (x.float() / scale).clamp(-448.0, 448.0).to(torch.float8_e4m3fn).view(torch.uint8)
+
+
+def to_device(case: Case, layout: str, device, copy_cache: bool = True, kv8=None):
     """Device tensors of a case: dict with raw/key/value caches (in `layout`), flat tables,
-    offsets, seq_lens, qk, v, gate, sqk, outputs."""
+    offsets, seq_lens, qk, v, gate, sqk, outputs.  kv8 = (k_scale, v_scale): e4m3 caches
+    (uint8 storage) holding the case's K / V quantised with those scales."""
     raw, key, value = cache_views(case.num_blocks, case.block_size, case.num_kv_heads,
-                                  case.head_dim, layout, device)
-    if copy_cache:
+                                  case.head_dim, layout, device,
+                                  torch.uint8 if kv8 else torch.bfloat16)
+    if copy_cache and kv8:
+        key.copy_(e4m3_bytes(case.key, kv8[0]))
+        value.copy_(e4m3_bytes(case.value, kv8[1]))
+    elif copy_cache:
         key.copy_(case.key.to(torch.bfloat16))
         value.copy_(case.value.to(torch.bfloat16))
     width = case.tables.shape[1]
