@@ -2351,7 +2351,7 @@ bool one_wave(F fn, dim3 grid, int smem) {
       return fits(cache[i].per_sm);
   int per_sm = 0;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           Smem<256, 8>::bytes(kMaxSub)) != cudaSuccess ||
+                           227 * 1024) != cudaSuccess ||
       cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, smem) != cudaSuccess)
     per_sm = 0;
   cudaGetLastError();
@@ -2404,10 +2404,17 @@ int32_t dispatch_fma(const KParams& kp, dim3 grid, cudaStream_t stream) {
             : launch<128, 1, NS, false, false, true>(kp, grid, smem, stream);
 }
 
-// FP8 (e4m3) caches: one 8-row tile, the FP8 ring and per-warp f16 tiles.
+// FP8 (e4m3) caches: one 8-row tile, the FP8 ring and per-warp f16 tiles.  A 16-row FP8
+// chunk carries half a bf16 chunk's bytes, so the ring has more stages for the same bytes
+// in flight.
+#ifndef DORY_KV8_STAGES
+#define DORY_KV8_STAGES 8
+#endif
+constexpr int kStagesKV8 = DORY_KV8_STAGES;
 template <int HD>
 int32_t dispatch_kv8(const KParams& kp, dim3 grid, cudaStream_t stream) {
-  constexpr int NS = Depth<HD, 1>::value;
+  constexpr int NS = kStagesKV8;
+  static_assert(NS % kConsumerWarps == 0, "ring stages must be a multiple of the consumer warps");
   static_assert(kConsumerWarps * 8 * (HD + 4) * 4 <= Smem<HD, NS, true>::kRegion,
                 "the warps' merge buffer must fit in the ring and staging tiles");
   const int smem = Smem<HD, NS, true>::bytes(kp.nsub);
