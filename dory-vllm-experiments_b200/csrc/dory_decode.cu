@@ -2329,7 +2329,7 @@ int sm_count();
 // once every CTA of the previous one has started, so its CTAs never hold slots that one
 // still needs).
 template <typename F>
-bool one_wave(F fn, dim3 grid, int smem) {
+bool one_wave(F fn, dim3 grid, int smem, int max_smem) {
   struct Entry {
     const void* fn;
     int dev, smem, per_sm;
@@ -2351,7 +2351,7 @@ bool one_wave(F fn, dim3 grid, int smem) {
       return fits(cache[i].per_sm);
   int per_sm = 0;
   if (cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           227 * 1024) != cudaSuccess ||
+                           max_smem) != cudaSuccess ||
       cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, fn, kThreads, smem) != cudaSuccess)
     per_sm = 0;
   cudaGetLastError();
@@ -2381,7 +2381,8 @@ int32_t dispatch(const KParams& kp, dim3 grid, cudaStream_t stream) {
   // The designated merger waits for the other splits of its (group, KV head) to finish:
   // only when every CTA of the grid is resident at once, so that none of them can be
   // waiting for a slot the merger holds.
-  const bool dm = one_wave(decode_kernel<HD, NT, NS, false, true>, grid, smem);
+  const bool dm = one_wave(decode_kernel<HD, NT, NS, false, true>, grid, smem,
+                           Smem<256, 8>::bytes(kMaxSub));
   // The sum-of-squares epilogue is a separate instantiation: compiled in, even unused, it
   // measured ~0.5 us slower on single-sequence calls.
   if (kp.sumsq)
@@ -2396,7 +2397,8 @@ int32_t dispatch(const KParams& kp, dim3 grid, cudaStream_t stream) {
 int32_t dispatch_fma(const KParams& kp, dim3 grid, cudaStream_t stream) {
   constexpr int NS = Depth<128, 1>::value;
   const int smem = Smem<128, NS>::bytes(kp.nsub);
-  const bool dm = one_wave(decode_kernel<128, 1, NS, false, true, true>, grid, smem);
+  const bool dm = one_wave(decode_kernel<128, 1, NS, false, true, true>, grid, smem,
+                           Smem<256, 8>::bytes(kMaxSub));
   if (kp.sumsq)
     return dm ? launch<128, 1, NS, true, true, true>(kp, grid, smem, stream)
               : launch<128, 1, NS, true, false, true>(kp, grid, smem, stream);
@@ -2418,7 +2420,8 @@ int32_t dispatch_kv8(const KParams& kp, dim3 grid, cudaStream_t stream) {
   static_assert(kConsumerWarps * 8 * (HD + 4) * 4 <= Smem<HD, NS, true>::kRegion,
                 "the warps' merge buffer must fit in the ring and staging tiles");
   const int smem = Smem<HD, NS, true>::bytes(kp.nsub);
-  const bool dm = one_wave(decode_kernel<HD, 1, NS, false, true, false, true>, grid, smem);
+  const bool dm = one_wave(decode_kernel<HD, 1, NS, false, true, false, true>, grid, smem,
+                           Smem<HD, NS, true>::bytes(kMaxSub));
   if (kp.sumsq)
     return dm ? launch<HD, 1, NS, true, true, false, true>(kp, grid, smem, stream)
               : launch<HD, 1, NS, true, false, false, true>(kp, grid, smem, stream);
