@@ -584,7 +584,8 @@ def bench_profile(args):
     torch.cuda.set_device(dev)
     spec = workload_spec(args.workload)
     lens_all = subset(spec.lens, args.max_seqs)
-    wl = DeviceWorkload(spec, lens_all, dev, 11, mem_fraction=args.mem_fraction)
+    wl = DeviceWorkload(spec, lens_all, dev, 11, mem_fraction=args.mem_fraction,
+                        kv_dtype=args.kv_dtype)
     attn = make_attention(wl, args)
     for _ in range(args.profile_steps):
         run_step(attn, wl)
