@@ -68,10 +68,13 @@ class VllmDecodeBinding:
     def decode(self, metadata, kv_cache: torch.Tensor, qk: torch.Tensor, v: torch.Tensor,
                sqk: torch.Tensor, sqk_factor: float, eps: float, window: int,
                softmax_scale: float, gate: torch.Tensor, out_nibble_major: torch.Tensor,
-               out_sumsq: torch.Tensor | None = None) -> None:
+               out_sumsq: torch.Tensor | None = None, k_scale: float = 1.0,
+               v_scale: float = 1.0) -> None:
         """qk FP32 [T, (heads + kv_heads) * head_dim] (rotated, not normalised), v FP32
         [T, kv_heads * head_dim], gate FP32 [T, heads * head_dim], out_nibble_major FP32
-        [T, 8, heads * head_dim / 8], for the T = qk.shape[0] requests of the batch."""
+        [T, 8, heads * head_dim / 8], for the T = qk.shape[0] requests of the batch.  With
+        an attention instance built for kv_cache_dtype="fp8", kv_cache is vLLM's fp8 cache
+        (uint8 e4m3 bytes, the same shape) and k_scale / v_scale the layer's float scales."""
         if int(metadata.max_query_len) != 1:
             raise NotImplementedError("only decode batches (one query token per request); "
                                       "prefill stays on vLLM's attention")
@@ -89,4 +92,4 @@ class VllmDecodeBinding:
         a.multi_from_raw(qk, v, sqk, sqk_factor, eps, self._cache_offsets[:tokens], key, value,
                          table, self._rows(table.stride(0))[:tokens], seq_lens[:tokens], window,
                          softmax_scale, gate, out_nibble_major, out_sumsq=out_sumsq,
-                         slot_mapping=slots[:tokens])
+                         slot_mapping=slots[:tokens], k_scale=k_scale, v_scale=v_scale)

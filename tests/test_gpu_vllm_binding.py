@@ -186,3 +186,37 @@ def test_slot_mapping_decides_where_rows_go():
         assert torch.equal(key_a[s // B, s % B].view(torch.int16), rows[t][0].view(torch.int16))
         assert torch.equal(val_a[s // B, s % B].view(torch.int16), rows[t][1].view(torch.int16))
     assert not (changed & ~expect).any()  # request 1's table slot and the padded row: untouched
+
+
+def test_fp8_cache_in_vllm_shape():
+    """vLLM's fp8 kv_cache_dtype: the cache tensor is uint8 e4m3 bytes in the backend's shape;
+    outputs against the oracle's e4m3 restatement, the slots vLLM's slot_mapping gives hold the
+    quantised rows, nothing else changes."""
+    import dory_oracle as O
+    triton_attn = triton_backend()
+    case = W.batched(seed=1300, lens=[40, 700, 15, 333])
+    NH, NKV, HD, B = case.num_heads, case.num_kv_heads, case.head_dim, case.block_size
+    ks, vs = 0.5, 0.25
+    shape = triton_attn.TritonAttentionBackend.get_kv_cache_shape(case.num_blocks, B, NKV, HD)
+    kv = torch.empty(shape, dtype=torch.uint8, device=DEV)
+    key, value = kv_cache_views(kv, NKV, HD)
+    key.copy_(W.e4m3_bytes(case.key, ks))
+    value.copy_(W.e4m3_bytes(case.value, vs))
+    _, meta, slots = vllm_batch(case, "vllm", 0)
+    attn = DecodeAttention(NH, NKV, HD, DEV, splits=8, max_tokens=case.tokens,
+                           kv_cache_dtype="fp8")
+    binding = VllmDecodeBinding(attn)
+    out = torch.full((case.tokens, 8, NH * HD // 8), float("nan"), device=DEV)
+    binding.decode(meta, kv, case.qk.to(DEV), case.v.to(DEV), case.sqk.to(DEV),
+                   case.sqk_factor, EPS, 0, case.scale, case.gate.to(DEV), out, k_scale=ks,
+                   v_scale=vs)
+    torch.cuda.synchronize()
+    attn.check_errors()
+    key8, value8 = W.e4m3_bytes(case.key, ks), W.e4m3_bytes(case.value, vs)
+    want = torch.stack([O.from_raw_fp8(case.qk[t], case.v[t], case.sqk, case.sqk_factor, EPS,
+                                       slots[t], key8, value8, case.tables[case.table_rows[t]],
+                                       case.seq_lens[t], 0, case.scale, case.gate[t], NH, NKV,
+                                       ks, vs) for t in range(case.tokens)])
+    assert_close(out.cpu(), want)
+    k_dev, v_dev = kv_cache_views(kv, NKV, HD)
+    assert torch.equal(k_dev.cpu(), key8) and torch.equal(v_dev.cpu(), value8)
