@@ -168,11 +168,8 @@ struct Smem {
   static constexpr int kTileBytes = KV8 ? (HD / 128) * kBoxBytes : kTile16;  // as copied
   static constexpr int kStageBytes = 2 * kTileBytes;
   static constexpr int kStages = 0;                           // 1024-byte aligned at run time
-  // FP8: each consumer warp's K and V tiles dequantized to f16 (the 16-bit tile layout)
-  static constexpr int kStaging = kStages + NS * kStageBytes;
-  static constexpr int kStagingBytes = KV8 ? kConsumerWarps * 2 * kTile16 : 0;
-  static constexpr int kRegion = NS * kStageBytes + kStagingBytes;  // reused after the loop
-  static constexpr int kBars = kStaging + kStagingBytes;      // full[NS], empty[NS]
+  static constexpr int kRegion = NS * kStageBytes;            // reused after the loop
+  static constexpr int kBars = kStages + NS * kStageBytes;    // full[NS], empty[NS]
   static constexpr int kMeta = kBars + 2 * NS * 8;            // int4 {phys, -, chunk, -}
   static constexpr int kQ = kMeta + NS * 16;                  // bf16 [16][HD]
   static constexpr int kSub = kQ + 16 * HD * 2;               // bf16 [nsub][2][HD]
@@ -366,35 +363,6 @@ __device__ __forceinline__ void mma16(float (&d)[4], uint32_t a0, uint32_t a1, u
   if constexpr (F16) mma_f16(d, a0, a1, a2, a3, b0, b1);
   else mma_bf16(d, a0, a1, a2, a3, b0, b1);
 }
-// FP8 stage -> this warp's f16 tiles: K and V of a 16-row chunk (K first) into the 16-bit
-// tile layout (tile_off), rows outside [lo, hi) or of a bad block (phys < 0) as zeros.
-template <int HD>
-__device__ __forceinline__ void dequant_stage(const uint8_t* st8, uint8_t* k16, int c, int phys,
-                                              int lo, int hi, int lane) {
-  constexpr int TILE8 = (HD / 128) * kBoxBytes, TILE16 = (HD / 64) * kBoxBytes;
-  constexpr int PIECES = kChunk * (HD / 16);  // 16-byte pieces of 16 e4m3 per tile
-#pragma unroll
-  for (int k = 0; k < 2 * PIECES / 32; ++k) {
-    const int idx = k * 32 + lane;
-    const bool is_v = idx >= PIECES;
-    const int j = is_v ? idx - PIECES : idx;
-    const int r = j / (HD / 16), d = (j % (HD / 16)) * 16;
-    const int pos = c * kChunk + r;
-    const bool ok = phys >= 0 && pos >= lo && pos < hi;
-    uint4 lo8 = make_uint4(0u, 0u, 0u, 0u), hi8 = make_uint4(0u, 0u, 0u, 0u);
-    if (ok) {
-      const uint4 w = *reinterpret_cast<const uint4*>(st8 + (is_v ? TILE8 : 0) + tile_off8(r, d));
-      lo8 = make_uint4(e4m3x2_to_f16x2(w.x & 0xffffu), e4m3x2_to_f16x2(w.x >> 16),
-                       e4m3x2_to_f16x2(w.y & 0xffffu), e4m3x2_to_f16x2(w.y >> 16));
-      hi8 = make_uint4(e4m3x2_to_f16x2(w.z & 0xffffu), e4m3x2_to_f16x2(w.z >> 16),
-                       e4m3x2_to_f16x2(w.w & 0xffffu), e4m3x2_to_f16x2(w.w >> 16));
-    }
-    uint8_t* dst = k16 + (is_v ? TILE16 : 0);
-    *reinterpret_cast<uint4*>(dst + tile_off(r, d)) = lo8;
-    *reinterpret_cast<uint4*>(dst + tile_off(r, d + 8)) = hi8;
-  }
-}
-
 // O^T += V^T P^T over one 16-row stage (256-dim heads): [16 dims x 8 rows] per m-tile (k-step
 // kk) and n-tile.  Lane l gives ldmatrix the address of V row (l & 7) + 8 * (l >> 4) of its
 // matrix; MASK: a lane whose row is outside the attended range (row_ok false) gives the
@@ -1541,9 +1509,18 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
     for (int kk = 0; kk < KT; ++kk) {
+      if constexpr (KV8) {
+        // FP8: k-step kk's slot pairs (2t4, 2t4+1), (2t4+8, 2t4+9) are the dims
+        // HD/4 * t4 + 4kk + {0, 1}, {2, 3}, the order the K operands are read in
+        const uint32_t* row = reinterpret_cast<const uint32_t*>(q2 + (nt * 8 + g) * HD);
+        const int pair = ((HD / 4) * t4 + 4 * kk) / 2;
+        qb[nt][kk][0] = bf16x2_to_f16x2(row[pair]);
+        qb[nt][kk][1] = bf16x2_to_f16x2(row[pair + 1]);
+      } else {
       const uint32_t* row = reinterpret_cast<const uint32_t*>(q2 + (nt * 8 + g) * HD + kk * 16);
-      qb[nt][kk][0] = KV8 ? bf16x2_to_f16x2(row[t4]) : row[t4];
-      qb[nt][kk][1] = KV8 ? bf16x2_to_f16x2(row[t4 + 4]) : row[t4 + 4];
+      qb[nt][kk][0] = row[t4];
+      qb[nt][kk][1] = row[t4 + 4];
+      }
     }
   // Row bounds of the two query rows this lane accumulates per n-tile.
   int rfirst[NT][2], rlen[NT][2];
@@ -1573,7 +1550,6 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
   // to each warp's accumulator); the chunks run only with tensor-map copies.
   const float kscore = KV8 ? kLog2e * p.k_scale : kLog2e;
   const int nloop = (KV8 && !use_tma) ? 0 : nchunks;
-  uint8_t* k16 = smem + L::kStaging + warp * 2 * L::kTile16;  // KV8: this warp's f16 tiles
 
   bool failed = false;
   // CUDA-core consumer state (FMA instantiations only): the query rows as FP32 (the same
@@ -1649,14 +1625,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     bool touched = false;
     const bool partial = !KV8 && use_tma && (c < c_full_lo || c >= c_full_hi || phys < 0);
     if constexpr (KV8) {
-      // FP8: the stage to this warp's f16 tiles (rows outside the range as zeros), and the
-      // stage goes straight back to the ring.
-      dequant_stage<HD>(kst, k16, c, phys, s_ci.lo, s_ci.hi, lane);
-      kst = k16;
-      vst = k16 + L::kTile16;
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0 && i + NS < nchunks) issue_chunk(i + NS);
+      // FP8: no slow path; the operands come from the stage's bytes below
     } else {
     if ((partial && !kRowMask) || (c >= sub_lo && c <= sub_hi) || any_foreign)
       touched = fixup_stage<HD>(p, kst, vst, c, phys, partial && !kRowMask, lane, s_ci, s_len,
@@ -1671,7 +1640,35 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) sc[nt][e] = sc2[nt][e] = 0.0f;
-    {
+    if constexpr (KV8) {
+      // e4m3 K straight into the f16 MMA operands: lane (g, t4) reads rows g and g + 8 at dims
+      // [HD/4 * t4, HD/4 * (t4 + 1)); k-step kk takes its dims HD/4 * t4 + 4kk .. + 3 as the
+      // slot pairs (2t4, 2t4+1) and (2t4+8, 2t4+9) (a dot product allows any order; the
+      // query fragments follow it).
+      constexpr int PK = HD / 64;  // 16-byte pieces per lane and row
+      uint32_t kw[2][4 * PK];
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int pi = 0; pi < PK; ++pi) {
+          const uint4 w =
+              *reinterpret_cast<const uint4*>(kst + tile_off8(g + 8 * h, (HD / 4) * t4 + 16 * pi));
+          kw[h][4 * pi + 0] = w.x;
+          kw[h][4 * pi + 1] = w.y;
+          kw[h][4 * pi + 2] = w.z;
+          kw[h][4 * pi + 3] = w.w;
+        }
+#pragma unroll
+      for (int kk = 0; kk < KT; ++kk) {
+        const uint32_t a0 = e4m3x2_to_f16x2(kw[0][kk] & 0xffffu);
+        const uint32_t a2 = e4m3x2_to_f16x2(kw[0][kk] >> 16);
+        const uint32_t a1 = e4m3x2_to_f16x2(kw[1][kk] & 0xffffu);
+        const uint32_t a3 = e4m3x2_to_f16x2(kw[1][kk] >> 16);
+        mma_f16((kk & 1) ? sc2[0] : sc[0], a0, a1, a2, a3, qb[0][kk][0], qb[0][kk][1]);
+      }
+#pragma unroll
+      for (int e = 0; e < 4; ++e) sc[0][e] += sc2[0][e];
+    } else {
       const uint32_t kbase_s = smem_u32(kst);
       const int kr = lane & 15, kd = (lane >> 4) * 8;
 #pragma unroll
@@ -1697,8 +1694,9 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
       float alpha[2];
 #pragma unroll
       for (int i = 0; i < 2; ++i) {
-        const bool v0 = pos0 >= rfirst[nt][i] && pos0 < rlen[nt][i];
-        const bool v1 = pos1 >= rfirst[nt][i] && pos1 < rlen[nt][i];
+        const bool bad = KV8 && phys < 0;  // FP8: a bad block's stage was never loaded
+        const bool v0 = !bad && pos0 >= rfirst[nt][i] && pos0 < rlen[nt][i];
+        const bool v1 = !bad && pos1 >= rfirst[nt][i] && pos1 < rlen[nt][i];
         const float x0 = v0 ? sc[nt][i] * kscore : -INFINITY;
         const float x1 = v1 ? sc[nt][2 + i] * kscore : -INFINITY;
         float tmax = fmaxf(x0, x1);
@@ -1725,7 +1723,41 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
       pb[nt][1] = movmatrix_t(KV8 ? pack_p_f16x2(pv[2], pv[3]) : pack_bf16x2(pv[2], pv[3]));
     }
     // O^T += V^T P^T : [16 dims x 8 rows] per m-tile and n-tile.
-    if constexpr (kRowMask) {
+    if constexpr (KV8) {
+      // e4m3 V^T operands: lane (g, t4) reads token rows 2t4, 2t4+1, 2t4+8, 2t4+9 at dims
+      // [HD/8 * g, HD/8 * (g + 1)) (rows outside the attended range as zeros); m-tile mt takes
+      // dims HD/8 * g + 2mt (m row g) and + 1 (m row g + 8), and byte permutes pair the two
+      // tokens of each k slot.  The stage is then free for its next chunk.
+      constexpr int PV = HD / 128;  // 16-byte pieces per lane and row
+      uint32_t vw[4][4 * PV];
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        const int r = 2 * t4 + (q4 & 1) + 8 * (q4 >> 1);
+        const int pos = c * kChunk + r;
+        const bool ok = phys >= 0 && pos >= s_ci.lo && pos < s_ci.hi;
+#pragma unroll
+        for (int pi = 0; pi < PV; ++pi) {
+          uint4 w = *reinterpret_cast<const uint4*>(vst + tile_off8(r, (HD / 8) * g + 16 * pi));
+          if (!ok) w = make_uint4(0u, 0u, 0u, 0u);
+          vw[q4][4 * pi + 0] = w.x;
+          vw[q4][4 * pi + 1] = w.y;
+          vw[q4][4 * pi + 2] = w.z;
+          vw[q4][4 * pi + 3] = w.w;
+        }
+      }
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0 && i + NS < nchunks) issue_chunk(i + NS);
+#pragma unroll
+      for (int mt = 0; mt < KT; ++mt) {
+        const uint32_t sel = (mt & 1) ? 0x7362u : 0x5140u;
+        const uint32_t plo = __byte_perm(vw[0][mt >> 1], vw[1][mt >> 1], sel);
+        const uint32_t phi = __byte_perm(vw[2][mt >> 1], vw[3][mt >> 1], sel);
+        const uint32_t a0 = e4m3x2_to_f16x2(plo & 0xffffu), a1 = e4m3x2_to_f16x2(plo >> 16);
+        const uint32_t a2 = e4m3x2_to_f16x2(phi & 0xffffu), a3 = e4m3x2_to_f16x2(phi >> 16);
+        mma_f16(o[0][mt], a0, a1, a2, a3, pb[0][0], pb[0][1]);
+      }
+    } else if constexpr (kRowMask) {
       // Rows outside [lo, hi) of an edge stage (every row of a bad block, whose stage was
       // not loaded) may hold anything, NaN included; P is zero there, but 0 * NaN is not.
       if (partial) {
@@ -1823,8 +1855,13 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
       const float vsc = KV8 ? p.v_scale : 1.0f;
 #pragma unroll
       for (int kk = 0; kk < KT; ++kk) {
-        dst[kk * 16 + g] = KV8 ? o[nt][kk][i] * vsc : o[nt][kk][i];
-        dst[kk * 16 + g + 8] = KV8 ? o[nt][kk][2 + i] * vsc : o[nt][kk][2 + i];
+        if constexpr (KV8) {  // m-tile kk holds dims HD/8 * g + 2kk (+ 1)
+          dst[(HD / 8) * g + 2 * kk] = o[nt][kk][i] * vsc;
+          dst[(HD / 8) * g + 2 * kk + 1] = o[nt][kk][2 + i] * vsc;
+        } else {
+        dst[kk * 16 + g] = o[nt][kk][i];
+        dst[kk * 16 + g + 8] = o[nt][kk][2 + i];
+        }
       }
     }
   }
@@ -2410,7 +2447,7 @@ int32_t dispatch_fma(const KParams& kp, dim3 grid, cudaStream_t stream) {
 // chunk carries half a bf16 chunk's bytes, so the ring has more stages for the same bytes
 // in flight.
 #ifndef DORY_KV8_STAGES
-#define DORY_KV8_STAGES 8
+#define DORY_KV8_STAGES 16
 #endif
 constexpr int kStagesKV8 = DORY_KV8_STAGES;
 template <int HD>
