@@ -712,7 +712,9 @@ def bench_ours(args, world, rank, local):
     line = {
         "metric": METRIC, "value": round(seqs_per_s, 2), "unit": "seqs/s", "n_gpus": world,
         "steps": steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
-        "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "bf16",
+        "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
+        # an FP8 cache is read as e4m3 bytes and multiplied in f16 (fp32 accumulation)
+        "dtype": "bf16" if args.kv_dtype == "bf16" else "fp8_e4m3",
         "data": "synthetic (seeded N(0,1) K/V, q/k/v, gate; random block-table permutations)",
         "config": config,
         "us_per_layer_step": round(us_per_layer, 3),

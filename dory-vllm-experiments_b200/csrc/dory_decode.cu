@@ -862,8 +862,14 @@ __device__ __forceinline__ void sumsq_tail(const KParams& p, const float* sv, in
 // ------------------------------------------------------------------------------------
 // The kernel.  grid = (splits, NKV, T); block = 160 threads (4 consumer warps + producer).
 // ------------------------------------------------------------------------------------
+// CTAs per SM the 128-dim FP8 instantiations are compiled for (registers cap them at 3;
+// 4 forces 96 registers with spills: 1.5% faster on large batches, 5-10% slower on the
+// small and single-sequence steps).
+#ifndef DORY_KV8_MIN_CTAS
+#define DORY_KV8_MIN_CTAS 3
+#endif
 template <int HD, int NT, int NS, bool SS, bool DM, bool FMA = false, bool KV8 = false>
-__global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? 3 : 1)
+__global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? (KV8 ? DORY_KV8_MIN_CTAS : 3) : 1)
     decode_kernel(const __grid_constant__ KParams p) {
   static_assert(!FMA || (HD == 128 && NT == 1), "the CUDA-core consumer is 128-dim, one tile");
   static_assert(!KV8 || (NT == 1 && !FMA && HD >= 128), "FP8 caches: 128/256-dim, one tile");
@@ -2443,11 +2449,11 @@ int32_t dispatch_fma(const KParams& kp, dim3 grid, cudaStream_t stream) {
             : launch<128, 1, NS, false, false, true>(kp, grid, smem, stream);
 }
 
-// FP8 (e4m3) caches: one 8-row tile, the FP8 ring and per-warp f16 tiles.  A 16-row FP8
-// chunk carries half a bf16 chunk's bytes, so the ring has more stages for the same bytes
-// in flight.
+// FP8 (e4m3) caches: one 8-row tile and the FP8 ring.  A 16-row FP8 chunk carries half a
+// bf16 chunk's bytes; 8 stages (32 KB for 128-dim heads) measured best (12 and 16 a little
+// slower, 24 much slower: 2 CTAs per SM).
 #ifndef DORY_KV8_STAGES
-#define DORY_KV8_STAGES 16
+#define DORY_KV8_STAGES 8
 #endif
 constexpr int kStagesKV8 = DORY_KV8_STAGES;
 template <int HD>
@@ -2455,7 +2461,7 @@ int32_t dispatch_kv8(const KParams& kp, dim3 grid, cudaStream_t stream) {
   constexpr int NS = kStagesKV8;
   static_assert(NS % kConsumerWarps == 0, "ring stages must be a multiple of the consumer warps");
   static_assert(kConsumerWarps * 8 * (HD + 4) * 4 <= Smem<HD, NS, true>::kRegion,
-                "the warps' merge buffer must fit in the ring and staging tiles");
+                "the warps' merge buffer must fit in the ring");
   const int smem = Smem<HD, NS, true>::bytes(kp.nsub);
   const bool dm = one_wave(decode_kernel<HD, 1, NS, false, true, false, true>, grid, smem,
                            Smem<HD, NS, true>::bytes(kMaxSub));
