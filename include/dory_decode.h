@@ -200,8 +200,7 @@ int32_t dory_decode_attention(const DoryDecodeParams* params, void* stream);
  *
  * The array's device address is looked up (cudaGetSymbolAddress) by the first call in each
  * CUDA context: the device's primary context (the runtime's), or a context a driver-API
- * host made current itself.  That first call should come before any stream capture in that
- * context.  Every call clears the merge counters on `stream` before its kernel; the device
+ * host made current itself.  Every call clears the merge counters on `stream` before its kernel; the device
  * error word is kept and gathers the DORY_DEVERR_* bits of every call until
  * dory_decode_static_scratch_fetch_errors reads it.  All calls share the one array and it
  * keeps the last call's contents, so calls that can overlap on the GPU (different streams,
