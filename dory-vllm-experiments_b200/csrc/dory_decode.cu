@@ -862,17 +862,16 @@ __device__ __forceinline__ void sumsq_tail(const KParams& p, const float* sv, in
 // ------------------------------------------------------------------------------------
 // The kernel.  grid = (splits, NKV, T); block = 160 threads (4 consumer warps + producer).
 // ------------------------------------------------------------------------------------
-// CTAs per SM the 128-dim FP8 instantiations are compiled for (registers cap them at 3;
-// 4 forces 96 registers with spills: 1.5% faster on large batches, 5-10% slower on the
-// small and single-sequence steps).
-#ifndef DORY_KV8_MIN_CTAS
-#define DORY_KV8_MIN_CTAS 3
-#endif
-template <int HD, int NT, int NS, bool SS, bool DM, bool FMA = false, bool KV8 = false>
-__global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? (KV8 ? DORY_KV8_MIN_CTAS : 3) : 1)
+// WIDE (128-dim FP8 instantiations for grids of many waves): compiled for 4 CTAs per SM
+// (96 registers, a few spills) instead of 3, for more resident warps in the consumer-bound
+// loop; slower on short grids, where the prologue and merge dominate.
+template <int HD, int NT, int NS, bool SS, bool DM, bool FMA = false, bool KV8 = false,
+          bool WIDE = false>
+__global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? (WIDE ? 4 : 3) : 1)
     decode_kernel(const __grid_constant__ KParams p) {
   static_assert(!FMA || (HD == 128 && NT == 1), "the CUDA-core consumer is 128-dim, one tile");
   static_assert(!KV8 || (NT == 1 && !FMA && HD >= 128), "FP8 caches: 128/256-dim, one tile");
+  static_assert(!WIDE || (KV8 && HD == 128), "the 4-CTA build is the 128-dim FP8 kernel's");
   using L = Smem<HD, NS, KV8>;
   constexpr int KT = HD / 16;          // MMA k-steps over head_dim / m-tiles of O^T
   constexpr int ROWS = NT * 8;         // query rows per CTA
@@ -1511,23 +1510,41 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? (KV8 ? DORY_K
   const int g = lane >> 2;
   const int t4 = lane & 3;
   uint32_t qb[NT][KT][2];
+  // FP8, 128-dim heads: the fragments live in the upper half of the query area (free with
+  // one 8-row tile), [KT / 2][32 lanes] x 16 bytes, reloaded per chunk rather than held in
+  // 16 registers (256-dim heads keep them in registers: one CTA per SM leaves room).  Every
+  // warp writes the same values and each lane reads back only what it wrote itself.
+  constexpr bool kQFragSmem = KV8 && HD == 128;
+  uint4* qfrag = reinterpret_cast<uint4*>(smem + L::kQ + 8 * HD * 2);
+  if constexpr (KV8) {
+    // k-step kk's slot pairs (2t4, 2t4+1), (2t4+8, 2t4+9) are the dims
+    // HD/4 * t4 + 4kk + {0, 1}, {2, 3}, the order the K operands are read in
+    static_assert(8 * HD * 2 >= (KT / 2) * 32 * 16, "the fragments fit in the free half");
+    const uint32_t* row = reinterpret_cast<const uint32_t*>(q2 + g * HD);
+#pragma unroll
+    for (int j = 0; j < KT / 2; ++j) {
+      const int pair = ((HD / 4) * t4 + 8 * j) / 2;
+      const uint4 f = make_uint4(bf16x2_to_f16x2(row[pair]), bf16x2_to_f16x2(row[pair + 1]),
+                                 bf16x2_to_f16x2(row[pair + 2]), bf16x2_to_f16x2(row[pair + 3]));
+      if constexpr (kQFragSmem) {
+        qfrag[j * 32 + lane] = f;
+      } else {
+        qb[0][2 * j][0] = f.x;
+        qb[0][2 * j][1] = f.y;
+        qb[0][2 * j + 1][0] = f.z;
+        qb[0][2 * j + 1][1] = f.w;
+      }
+    }
+  } else {
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
     for (int kk = 0; kk < KT; ++kk) {
-      if constexpr (KV8) {
-        // FP8: k-step kk's slot pairs (2t4, 2t4+1), (2t4+8, 2t4+9) are the dims
-        // HD/4 * t4 + 4kk + {0, 1}, {2, 3}, the order the K operands are read in
-        const uint32_t* row = reinterpret_cast<const uint32_t*>(q2 + (nt * 8 + g) * HD);
-        const int pair = ((HD / 4) * t4 + 4 * kk) / 2;
-        qb[nt][kk][0] = bf16x2_to_f16x2(row[pair]);
-        qb[nt][kk][1] = bf16x2_to_f16x2(row[pair + 1]);
-      } else {
       const uint32_t* row = reinterpret_cast<const uint32_t*>(q2 + (nt * 8 + g) * HD + kk * 16);
       qb[nt][kk][0] = row[t4];
       qb[nt][kk][1] = row[t4 + 4];
-      }
     }
+  }
   // Row bounds of the two query rows this lane accumulates per n-tile.
   int rfirst[NT][2], rlen[NT][2];
 #pragma unroll
@@ -1666,11 +1683,17 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? (KV8 ? DORY_K
         }
 #pragma unroll
       for (int kk = 0; kk < KT; ++kk) {
+        uint32_t b0 = qb[0][kk][0], b1 = qb[0][kk][1];
+        if constexpr (kQFragSmem) {
+          const uint4 qf = qfrag[(kk >> 1) * 32 + lane];
+          b0 = (kk & 1) ? qf.z : qf.x;
+          b1 = (kk & 1) ? qf.w : qf.y;
+        }
         const uint32_t a0 = e4m3x2_to_f16x2(kw[0][kk] & 0xffffu);
         const uint32_t a2 = e4m3x2_to_f16x2(kw[0][kk] >> 16);
         const uint32_t a1 = e4m3x2_to_f16x2(kw[1][kk] & 0xffffu);
         const uint32_t a3 = e4m3x2_to_f16x2(kw[1][kk] >> 16);
-        mma_f16((kk & 1) ? sc2[0] : sc[0], a0, a1, a2, a3, qb[0][kk][0], qb[0][kk][1]);
+        mma_f16((kk & 1) ? sc2[0] : sc[0], a0, a1, a2, a3, b0, b1);
       }
 #pragma unroll
       for (int e = 0; e < 4; ++e) sc[0][e] += sc2[0][e];
@@ -2330,9 +2353,10 @@ int32_t fail(int32_t status, const char* fmt, ...) {
   return status;
 }
 
-template <int HD, int NT, int NS, bool SS, bool DM, bool FMA = false, bool KV8 = false>
+template <int HD, int NT, int NS, bool SS, bool DM, bool FMA = false, bool KV8 = false,
+          bool WIDE = false>
 int32_t launch(const KParams& kp, dim3 grid, int smem_bytes, cudaStream_t stream) {
-  auto fn = decode_kernel<HD, NT, NS, SS, DM, FMA, KV8>;
+  auto fn = decode_kernel<HD, NT, NS, SS, DM, FMA, KV8, WIDE>;
   static int configured[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return fail(DORY_ERR_CUDA, "cudaGetDevice failed");
@@ -2465,6 +2489,13 @@ int32_t dispatch_kv8(const KParams& kp, dim3 grid, cudaStream_t stream) {
   const int smem = Smem<HD, NS, true>::bytes(kp.nsub);
   const bool dm = one_wave(decode_kernel<HD, 1, NS, false, true, false, true>, grid, smem,
                            Smem<HD, NS, true>::bytes(kMaxSub));
+  if constexpr (HD == 128) {
+    // Grids of at least 8 waves of 4 CTAs per SM (large batches) take the 4-CTA build.
+    const long long ctas = (long long)grid.x * grid.y * grid.z;
+    if (!dm && ctas >= 8LL * 4 * sm_count())
+      return kp.sumsq ? launch<HD, 1, NS, true, false, false, true, true>(kp, grid, smem, stream)
+                      : launch<HD, 1, NS, false, false, false, true, true>(kp, grid, smem, stream);
+  }
   if (kp.sumsq)
     return dm ? launch<HD, 1, NS, true, true, false, true>(kp, grid, smem, stream)
               : launch<HD, 1, NS, true, false, false, true>(kp, grid, smem, stream);

@@ -178,3 +178,68 @@ def test_bad_scale_and_dtype_are_refused():
         attn.from_raw(d["qk"][0], d["v"][0], d["sqk"], case.sqk_factor, EPS, d["slots"][0:1],
                       d["key"], d["value"], d["tables"][0], d["seq_lens"][0:1], 0, case.scale,
                       d["gate"][0], d["out"][0])
+
+
+@pytest.mark.parametrize("shape", [(32, 8, 128), (16, 4, 256)])
+def test_out_of_range_block_is_reported_and_left_out(shape):
+    """A block id beyond the pool is reported (DORY_DEVERR_BLOCK_OOB), never dereferenced, and
+    its 16 positions drop out of the softmax: the output equals the oracle's over the table
+    without that entry (window 0, so the positions' order does not matter)."""
+    nh, nkv, hd = shape
+    case = W.single(seed=1230 + hd, context=300, pool_blocks=30, num_heads=nh,
+                    num_kv_heads=nkv, head_dim=hd)
+    dev = torch.device("cuda")
+    ks, vs = 0.5, 0.25
+    d = W.to_device(case, "triton", dev, kv8=(ks, vs))
+    q = O.raw_qkv(case.qk[0], case.v[0], case.sqk, case.sqk_factor, EPS, nh, nkv, hd)[0]
+    q = q.reshape(-1).to(dev)
+    bad = d["tables"][0].clone()
+    bad[3] = 10_000_000  # far outside the 30-block pool
+    attn = DecodeAttention(nh, nkv, hd, dev, splits=4, kv_cache_dtype="fp8")
+    attn(q, d["key"], d["value"], bad, d["seq_lens"][0:1], 0, case.scale, d["gate"][0],
+         d["out"][0], k_scale=ks, v_scale=vs)
+    torch.cuda.synchronize()
+    assert attn.fetch_errors() & 1  # DORY_DEVERR_BLOCK_OOB
+    out = d["out"][0].cpu()
+    assert torch.isfinite(out).all()
+    table = case.tables[0]
+    kept = torch.cat([table[:3], table[4:]])
+    want = O.call_fp8(q.cpu(), d["key"].cpu().contiguous(), d["value"].cpu().contiguous(), kept,
+                      case.seq_lens[0] - case.block_size, 0, case.scale, case.gate[0], nh, ks,
+                      vs)
+    assert_close(out, want)
+
+
+@pytest.mark.parametrize("sumsq", [False, True])
+def test_many_wave_batch(sumsq):
+    """64 sequences x 8 KV heads x 16 splits = 8,192 CTAs: the 4-CTA-per-SM build of the
+    128-dim FP8 kernel (grids of 8 or more waves), with and without the output's sum of
+    squares; padding, a window, outputs, statistic and cache bytes against the oracle."""
+    case = W.batched(seed=1240, num_seqs=64, window=700)
+    case.seq_lens[5] = 0
+    ks, vs = 0.5, 0.25
+    dev = torch.device("cuda")
+    d = W.to_device(case, "triton", dev, kv8=(ks, vs))
+    T = case.tokens
+    attn = DecodeAttention(32, 8, 128, dev, splits=16, max_tokens=T, kv_cache_dtype="fp8")
+    ss = torch.full((T,), -1.0, device=dev) if sumsq else None
+    attn.multi_from_raw(d["qk"], d["v"], d["sqk"], case.sqk_factor, EPS, d["cache_offsets"],
+                        d["key"], d["value"], d["tables"], d["table_offsets"], d["seq_lens"],
+                        case.window, case.scale, d["gate"], d["out"], out_sumsq=ss,
+                        k_scale=ks, v_scale=vs)
+    torch.cuda.synchronize()
+    attn.check_errors()
+    key8, value8 = W.e4m3_bytes(case.key, ks), W.e4m3_bytes(case.value, vs)
+    want = torch.stack([
+        O.from_raw_fp8(case.qk[t], case.v[t], case.sqk, case.sqk_factor, EPS,
+                       case.slot(t) if case.seq_lens[t] > 0 else -1, key8, value8,
+                       case.tables[case.table_rows[t]], case.seq_lens[t], case.window,
+                       case.scale, case.gate[t], 32, 8, ks, vs) for t in range(T)])
+    out = d["out"].cpu()
+    assert torch.isfinite(out).all()
+    assert_close(out, want)
+    assert torch.equal(d["key"].cpu(), key8)
+    assert torch.equal(d["value"].cpu(), value8)
+    if sumsq:
+        torch.testing.assert_close(ss.cpu(), out.double().square().sum((1, 2)).float(),
+                                   rtol=1e-5, atol=1e-6)
