@@ -184,11 +184,15 @@ WORKLOADS = ("config5", "config1", "config2", "config3", "config4",
              "dory640", "dory2048", "dory8192")
 
 
-def tuned_splits(workload: str, world: int):
+def tuned_splits(workload: str, world: int, kv_dtype: str = "bf16"):
     """(splits, min_blocks_per_split) measured fastest on B200 for each workload; config 5
     uses 4 splits once its 512 sequences are partitioned over 2+ GPUs, and 3 splits at 8+
     GPUs, where each GPU's sequences run longest-first (`longest_first`; measured on one
-    GPU's share of each partition)."""
+    GPU's share of each partition).  With an FP8 cache on one GPU, config 5 measured
+    fastest with 2 splits of at least 192 blocks (426 us, against 432 at 128 and 449 at 64
+    blocks)."""
+    if workload == "config5" and world == 1 and kv_dtype == "fp8":
+        return (2, 192)
     if workload == "config5":
         return (2, 64) if world == 1 else (4, 64) if world < 8 else (3, 64)
     return {"config1": (16, 1), "config2": (16, 1), "config3": (2, 32),
@@ -1333,7 +1337,7 @@ def main() -> int:
     if args.warmup < 3:
         ap.error("--warmup must be >= 3")
     world, rank, local = dist_env()
-    tuned = tuned_splits(args.workload, world)
+    tuned = tuned_splits(args.workload, world, args.kv_dtype)
     if args.splits is None:
         args.splits = tuned[0]
     if args.min_blocks_per_split is None:

@@ -862,7 +862,7 @@ __device__ __forceinline__ void sumsq_tail(const KParams& p, const float* sv, in
 // ------------------------------------------------------------------------------------
 // The kernel.  grid = (splits, NKV, T); block = 160 threads (4 consumer warps + producer).
 // ------------------------------------------------------------------------------------
-// WIDE (128-dim FP8 instantiations for grids of many waves): compiled for 4 CTAs per SM
+// WIDE (128-dim FP8 instantiations for grids of several waves): compiled for 4 CTAs per SM
 // (96 registers, a few spills) instead of 3, for more resident warps in the consumer-bound
 // loop; slower on short grids, where the prologue and merge dominate.
 template <int HD, int NT, int NS, bool SS, bool DM, bool FMA = false, bool KV8 = false,
@@ -2480,6 +2480,10 @@ int32_t dispatch_fma(const KParams& kp, dim3 grid, cudaStream_t stream) {
 #define DORY_KV8_STAGES 8
 #endif
 constexpr int kStagesKV8 = DORY_KV8_STAGES;
+#ifndef DORY_KV8_WIDE_WAVES
+#define DORY_KV8_WIDE_WAVES 2
+#endif
+constexpr int kWideWaves = DORY_KV8_WIDE_WAVES;
 template <int HD>
 int32_t dispatch_kv8(const KParams& kp, dim3 grid, cudaStream_t stream) {
   constexpr int NS = kStagesKV8;
@@ -2490,9 +2494,10 @@ int32_t dispatch_kv8(const KParams& kp, dim3 grid, cudaStream_t stream) {
   const bool dm = one_wave(decode_kernel<HD, 1, NS, false, true, false, true>, grid, smem,
                            Smem<HD, NS, true>::bytes(kMaxSub));
   if constexpr (HD == 128) {
-    // Grids of at least 8 waves of 4 CTAs per SM (large batches) take the 4-CTA build.
+    // Grids of at least kWideWaves waves of 4 CTAs per SM (large batches) take the 4-CTA
+    // build.
     const long long ctas = (long long)grid.x * grid.y * grid.z;
-    if (!dm && ctas >= 8LL * 4 * sm_count())
+    if (!dm && ctas >= (long long)kWideWaves * 4 * sm_count())
       return kp.sumsq ? launch<HD, 1, NS, true, false, false, true, true>(kp, grid, smem, stream)
                       : launch<HD, 1, NS, false, false, false, true, true>(kp, grid, smem, stream);
   }

@@ -210,18 +210,19 @@ def test_out_of_range_block_is_reported_and_left_out(shape):
     assert_close(out, want)
 
 
-@pytest.mark.parametrize("sumsq", [False, True])
-def test_many_wave_batch(sumsq):
-    """64 sequences x 8 KV heads x 16 splits = 8,192 CTAs: the 4-CTA-per-SM build of the
-    128-dim FP8 kernel (grids of 8 or more waves), with and without the output's sum of
-    squares; padding, a window, outputs, statistic and cache bytes against the oracle."""
+@pytest.mark.parametrize("splits,sumsq", [(16, False), (16, True), (2, False), (2, True)])
+def test_large_batch(splits, sumsq):
+    """64 sequences x 8 KV heads: with 16 splits (8,192 CTAs) the 4-CTA-per-SM build of the
+    128-dim FP8 kernel (grids of 2 or more waves), with 2 splits (1,024 CTAs) the 3-CTA build
+    with the last-arriving split merging; with and without the output's sum of squares;
+    padding, a window, outputs, statistic and cache bytes against the oracle."""
     case = W.batched(seed=1240, num_seqs=64, window=700)
     case.seq_lens[5] = 0
     ks, vs = 0.5, 0.25
     dev = torch.device("cuda")
     d = W.to_device(case, "triton", dev, kv8=(ks, vs))
     T = case.tokens
-    attn = DecodeAttention(32, 8, 128, dev, splits=16, max_tokens=T, kv_cache_dtype="fp8")
+    attn = DecodeAttention(32, 8, 128, dev, splits=splits, max_tokens=T, kv_cache_dtype="fp8")
     ss = torch.full((T,), -1.0, device=dev) if sumsq else None
     attn.multi_from_raw(d["qk"], d["v"], d["sqk"], case.sqk_factor, EPS, d["cache_offsets"],
                         d["key"], d["value"], d["tables"], d["table_offsets"], d["seq_lens"],
