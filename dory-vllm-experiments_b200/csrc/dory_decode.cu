@@ -657,6 +657,67 @@ __device__ __forceinline__ bool fixup_stage(const KParams& p, uint8_t* kst, uint
   return touched;
 }
 
+// The e4m3 bytes of 16 dims of a new row (exact e4m3 values held as bf16), dim 0 in byte 0.
+__device__ __forceinline__ uint4 e4m3x16(const __nv_bfloat16* src) {
+  uint32_t b[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e)
+    b[e] = f32x2_to_e4m3x2(__bfloat162float(src[2 * e]), __bfloat162float(src[2 * e + 1]));
+  return make_uint4(b[0] | (b[1] << 16), b[2] | (b[3] << 16), b[4] | (b[5] << 16),
+                    b[6] | (b[7] << 16));
+}
+
+// FP8 shared caches: a stage that holds a sub token's new row gets the row's e4m3 bytes (the
+// write-all-first order, as fixup_stage does for bf16 stages), and the rows of this CTA's
+// own group tokens are appended to the cache here.  Rows outside the attended range and bad
+// blocks need no zeroing: the consumer masks them.
+template <int HD>
+__device__ __forceinline__ void fixup_stage8(const KParams& p, uint8_t* kst, uint8_t* vst, int c,
+                                             int phys, int lane, const CtaInfo& ci,
+                                             const int* s_len, const int* s_phys,
+                                             const long long* s_coff, const long long* s_toff,
+                                             const __nv_bfloat16* subkv) {
+  constexpr int kVec8 = HD / 16;  // 16-byte pieces per e4m3 row
+  const int B = p.B;
+  const int CPB = B / kChunk;
+  for (int s = 0; s < ci.nsub; ++s) {
+    const int len = s_len[s];
+    if (len <= 0) continue;
+    const int pos = len - 1;
+    const bool same = s_coff[s] == ci.coff && s_toff[s] == ci.toff;
+    int r = -1;
+    if (same) {
+      if (pos / kChunk == c) r = pos % kChunk;
+    } else if (phys >= 0 && s_phys[s] == phys && s_coff[s] == ci.coff) {
+      const int rr = mod_p2(pos, B, p.b_shift) - mod_p2(c, CPB, p.cpb_shift) * kChunk;
+      if (rr >= 0 && rr < kChunk) r = rr;
+    }
+    if (r < 0) continue;
+    long long base = -1;  // the cache row this CTA appends, if any
+    if (same && s >= ci.ibase && s < ci.ibase + ci.gcount) {
+      long long slot = -1;
+      if (p.slot_mapping) slot = p.slot_mapping[s];  // negative: not cached
+      else if (phys >= 0) slot = (long long)phys * B + mod_p2(pos, B, p.b_shift);
+      if (slot >= 0) {
+        const long long blk = slot / B;
+        if ((p.ncache_blocks > 0 && blk >= p.ncache_blocks) || !ci.offset_ok) {
+          if (lane == 0) record_error(p.err, DORY_DEVERR_SLOT_OOB);
+        } else {
+          base = s_coff[s] + blk * p.sb + (slot % B) * p.so + (long long)ci.kvh * p.sh;
+        }
+      }
+    }
+    for (int idx = lane; idx < 2 * kVec8; idx += 32) {
+      const bool is_v = idx >= kVec8;
+      const int w = is_v ? idx - kVec8 : idx;
+      const uint4 val = e4m3x16(subkv + (s * 2 + (is_v ? 1 : 0)) * HD + w * 16);
+      *reinterpret_cast<uint4*>((is_v ? vst : kst) + tile_off8(r, w * 16)) = val;
+      if (base >= 0)
+        reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(is_v ? p.vc : p.kc) + base)[w] = val;
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------------
 // Cross-split merge of one (token group, KV head) by its last CTA: thread tid owns output
 // units tid + k * 128 (k < UPT), a unit being 4 consecutive dims of one query row.
@@ -1445,8 +1506,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? (WIDE ? 4 : 3
 #pragma unroll
       for (int i = 0; i < PER_LANE; ++i) {
         const int d = lane * PER_LANE + i;
-        subkv[(s * 2 + 0) * HD + d] = __float2bfloat16_rn(__fmul_rn(kv[i], rn));
-        subkv[(s * 2 + 1) * HD + d] = __float2bfloat16_rn(vsrc[d]);
+        subkv[(s * 2 + 0) * HD + d] = new_kv<KV8>(__fmul_rn(kv[i], rn), p.k_scale);
+        subkv[(s * 2 + 1) * HD + d] = new_kv<KV8>(vsrc[d], p.v_scale);
       }
     }
   }
@@ -1482,13 +1543,7 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? (WIDE ? 4 : 3
             for (int idx = lane; idx < 2 * kVec8; idx += 32) {
               const bool is_v = idx >= kVec8;
               const int w = is_v ? idx - kVec8 : idx;
-              const __nv_bfloat16* src = subkv + (is_v ? HD : 0) + w * 16;
-              uint32_t b[8];
-#pragma unroll
-              for (int e = 0; e < 8; ++e)
-                b[e] = f32x2_to_e4m3x2(__bfloat162float(src[2 * e]), __bfloat162float(src[2 * e + 1]));
-              const uint4 val = make_uint4(b[0] | (b[1] << 16), b[2] | (b[3] << 16),
-                                           b[4] | (b[5] << 16), b[6] | (b[7] << 16));
+              const uint4 val = e4m3x16(subkv + (is_v ? HD : 0) + w * 16);
               uint8_t* dst = reinterpret_cast<uint8_t*>(is_v ? p.vc : p.kc) + base;
               reinterpret_cast<uint4*>(dst)[w] = val;
             }
@@ -1648,7 +1703,13 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? (WIDE ? 4 : 3
     bool touched = false;
     const bool partial = !KV8 && use_tma && (c < c_full_lo || c >= c_full_hi || phys < 0);
     if constexpr (KV8) {
-      // FP8: no slow path; the operands come from the stage's bytes below
+      // FP8: only stages holding a shared-cache sub token's new row take a slow path (the
+      // row's bytes, and its append); edges and bad blocks are masked by the consumer.
+      if ((c >= sub_lo && c <= sub_hi) || any_foreign) {
+        fixup_stage8<HD>(p, kst, vst, c, phys, lane, s_ci, s_len, s_phys, s_coff, s_toff,
+                         subkv);
+        __syncwarp();
+      }
     } else {
     if ((partial && !kRowMask) || (c >= sub_lo && c <= sub_hi) || any_foreign)
       touched = fixup_stage<HD>(p, kst, vst, c, phys, partial && !kRowMask, lane, s_ci, s_len,
@@ -2857,10 +2918,10 @@ int32_t dory_decode_attention(const DoryDecodeParams* P, void* stream) {
     return fail(DORY_ERR_UNSUPPORTED, "block_size %d is not a multiple of 16", a.block_size);
   const int G = a.num_heads / a.num_kv_heads;
   if (G > 16) return fail(DORY_ERR_UNSUPPORTED, "%d query heads per KV head (max 16)", G);
-  if (kv8 && (HD < 128 || G > 8 || shared || fma || a.num_cache_blocks <= 0))
+  if (kv8 && (HD < 128 || G > 8 || fma || a.num_cache_blocks <= 0))
     return fail(DORY_ERR_UNSUPPORTED,
                 "FP8 caches take 128/256-dim heads, at most 8 query heads per KV head, a "
-                "known block count, no shared cache and the tensor-core consumer");
+                "known block count and the tensor-core consumer");
   if (kv8 && !(a.k_scale > 0.0f && a.v_scale > 0.0f && a.k_scale < 3.4e38f && a.v_scale < 3.4e38f))
     return fail(DORY_ERR_INVALID_ARGUMENT, "FP8 caches need positive, finite k/v scales");
   if (fma && (HD != 128 || G > 4 || shared))

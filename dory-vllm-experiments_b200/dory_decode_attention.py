@@ -72,8 +72,8 @@ class DecodeAttention:
     views of the same shape), K = e4m3 * k_scale and V = e4m3 * v_scale, the scales passed
     to each call (vLLM's per-layer k_scale / v_scale, default 1.0); a raw call appends
     e4m3(bf16(k) / k_scale) and e4m3(bf16(v) / v_scale) (round to nearest even, saturated at
-    +-448) and attends those values.  128/256-dim heads, at most 8 query heads per KV head,
-    no shared cache.
+    +-448) and attends those values, shared caches included.  128/256-dim heads, at most 8
+    query heads per KV head.
     """
 
     def __init__(self, num_heads: int, num_kv_heads: int, head_dim: int, device: torch.device,

@@ -147,8 +147,9 @@ typedef struct DoryDecodeParams {
                                    * k_scale and V = e4m3 * v_scale, and a raw call appends
                                    * e4m3(bf16(k) / k_scale) and e4m3(bf16(v) / v_scale),
                                    * rounded to nearest even and saturated at +-448, the
-                                   * values it attends.  128/256-dim heads, at most 8 query
-                                   * heads per KV head, no SHARED_CACHE, num_cache_blocks > 0.
+                                   * values it attends (SHARED_CACHE included).  128/256-dim
+                                   * heads, at most 8 query heads per KV head,
+                                   * num_cache_blocks > 0.
                                    * No counterpart in the reference (its caches are bf16;
                                    * vLLM's "fp8" kv_cache_dtype).                           */
   float k_scale;                  /* FP8 caches: positive, finite                           */

@@ -415,6 +415,66 @@ def from_raw_fp8(qk, v, sqk, sqk_factor, eps, slot: int, key8, value8, block_tab
     return nibble_major(out * gate.float().cpu())
 
 
+def multi_from_raw_fp8(qk, v, sqk, sqk_factor, eps, cache_offsets, key8_flat, value8_flat,
+                       cache_shape, cache_strides, block_tables_flat, block_table_offsets,
+                       seq_lens, window: int, softmax_scale: float, gate, num_heads: int,
+                       num_kv_heads: int, k_scale: float, v_scale: float,
+                       shared_cache: bool = False) -> torch.Tensor:
+    """DecodeAttention.multi_from_raw over e4m3 caches: multi_from_raw's semantics above
+    (dory_decode_attention.py:270-305; shared caches write every token's row first,
+    :294-301) with each token's new bf16 k / v quantised with the layer's scales, attended as
+    those values and appended as those bytes.  key8_flat / value8_flat are the flat uint8
+    storage; token t's view is as_strided(cache_shape, cache_strides, cache_offsets[t])."""
+    T = qk.shape[0]
+    HD = cache_shape[-1]
+    B = cache_shape[1]
+    keyf, valuef = e4m3_dequantize(key8_flat, k_scale), e4m3_dequantize(value8_flat, v_scale)
+    views, news, slots = [], [], []
+    for t in range(T):
+        off = int(cache_offsets[t])
+        table = block_tables_flat[int(block_table_offsets[t]):]
+        views.append([x.as_strided(cache_shape, cache_strides, off)
+                      for x in (keyf, valuef, key8_flat, value8_flat)] + [table])
+        q, k_new, v_new = raw_qkv(qk[t], v[t], sqk, sqk_factor, eps, num_heads, num_kv_heads,
+                                  HD)
+        news.append((q, e4m3_quantize(k_new, k_scale), e4m3_quantize(v_new, v_scale)))
+        n = int(seq_lens[t])
+        slots.append(int(table[(n - 1) // B]) * B + (n - 1) % B if n > 0 else -1)
+
+    def put(t, rows):
+        kf, vf, k8, v8, _ = views[t]
+        b, o = slots[t] // B, slots[t] % B
+        saved = (kf[b, o].clone(), vf[b, o].clone())
+        kf[b, o], vf[b, o] = rows
+        return saved
+
+    def deq(t):
+        return (e4m3_dequantize(news[t][1], k_scale), e4m3_dequantize(news[t][2], v_scale))
+
+    outs = []
+    if shared_cache:
+        for t in range(T):
+            if slots[t] >= 0:
+                put(t, deq(t))
+    for t in range(T):
+        kf, vf, _, _, table = views[t]
+        n = int(seq_lens[t])
+        if n <= 0:
+            outs.append(nibble_major(torch.zeros(num_heads * HD) * gate[t].float().cpu()))
+            continue
+        saved = None if shared_cache else put(t, deq(t))
+        out = attention(news[t][0], kf, vf, table, n, window, num_heads, B, softmax_scale)
+        if saved is not None:
+            put(t, saved)
+        outs.append(nibble_major(out * gate[t].float().cpu()))
+    for t in range(T):  # the appended bytes
+        if slots[t] >= 0:
+            _, _, k8, v8, _ = views[t]
+            k8[slots[t] // B, slots[t] % B] = news[t][1]
+            v8[slots[t] // B, slots[t] % B] = news[t][2]
+    return torch.stack(outs)
+
+
 def relative_error(x: torch.Tensor, reference: torch.Tensor) -> float:
     """Relative L2 error (kernels/bench_mlp.py:120-121)."""
     x, reference = x.float().flatten(), reference.float().flatten()

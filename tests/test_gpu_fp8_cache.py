@@ -9,8 +9,9 @@ have (parity unpinned: there is no reference output to compare with).
   k_scale) and e4m3(bf16(v) / v_scale) exactly.
 * Layouts (K and V interleaved per row, or separate), 128- and 256-dim heads, 4 or 8 query
   heads per KV head, windows, split layouts, padding tokens, NaN bytes outside the attended
-  ranges, scales other than 1, the non-raw call; and agreement with the bf16 path on a
-  cache whose bf16 values are the dequantised ones (power-of-two scales keep them exact).
+  ranges, scales other than 1, shared caches, the non-raw call; and agreement with the bf16
+  path on a cache whose bf16 values are the dequantised ones (power-of-two scales keep them
+  exact).
 """
 
 from __future__ import annotations
@@ -54,6 +55,15 @@ def run_fp8(case: W.Case, layout="triton", splits=16, scales=(1.0, 1.0), window=
     torch.cuda.synchronize()
     attn.check_errors()
     key8, value8 = W.e4m3_bytes(case.key, ks), W.e4m3_bytes(case.value, vs)
+    if case.shared:  # write-all-first over one cache (oracle.multi_from_raw_fp8)
+        width = case.tables.shape[1]
+        want = O.multi_from_raw_fp8(
+            case.qk, case.v, case.sqk, case.sqk_factor, EPS, torch.zeros(T, dtype=torch.int64),
+            key8.view(-1), value8.view(-1), tuple(key8.shape), key8.stride(),
+            case.tables.reshape(-1), torch.tensor([r * width for r in case.table_rows]),
+            case.seq_lens, case.window, case.scale, case.gate, case.num_heads,
+            case.num_kv_heads, ks, vs, shared_cache=True)
+        return d["out"].cpu(), want, (d["key"].cpu(), d["value"].cpu()), (key8, value8)
     want = []
     for t in range(T):
         want.append(O.from_raw_fp8(case.qk[t], case.v[t], case.sqk, case.sqk_factor, EPS,
@@ -160,10 +170,31 @@ def test_unsupported_shapes_are_refused(shape):
         run_fp8(case)
 
 
-def test_shared_cache_is_refused():
-    case = W.wavefront(seed=1221, prompt=100, generated=0, tokens=2)
-    with pytest.raises(NotImplementedError):
-        run_fp8(case)
+@pytest.mark.parametrize("hd", [128, 256])
+@pytest.mark.parametrize("tokens", [2, 4, 6])
+def test_shared_wavefront(tokens, hd):
+    """Shared ("last_loop") caches: tokens at consecutive positions read each other's new
+    rows as e4m3 bytes (write-all-first); groups of 8 / G tokens per CTA, more than four sub
+    tokens, each CTA appending its own group's rows."""
+    nh, nkv = (32, 8) if hd == 128 else (16, 4)
+    case = W.wavefront(seed=1260 + tokens + hd, prompt=450, generated=3, tokens=tokens,
+                       num_heads=nh, num_kv_heads=nkv, head_dim=hd)
+    check(case, splits=8, scales=(0.5, 0.25))
+
+
+def test_shared_wavefront_window_and_split_layouts():
+    case = W.wavefront(seed=1270, prompt=700, tokens=4, window=300)
+    for splits in (1, 16):
+        check(case, splits=splits, scales=(1.0, 2.0))
+
+
+def test_shared_with_distinct_tables_falls_back_per_token():
+    """Tokens reading one pool through different table rows: processed per token, every new
+    row still substituted where it aliases another token's block."""
+    case = W.wavefront(seed=1271, prompt=300, tokens=4)
+    case.tables = torch.cat([case.tables, case.tables])
+    case.table_rows = [0, 0, 1, 1]
+    check(case, splits=4, scales=(0.25, 0.5))
 
 
 def test_bad_scale_and_dtype_are_refused():
