@@ -664,8 +664,8 @@ def bench_ours(args, world, rank, local):
     wl = DeviceWorkload(spec, lens, dev, spec.seed + 1000 * rank, kv_dtype=args.kv_dtype)
     if args.sumsq:
         wl.sumsq = torch.zeros(wl.num_layers, wl.tokens, device=dev)
-    if args.kv_dtype == "fp8" and (args.path != "fused" or spec.shared):
-        raise SystemExit("--kv-dtype fp8 takes the fused path of unshared workloads")
+    if args.kv_dtype == "fp8" and args.path != "fused":
+        raise SystemExit("--kv-dtype fp8 takes the fused path")
     if args.path in ("separate", "call") and wl.tokens != 1:
         raise SystemExit(f"--path {args.path} takes single-sequence workloads "
                          "(config1, config4, dory*)")

@@ -117,11 +117,13 @@ class WavefrontAttention:
                        eps: float, block_tables: torch.Tensor, seq_lens: torch.Tensor,
                        window: int, softmax_scale: float, gate: torch.Tensor,
                        out_nibble_major: torch.Tensor, shared_cache: bool = False,
-                       out_sumsq: torch.Tensor | None = None) -> None:
+                       out_sumsq: torch.Tensor | None = None, *, k_scale: float = 1.0,
+                       v_scale: float = 1.0) -> None:
         """The rows' multi_from_raw (qk FP32 [rows, (heads + kv_heads) * head_dim], v, gate,
         out_nibble_major [rows, 8, heads * head_dim / 8], seq_lens int32 [rows]; row t at
         loop pattern[t]) against the layer's caches and the engine's block tables
-        ([tables, width], contiguous)."""
+        ([tables, width], contiguous).  k_scale / v_scale: the layer's FP8 cache scales
+        (an instance built with kv_cache_dtype="fp8")."""
         if block_tables.dim() != 2 or block_tables.shape[1] != layer.width:
             raise ValueError("block_tables must be [tables, width] with the layer's width")
         if len(pattern) != qk.shape[0]:
@@ -130,7 +132,8 @@ class WavefrontAttention:
         self.attention.multi_from_raw(qk, v, sqk, sqk_factor, eps, cache_offsets, layer.key,
                                       layer.value, block_tables, table_offsets, seq_lens,
                                       window, softmax_scale, gate, out_nibble_major,
-                                      shared_cache=shared_cache, out_sumsq=out_sumsq)
+                                      shared_cache=shared_cache, out_sumsq=out_sumsq,
+                                      k_scale=k_scale, v_scale=v_scale)
 
 
 def entry_slots(block_tables: torch.Tensor, position: torch.Tensor, block_size: int,
@@ -150,13 +153,16 @@ class AttentionSublayer:
     """One attention layer of the recurrent block: its bound caches (WavefrontLayer) and the
     per-layer inputs of the non-GEMM steps of `MultiTokenSublayers.attention`
     (kernels/dory_multi_token.py:183-210): sqk for the q normalisation, s_gate and the
-    rotary cos/sin table for the q/k/v/gate epilogue, alpha for the residual update, and the
-    layer's window and softmax scale."""
+    rotary cos/sin table for the q/k/v/gate epilogue, alpha for the residual update, the
+    layer's window and softmax scale, and its FP8 cache scales (k_scale / v_scale, used when
+    the block's DecodeAttention has kv_cache_dtype="fp8")."""
 
     def __init__(self, layer: WavefrontLayer, sqk: torch.Tensor, s_gate: torch.Tensor,
-                 cos_sin: torch.Tensor, alpha: torch.Tensor, window: int, softmax_scale: float):
+                 cos_sin: torch.Tensor, alpha: torch.Tensor, window: int, softmax_scale: float,
+                 k_scale: float = 1.0, v_scale: float = 1.0):
         self.layer, self.sqk, self.s_gate, self.cos_sin = layer, sqk, s_gate, cos_sin
         self.alpha, self.window, self.softmax_scale = alpha, int(window), float(softmax_scale)
+        self.k_scale, self.v_scale = float(k_scale), float(v_scale)
 
 
 class WavefrontRecurrentBlock:
@@ -239,7 +245,8 @@ class WavefrontRecurrentBlock:
                                      self.sqk_factor, self.eps, self.block_tables, seq_lens[:k],
                                      sub.window, sub.softmax_scale, self.gate[:k],
                                      self.attention_out[:k], shared_cache=self.shared_cache,
-                                     out_sumsq=self.sumsq[:k])
+                                     out_sumsq=self.sumsq[:k], k_scale=sub.k_scale,
+                                     v_scale=sub.v_scale)
             if self.out_gemv is not None:
                 self.out_gemv(i, self.attention_out[:k], self.out_partials(i, k))
             out, nm = self.h[i % 2][:k], self.h_nm[i % 2][:k]

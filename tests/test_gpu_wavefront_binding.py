@@ -6,7 +6,8 @@
   loop's cache and every loop's cache bit-exact after its row's append
   (kernels/dory_wavefront_engine.py:257-332, :393-420).
 * A shared "last_loop" cache (the same tensor for every loop, shared_cache=True): the
-  wavefront's rows against the oracle's write-all-first semantics.
+  wavefront's rows against the oracle's write-all-first semantics, with bf16 and FP8 (e4m3)
+  caches.
 * Both vLLM cache layouts; `entry_slots` against the slots the oracle appends at.
 """
 
@@ -95,6 +96,35 @@ def test_shared_last_loop_cache():
     assert_close(d["out"].cpu(), oracle_out(case))
     exp = expected_raw(case, "triton", before.cpu(), oracle_rows(case))
     assert torch.equal(d["raw"].cpu().view(torch.int16), exp.view(torch.int16))
+
+
+def test_shared_last_loop_fp8_cache():
+    """The same call over an e4m3 cache (kv_cache_dtype="fp8", the layer's scales passed
+    through the binding): outputs and cache bytes against oracle.multi_from_raw_fp8."""
+    import dory_oracle as O
+    case = W.wavefront(seed=311, prompt=700, generated=4, tokens=3)
+    ks, vs = 0.5, 0.25
+    d = W.to_device(case, "triton", DEV, kv8=(ks, vs))
+    width = case.tables.shape[1]
+    layer = WB.WavefrontLayer([d["raw"]] * 3, [0] * 3, width, case.num_kv_heads, case.head_dim)
+    attn = DecodeAttention(case.num_heads, case.num_kv_heads, case.head_dim, DEV, max_tokens=3,
+                           kv_cache_dtype="fp8")
+    WB.WavefrontAttention(attn).attention_call(
+        layer, WB.recurrent_pattern(3), d["qk"], d["v"], d["sqk"], case.sqk_factor, EPS,
+        d["tables"], d["seq_lens"], case.window, case.scale, d["gate"], d["out"],
+        shared_cache=True, k_scale=ks, v_scale=vs)
+    torch.cuda.synchronize()
+    attn.check_errors()
+    key8, value8 = W.e4m3_bytes(case.key, ks), W.e4m3_bytes(case.value, vs)
+    want = O.multi_from_raw_fp8(
+        case.qk, case.v, case.sqk, case.sqk_factor, EPS, torch.zeros(3, dtype=torch.int64),
+        key8.view(-1), value8.view(-1), tuple(key8.shape), key8.stride(),
+        case.tables.reshape(-1), torch.zeros(3, dtype=torch.int64), case.seq_lens,
+        case.window, case.scale, case.gate, case.num_heads, case.num_kv_heads, ks, vs,
+        shared_cache=True)
+    assert_close(d["out"].cpu(), want)
+    assert torch.equal(d["key"].cpu(), key8)
+    assert torch.equal(d["value"].cpu(), value8)
 
 
 def test_entry_slots_on_the_device():
