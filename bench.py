@@ -640,7 +640,7 @@ def roofline_of(wl: DeviceWorkload, workload: str, us_per_launch: float) -> dict
     peaks = load_peaks()
     per_launch = wl.algorithmic_bytes_per_step() / len(wl.layers)
     achieved = per_launch / (us_per_launch * 1e-6) / 1e9
-    ratio = read_traffic_ratio(workload)
+    ratio = read_traffic_ratio(workload, "fp8" if wl.kv8 else "bf16")
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks[0], "unit": "GB/s",
             "frac": round(achieved / peaks[0], 4),
             "traffic": int(ratio * per_launch) if ratio else None, "peak_source": peaks[1],
@@ -988,10 +988,12 @@ def load_peaks():
         return 6650.0, "fallback (6.65 TB/s earlier pool measurement)"
 
 
-def read_traffic_ratio(workload: str):
+def read_traffic_ratio(workload: str, kv_dtype: str = "bf16"):
     """DRAM traffic / algorithmic bytes of one launch, from the committed ncu summary of this
-    workload (profiles/decode_kernel_<workload>.txt), or None."""
-    path = ROOT / "profiles" / f"decode_kernel_{workload}.txt"
+    workload and cache type (profiles/decode_kernel_<workload>.txt, or
+    decode_kernel_fp8_<workload>.txt for FP8 caches), or None."""
+    kind = "fp8_" if kv_dtype == "fp8" else ""
+    path = ROOT / "profiles" / f"decode_kernel_{kind}{workload}.txt"
     if not path.exists():
         return None
     for line in path.read_text().splitlines():

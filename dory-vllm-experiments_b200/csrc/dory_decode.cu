@@ -1592,13 +1592,14 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? (WIDE ? 4 : 3
     }
   } else {
 #pragma unroll
-  for (int nt = 0; nt < NT; ++nt)
+    for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
-    for (int kk = 0; kk < KT; ++kk) {
-      const uint32_t* row = reinterpret_cast<const uint32_t*>(q2 + (nt * 8 + g) * HD + kk * 16);
-      qb[nt][kk][0] = row[t4];
-      qb[nt][kk][1] = row[t4 + 4];
-    }
+      for (int kk = 0; kk < KT; ++kk) {
+        const uint32_t* row =
+            reinterpret_cast<const uint32_t*>(q2 + (nt * 8 + g) * HD + kk * 16);
+        qb[nt][kk][0] = row[t4];
+        qb[nt][kk][1] = row[t4 + 4];
+      }
   }
   // Row bounds of the two query rows this lane accumulates per n-tile.
   int rfirst[NT][2], rlen[NT][2];
@@ -1711,10 +1712,10 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? (WIDE ? 4 : 3
         __syncwarp();
       }
     } else {
-    if ((partial && !kRowMask) || (c >= sub_lo && c <= sub_hi) || any_foreign)
-      touched = fixup_stage<HD>(p, kst, vst, c, phys, partial && !kRowMask, lane, s_ci, s_len,
-                                s_phys, s_coff, s_toff, subkv);
-    __syncwarp();
+      if ((partial && !kRowMask) || (c >= sub_lo && c <= sub_hi) || any_foreign)
+        touched = fixup_stage<HD>(p, kst, vst, c, phys, partial && !kRowMask, lane, s_ci,
+                                  s_len, s_phys, s_coff, s_toff, subkv);
+      __syncwarp();
     }
 
     // S^T = K Q^T : [16 tokens x 8 rows] per n-tile, as two independent MMA chains (even
@@ -1949,8 +1950,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? (WIDE ? 4 : 3
           dst[(HD / 8) * g + 2 * kk] = o[nt][kk][i] * vsc;
           dst[(HD / 8) * g + 2 * kk + 1] = o[nt][kk][2 + i] * vsc;
         } else {
-        dst[kk * 16 + g] = o[nt][kk][i];
-        dst[kk * 16 + g + 8] = o[nt][kk][2 + i];
+          dst[kk * 16 + g] = o[nt][kk][i];
+          dst[kk * 16 + g + 8] = o[nt][kk][2 + i];
         }
       }
     }
