@@ -171,7 +171,9 @@ struct Smem {
   static constexpr int kRegion = NS * kStageBytes;            // reused after the loop
   static constexpr int kBars = kStages + NS * kStageBytes;    // full[NS], empty[NS]
   static constexpr int kMeta = kBars + 2 * NS * 8;            // int4 {phys, -, chunk, -}
-  static constexpr int kQ = kMeta + NS * 16;                  // bf16 [16][HD]
+  // bf16 [16][HD]; with one 8-row tile the upper half holds the CUDA-core consumer's P
+  // buffers or the 128-dim FP8 kernel's query fragments
+  static constexpr int kQ = kMeta + NS * 16;
   static constexpr int kSub = kQ + 16 * HD * 2;               // bf16 [nsub][2][HD]
   static int bytes(int nsub) { return kSub + (nsub > 0 ? nsub : 1) * 2 * HD * 2 + 1024; }
 };
