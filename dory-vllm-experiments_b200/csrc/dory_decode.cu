@@ -927,14 +927,17 @@ __device__ __forceinline__ void sumsq_tail(const KParams& p, const float* sv, in
 // ------------------------------------------------------------------------------------
 // WIDE (128-dim FP8 instantiations for grids of several waves): compiled for 4 CTAs per SM
 // (96 registers, a few spills) instead of 3, for more resident warps in the consumer-bound
-// loop; slower on short grids, where the prologue and merge dominate.
+// loop; slower on short grids, where the prologue and merge dominate.  SHK (FP8
+// instantiations for shared caches): the only FP8 builds with the new-row slow path, whose
+// code alone slowed the other FP8 builds by 2-3%.
 template <int HD, int NT, int NS, bool SS, bool DM, bool FMA = false, bool KV8 = false,
-          bool WIDE = false>
+          bool WIDE = false, bool SHK = false>
 __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? (WIDE ? 4 : 3) : 1)
     decode_kernel(const __grid_constant__ KParams p) {
   static_assert(!FMA || (HD == 128 && NT == 1), "the CUDA-core consumer is 128-dim, one tile");
   static_assert(!KV8 || (NT == 1 && !FMA && HD >= 128), "FP8 caches: 128/256-dim, one tile");
   static_assert(!WIDE || (KV8 && HD == 128), "the 4-CTA build is the 128-dim FP8 kernel's");
+  static_assert(!SHK || (KV8 && !WIDE), "shared-cache builds are FP8 3-CTA builds");
   using L = Smem<HD, NS, KV8>;
   constexpr int KT = HD / 16;          // MMA k-steps over head_dim / m-tiles of O^T
   constexpr int ROWS = NT * 8;         // query rows per CTA
@@ -1508,8 +1511,8 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? (WIDE ? 4 : 3
 #pragma unroll
       for (int i = 0; i < PER_LANE; ++i) {
         const int d = lane * PER_LANE + i;
-        subkv[(s * 2 + 0) * HD + d] = new_kv<KV8>(__fmul_rn(kv[i], rn), p.k_scale);
-        subkv[(s * 2 + 1) * HD + d] = new_kv<KV8>(vsrc[d], p.v_scale);
+        subkv[(s * 2 + 0) * HD + d] = new_kv<SHK>(__fmul_rn(kv[i], rn), p.k_scale);
+        subkv[(s * 2 + 1) * HD + d] = new_kv<SHK>(vsrc[d], p.v_scale);
       }
     }
   }
@@ -1705,14 +1708,16 @@ __global__ void __launch_bounds__(kThreads, NT == 1 && HD <= 128 ? (WIDE ? 4 : 3
     // (zeroing, substitution, the append itself); the rest go straight to the math.
     bool touched = false;
     const bool partial = !KV8 && use_tma && (c < c_full_lo || c >= c_full_hi || phys < 0);
-    if constexpr (KV8) {
-      // FP8: only stages holding a shared-cache sub token's new row take a slow path (the
+    if constexpr (SHK) {
+      // FP8, shared caches: only stages holding a sub token's new row take a slow path (the
       // row's bytes, and its append); edges and bad blocks are masked by the consumer.
       if ((c >= sub_lo && c <= sub_hi) || any_foreign) {
         fixup_stage8<HD>(p, kst, vst, c, phys, lane, s_ci, s_len, s_phys, s_coff, s_toff,
                          subkv);
         __syncwarp();
       }
+    } else if constexpr (KV8) {
+      // FP8 without shared caches: no slow path (the new row enters the merge apart)
     } else {
       if ((partial && !kRowMask) || (c >= sub_lo && c <= sub_hi) || any_foreign)
         touched = fixup_stage<HD>(p, kst, vst, c, phys, partial && !kRowMask, lane, s_ci,
@@ -2418,9 +2423,9 @@ int32_t fail(int32_t status, const char* fmt, ...) {
 }
 
 template <int HD, int NT, int NS, bool SS, bool DM, bool FMA = false, bool KV8 = false,
-          bool WIDE = false>
+          bool WIDE = false, bool SHK = false>
 int32_t launch(const KParams& kp, dim3 grid, int smem_bytes, cudaStream_t stream) {
-  auto fn = decode_kernel<HD, NT, NS, SS, DM, FMA, KV8, WIDE>;
+  auto fn = decode_kernel<HD, NT, NS, SS, DM, FMA, KV8, WIDE, SHK>;
   static int configured[64] = {0};
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return fail(DORY_ERR_CUDA, "cudaGetDevice failed");
@@ -2555,6 +2560,15 @@ int32_t dispatch_kv8(const KParams& kp, dim3 grid, cudaStream_t stream) {
   static_assert(kConsumerWarps * 8 * (HD + 4) * 4 <= Smem<HD, NS, true>::kRegion,
                 "the warps' merge buffer must fit in the ring");
   const int smem = Smem<HD, NS, true>::bytes(kp.nsub);
+  if (kp.shared) {
+    const bool dm = one_wave(decode_kernel<HD, 1, NS, false, true, false, true, false, true>,
+                             grid, smem, Smem<HD, NS, true>::bytes(kMaxSub));
+    if (kp.sumsq)
+      return dm ? launch<HD, 1, NS, true, true, false, true, false, true>(kp, grid, smem, stream)
+                : launch<HD, 1, NS, true, false, false, true, false, true>(kp, grid, smem, stream);
+    return dm ? launch<HD, 1, NS, false, true, false, true, false, true>(kp, grid, smem, stream)
+              : launch<HD, 1, NS, false, false, false, true, false, true>(kp, grid, smem, stream);
+  }
   const bool dm = one_wave(decode_kernel<HD, 1, NS, false, true, false, true>, grid, smem,
                            Smem<HD, NS, true>::bytes(kMaxSub));
   if constexpr (HD == 128) {

@@ -28,6 +28,7 @@ from gpu_helpers import assert_close
 pytestmark = pytest.mark.gpu
 
 CASES = specs.specs()
+DEV = torch.device("cuda")
 
 
 def run_fp8(case: W.Case, layout="triton", splits=16, scales=(1.0, 1.0), window=None,
@@ -275,3 +276,34 @@ def test_large_batch(splits, sumsq):
     if sumsq:
         torch.testing.assert_close(ss.cpu(), out.double().square().sum((1, 2)).float(),
                                    rtol=1e-5, atol=1e-6)
+
+
+@pytest.mark.parametrize("hd", [128, 256])
+def test_shared_wavefront_with_sumsq(hd):
+    """The recurrent block's call: a shared-cache wavefront with the output's sum of squares
+    (out_sumsq) over an e4m3 cache; outputs, statistic and bytes against the oracle."""
+    nh, nkv = (32, 8) if hd == 128 else (16, 4)
+    case = W.wavefront(seed=1280 + hd, prompt=900, generated=2, tokens=4, num_heads=nh,
+                       num_kv_heads=nkv, head_dim=hd)
+    ks, vs = 0.5, 0.5
+    d = W.to_device(case, "triton", DEV, kv8=(ks, vs))
+    attn = DecodeAttention(nh, nkv, hd, DEV, splits=8, max_tokens=4, kv_cache_dtype="fp8")
+    ss = torch.full((4,), -1.0, device=DEV)
+    attn.multi_from_raw(d["qk"], d["v"], d["sqk"], case.sqk_factor, EPS, d["cache_offsets"],
+                        d["key"], d["value"], d["tables"], d["table_offsets"], d["seq_lens"],
+                        case.window, case.scale, d["gate"], d["out"], shared_cache=True,
+                        out_sumsq=ss, k_scale=ks, v_scale=vs)
+    torch.cuda.synchronize()
+    attn.check_errors()
+    key8, value8 = W.e4m3_bytes(case.key, ks), W.e4m3_bytes(case.value, vs)
+    want = O.multi_from_raw_fp8(
+        case.qk, case.v, case.sqk, case.sqk_factor, EPS, torch.zeros(4, dtype=torch.int64),
+        key8.view(-1), value8.view(-1), tuple(key8.shape), key8.stride(),
+        case.tables.reshape(-1), torch.zeros(4, dtype=torch.int64), case.seq_lens,
+        case.window, case.scale, case.gate, nh, nkv, ks, vs, shared_cache=True)
+    out = d["out"].cpu()
+    assert_close(out, want)
+    assert torch.equal(d["key"].cpu(), key8)
+    assert torch.equal(d["value"].cpu(), value8)
+    torch.testing.assert_close(ss.cpu(), out.double().square().sum((1, 2)).float(),
+                               rtol=1e-5, atol=1e-6)
